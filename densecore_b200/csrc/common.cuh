@@ -1,0 +1,60 @@
+// common.cuh -- shared definitions of the sm_100a SDPA library: the problem description
+// every kernel receives, mask access, the per-thread error slot and launch helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/densecore_sdpa.h"
+
+namespace dc {
+
+// One attention problem: q (B,H,L,E), k (B,Hkv,S,E), v (B,Hkv,S,Ev), out (B,H,L,Ev),
+// lse (B,H,L). Strides are in elements; a mask stride of 0 broadcasts that dim.
+struct AttnProblem {
+    const float *q, *k, *v;
+    float *out, *lse;
+    int64_t B, H, Hkv, L, S, E, Ev;
+    int64_t qs[4], ks[4], vs[4], os[4], ls[3];
+    const void *mask;
+    int mask_kind;  // 0 none, 1 float additive, 2 bool (nonzero = may attend)
+    int64_t ms[4];
+    int causal;
+    float scale;
+    int group;  // H / Hkv
+};
+
+// Backward extras: grad_out (B,H,L,Ev), dq (B,H,L,E), dk (B,Hkv,S,E), dv (B,Hkv,S,Ev),
+// delta (B*H*L, contiguous; sum(grad_out * out) per row).
+struct AttnGrads {
+    const float *dout;
+    float *dq, *dk, *dv;
+    float *delta;
+    int64_t dos[4], dqs[4], dks[4], dvs[4];
+};
+
+enum MaskKind { MASK_NONE = 0, MASK_FLOAT = 1, MASK_BOOL = 2 };
+
+__device__ __forceinline__ float mask_value(const AttnProblem &p, int64_t b, int64_t h,
+                                            int64_t i, int64_t j) {
+    int64_t off = b * p.ms[0] + h * p.ms[1] + i * p.ms[2] + j * p.ms[3];
+    if (p.mask_kind == MASK_FLOAT) return static_cast<const float *>(p.mask)[off];
+    return static_cast<const uint8_t *>(p.mask)[off] ? 0.0f : -INFINITY;
+}
+
+// Whether key j is visible to query row i under top-left causal alignment.
+__device__ __forceinline__ bool causal_visible(int causal, int64_t i, int64_t j) {
+    return !causal || j <= i;
+}
+
+// Host side: the thread's last error message and a setter that returns the status.
+void set_error(const std::string &msg);
+int fail(int status, const std::string &msg);
+int cuda_fail(cudaError_t err, const char *what);
+
+// Checks the launch just issued on `stream`; returns DC_OK or DC_ERR_CUDA.
+int check_launch(const char *what);
+
+}  // namespace dc

@@ -1,0 +1,37 @@
+// kernels.h -- host-side launchers of the SDPA kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace dc {
+
+struct MergeStrides {
+    int64_t oas[4], las[3], ops[4], lps[3];
+};
+
+// CUDA-core kernels (attn_simt.cu): any head dim <= 256, any strides.
+int simt_forward(const AttnProblem &p, cudaStream_t stream);
+int bwd_delta(const AttnProblem &p, const AttnGrads &g, cudaStream_t stream);
+int simt_backward(const AttnProblem &p, const AttnGrads &g, cudaStream_t stream);
+int simt_probs(const AttnProblem &p, float *probs, const int64_t ps[4], int average,
+               cudaStream_t stream);
+int merge(float *oa, float *la, const float *op, const float *lp, int64_t B, int64_t H,
+          int64_t L, int64_t Ev, const MergeStrides &st, cudaStream_t stream);
+
+// Split-KV decode (decode.cu): q_len == 1, head dim 64 or 128, rows of 16-byte multiples.
+bool decode_supported(const AttnProblem &p);
+int decode_pick_splits(const AttnProblem &p);
+size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Ev, int splits);
+int decode_forward(const AttnProblem &p, int splits, void *workspace, cudaStream_t stream);
+
+// tcgen05 tensor-core kernels (attn_tc.cu): head dim 64 or 128, E == Ev, unit-stride rows
+// on 16-byte boundaries.
+bool tc_forward_supported(const AttnProblem &p);
+int tc_forward(const AttnProblem &p, int precision, cudaStream_t stream);
+bool tc_backward_supported(const AttnProblem &p);
+int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream);
+
+}  // namespace dc

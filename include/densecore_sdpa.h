@@ -1,0 +1,157 @@
+/*
+ * densecore_sdpa.h -- C ABI of the B200 (sm_100a) scaled-dot-product-attention library.
+ *
+ * This is the drop-in boundary for DenseCore's flash-attention path. DenseCore reaches its
+ * native kernels through two pyo3 functions in src/lib.rs; each entry point below replaces
+ * one of them (or adds a device-only step the CPU path did not need) and keeps their
+ * argument meaning and error behaviour:
+ *
+ *   dc_sdpa_fwd   <- _flash_attention           src/lib.rs:609-638 (-> torch_attention::forward)
+ *   dc_sdpa_bwd   <- _flash_attention_backward  src/lib.rs:640-683 (-> torch_attention::backward)
+ *   dc_sdpa_decode   q_len == 1 case of _flash_attention (torch_attention.rs:157, q_split -> 1)
+ *   dc_attn_merge    logsumexp merge of partial results (ring attention; no CPU counterpart)
+ *   dc_attn_probs    softmax(scale*QK^T + mask) averaged over heads: the need_weights output of
+ *                    multi_head_attention_forward (python/densecore/functional.py:456-461)
+ *   dc_last_error    the message of the last failure on this thread (PyErr text in lib.rs)
+ *
+ * Conventions
+ *  - Tensors are device pointers with sizes and strides in elements (dc_tensor_t). q is
+ *    (B, H, L, E); k is (B, Hkv, S, E); v is (B, Hkv, S, Ev); H % Hkv == 0 (grouped-query).
+ *    out is (B, H, L, Ev) and lse is (B, H, L), both float32, written by the library.
+ *  - mask (nullable) is either float32 (added to the scaled scores) or bool/uint8 (1 = may
+ *    attend, 0 = -inf), of 4 dims broadcastable to (B, H, L, S): a broadcast dim has size 1 or
+ *    stride 0. This is the mask DenseCore's _flash_mask (functional.py:343-364) builds, without
+ *    materialising it.
+ *  - causal is top-left aligned: query row i attends keys j <= i (torch_attention.rs:176-180).
+ *  - has_scale == 0 means scale = (float)(1/sqrt(E)) computed in double
+ *    (torch_attention.rs:37-40).
+ *  - A fully masked query row gives out = 0, lse = 0 and zero gradients, as
+ *    torch_attention.rs:223-226 and :258-271 do.
+ *  - precision: DC_PREC_3XTF32 (default; fp32-class accuracy on tcgen05 tensor cores),
+ *    DC_PREC_TF32 (opt-in single-pass TF32) or DC_PREC_FP32 (CUDA-core fp32). Shapes the
+ *    tensor-core kernels do not cover run the CUDA-core kernels whatever the precision.
+ *  - Launches are asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream).
+ *    No call synchronises the host. There is no CPU fallback: with no usable device the call
+ *    fails with DC_ERR_CUDA.
+ *  - Return value: DC_OK, or an error code; dc_last_error() then holds the message.
+ *    DC_ERR_VALUE corresponds to the reference's ValueError (shape errors, lib.rs:562-570,
+ *    :601-605, :658-662); DC_ERR_RUNTIME / DC_ERR_CUDA to its RuntimeError (lib.rs:633, :677).
+ */
+#ifndef DENSECORE_SDPA_H
+#define DENSECORE_SDPA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DC_API __attribute__((visibility("default")))
+#else
+#define DC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DC_SDPA_ABI_VERSION 1
+
+enum dc_status {
+    DC_OK = 0,
+    DC_ERR_VALUE = 1,       /* bad shapes / arguments (the reference's ValueError) */
+    DC_ERR_RUNTIME = 2,     /* kernel-side failure (the reference's RuntimeError) */
+    DC_ERR_CUDA = 3,        /* CUDA runtime / driver error */
+    DC_ERR_UNSUPPORTED = 4  /* valid request this build does not implement */
+};
+
+enum dc_dtype { DC_F32 = 0, DC_BOOL = 1 };
+
+enum dc_precision { DC_PREC_3XTF32 = 0, DC_PREC_TF32 = 1, DC_PREC_FP32 = 2 };
+
+/* A strided device tensor view. Unused trailing dims are ignored (ndim <= 4). */
+typedef struct dc_tensor {
+    void *data;
+    int32_t dtype;      /* enum dc_dtype */
+    int32_t ndim;
+    int64_t sizes[4];
+    int64_t strides[4]; /* in elements */
+} dc_tensor_t;
+
+/* Forward: out (B,H,L,Ev) and lse (B,H,L).  Replaces _flash_attention, src/lib.rs:609-638. */
+DC_API int dc_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                dc_tensor_t *out, dc_tensor_t *lse, void *stream);
+
+/* Bytes of device scratch dc_sdpa_bwd needs for these shapes (the per-row
+ * sum(grad_out*out) of torch_attention.rs:327-330, plus alignment). */
+DC_API size_t dc_sdpa_bwd_workspace_size(int64_t batch, int64_t heads, int64_t q_len);
+
+/* Backward: grad_q (B,H,L,E), grad_k (B,Hkv,S,E), grad_v (B,Hkv,S,Ev), overwritten.
+ * workspace may be NULL (then the library takes stream-ordered memory with
+ * cudaMallocAsync); otherwise it must hold dc_sdpa_bwd_workspace_size() bytes.
+ * Replaces _flash_attention_backward, src/lib.rs:640-683. */
+DC_API int dc_sdpa_bwd(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tensor_t *k,
+                const dc_tensor_t *v, const dc_tensor_t *out, const dc_tensor_t *lse,
+                const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                dc_tensor_t *grad_q, dc_tensor_t *grad_k, dc_tensor_t *grad_v, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* Bytes of scratch dc_sdpa_decode needs for num_splits partial results per (batch, head). */
+DC_API size_t dc_sdpa_decode_workspace_size(int64_t batch, int64_t heads, int64_t head_dim_v,
+                                     int num_splits);
+
+/* The split count dc_sdpa_decode picks for num_splits <= 0 on the current device. */
+DC_API int dc_sdpa_decode_default_splits(int64_t batch, int64_t heads, int64_t kv_len);
+
+/* Decode (q_len == 1) by split-KV: num_splits CTAs stream disjoint key ranges of each
+ * (batch, head) and a second pass merges them by logsumexp. num_splits <= 0 picks a split
+ * count that fills the GPU. Same result contract as dc_sdpa_fwd with L == 1, non-causal
+ * (a causal q_len == 1 row sees only key 0 and is served by dc_sdpa_fwd).
+ * The q_len == 1 case of _flash_attention, src/lib.rs:609-638 / torch_attention.rs:157. */
+DC_API int dc_sdpa_decode(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                   const dc_tensor_t *mask, int has_scale, double scale, int num_splits,
+                   dc_tensor_t *out, dc_tensor_t *lse, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
+/* In-place logsumexp merge of a partial attention result into an accumulator over the same
+ * rows: lse = log(exp(lse_acc) + exp(lse_part)), out_acc = out_acc*exp(lse_acc - lse) +
+ * out_part*exp(lse_part - lse). Rows with lse_part = -inf leave the accumulator unchanged; an
+ * accumulator row with lse_acc = -inf takes the partial as it is. Tensors are (B,H,L,Ev) and (B,H,L)
+ * strided views. Used by ring attention after each K/V block (no reference counterpart: the
+ * reference has no sequence parallelism). */
+DC_API int dc_attn_merge(dc_tensor_t *out_acc, dc_tensor_t *lse_acc, const dc_tensor_t *out_part,
+                  const dc_tensor_t *lse_part, void *stream);
+
+/* Head-averaged attention probabilities (B, L, S): mean over H of
+ * exp(scale*q.k + mask - lse) with lse from dc_sdpa_fwd, zero where masked or causal-hidden.
+ * The need_weights=True, average_attn_weights=True output of
+ * multi_head_attention_forward (python/densecore/functional.py:456-461). With
+ * average_heads == 0, probs is (B, H, L, S) instead. */
+DC_API int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *lse,
+                  const dc_tensor_t *mask, int causal, int has_scale, double scale,
+                  int average_heads, dc_tensor_t *probs, void *stream);
+
+/* Kernel tracing. While enabled, every kernel the library launches is bracketed by two
+ * CUDA events on its launch stream. dc_kernel_timing_report() waits for the recorded events
+ * and writes {"<kernel>": [launches, total_ms], ...} as JSON into buf (truncated to len);
+ * reset != 0 then forgets the records. Returns the number of launches reported, or -1.
+ * (DenseCore has no tracing of its own; it profiles with cProfile.) */
+DC_API int dc_kernel_timing(int enable);
+DC_API int dc_kernel_timing_report(char *buf, size_t len, int reset);
+
+/* Message of the last failing call on this host thread ("" if none). */
+DC_API const char *dc_last_error(void);
+
+/* DC_SDPA_ABI_VERSION of the loaded library. */
+DC_API int dc_abi_version(void);
+
+/* Which kernel family dc_sdpa_fwd would pick for these shapes: 0 = CUDA-core (fp32 FMA),
+ * 1 = tcgen05 tensor cores, 2 = split-KV decode; -1 on invalid shapes. For tests and the
+ * benchmark's launch accounting. */
+DC_API int dc_sdpa_fwd_path(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                     const dc_tensor_t *mask, int causal, int precision);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DENSECORE_SDPA_H */
