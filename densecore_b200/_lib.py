@@ -22,7 +22,7 @@ DC_PREC_3XTF32, DC_PREC_TF32, DC_PREC_FP32 = 0, 1, 2
 # Every entry point include/densecore_sdpa.h declares.
 EXPORTS = ("dc_sdpa_fwd", "dc_sdpa_bwd_workspace_size", "dc_sdpa_bwd", "dc_sdpa_decode_workspace_size",
            "dc_sdpa_decode_default_splits", "dc_sdpa_decode", "dc_attn_merge", "dc_attn_probs",
-           "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report")
+           "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report", "dc_device_status")
 
 
 class DcTensor(ctypes.Structure):
@@ -72,6 +72,8 @@ def load():
         L.dc_abi_version.restype = i
         L.dc_sdpa_fwd_path.argtypes = [_P, _P, _P, _P, i, i]
         L.dc_sdpa_fwd_path.restype = i
+        L.dc_device_status.argtypes = [i]
+        L.dc_device_status.restype = i
         L.dc_kernel_timing.argtypes = [i]
         L.dc_kernel_timing.restype = i
         L.dc_kernel_timing_report.argtypes = [ctypes.c_char_p, sz, i]

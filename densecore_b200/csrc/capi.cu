@@ -191,6 +191,15 @@ const char *dc_last_error(void) { return g_last_error.c_str(); }
 
 int dc_abi_version(void) { return DC_SDPA_ABI_VERSION; }
 
+int dc_device_status(int reset) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cuda_fail(e, "device status");
+        return -1;
+    }
+    return device_error(reset);
+}
+
 int dc_sdpa_fwd_path(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
                      const dc_tensor_t *mask, int causal, int precision) {
     AttnProblem p;

@@ -33,5 +33,7 @@ bool tc_forward_supported(const AttnProblem &p);
 int tc_forward(const AttnProblem &p, int precision, cudaStream_t stream);
 bool tc_backward_supported(const AttnProblem &p);
 int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream);
+// The tensor-core kernels' device error word (sm100::DeviceError); -1 if it cannot be read.
+int device_error(int reset);
 
 }  // namespace dc

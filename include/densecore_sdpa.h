@@ -138,6 +138,11 @@ DC_API int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_te
 DC_API int dc_kernel_timing(int enable);
 DC_API int dc_kernel_timing_report(char *buf, size_t len, int reset);
 
+/* Device-side status of the tensor-core kernels: 0, or 1 when a kernel gave up on a wait
+ * that did not complete within its bound (2 s); that CTA then unwound without writing its
+ * outputs. Synchronises with the device. reset != 0 clears the status. -1 on a CUDA error. */
+DC_API int dc_device_status(int reset);
+
 /* Message of the last failing call on this host thread ("" if none). */
 DC_API const char *dc_last_error(void);
 

@@ -258,10 +258,12 @@ def test_full_size_long_context_prefix_property():
     ro, rl = oracle.flash_forward(*pre, causal=True)
     _assert_close("prefix out", out[:, :, :P].cpu().numpy(), ro, 1e-5)
     _assert_close("prefix lse", lse[:, :, :P].cpu().numpy(), rl, 1e-5)
-    # Value linearity: out(V = 1) is exactly the all-ones row for every visible row.
+    # Value linearity: out(V = 1) is the all-ones row for every visible row, up to the fp32
+    # rounding of two sums of up to 32768 terms taken in different orders (~2^-24 * log2(n)
+    # per level, bounded here by 64 ulp).
     ones = torch.ones_like(v)
     o1, _ = dc._flash_attention(q, k, ones, True)
-    assert float((o1 - 1).abs().max()) < 1e-5
+    assert float((o1 - 1).abs().max()) < 64 * 2.0 ** -23
 
 
 def test_full_size_decode_sampled_rows():
