@@ -39,6 +39,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
+#include "tma_host.h"
 #include "trace.h"
 
 namespace dc {
@@ -96,8 +97,10 @@ struct TcFwdArgs {
     float scale_log2;
 };
 
-// hi = tf32(x) in place, lo = tf32(x - hi) at the same offset of the lo buffer.
-__device__ __forceinline__ void split_tile(uint8_t *hi, uint8_t *lo, uint32_t bytes, int t, int nt) {
+// hi = tf32(x) in place and, when split, lo = tf32(x - hi) at the same offset of the lo
+// buffer. Single-pass TF32 rounds to nearest here rather than letting the tensor core drop
+// the low mantissa bits (which would bias every operand toward zero).
+__device__ __forceinline__ void split_tile(uint8_t *hi, uint8_t *lo, uint32_t bytes, int t, int nt, int split) {
     float4 *h = reinterpret_cast<float4 *>(hi);
     float4 *l = reinterpret_cast<float4 *>(lo);
     for (uint32_t i = t; i < bytes / 16; i += nt) {
@@ -105,10 +108,10 @@ __device__ __forceinline__ void split_tile(uint8_t *hi, uint8_t *lo, uint32_t by
         uint32_t a0 = tf32_rna(x.x), a1 = tf32_rna(x.y), a2 = tf32_rna(x.z), a3 = tf32_rna(x.w);
         float4 hv = make_float4(__uint_as_float(a0), __uint_as_float(a1), __uint_as_float(a2),
                                 __uint_as_float(a3));
-        float4 lv = make_float4(__uint_as_float(tf32_rna(x.x - hv.x)), __uint_as_float(tf32_rna(x.y - hv.y)),
-                                __uint_as_float(tf32_rna(x.z - hv.z)), __uint_as_float(tf32_rna(x.w - hv.w)));
         h[i] = hv;
-        l[i] = lv;
+        if (split)
+            l[i] = make_float4(__uint_as_float(tf32_rna(x.x - hv.x)), __uint_as_float(tf32_rna(x.y - hv.y)),
+                               __uint_as_float(tf32_rna(x.z - hv.z)), __uint_as_float(tf32_rna(x.w - hv.w)));
     }
 }
 
@@ -282,24 +285,22 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         // --------------------------------------------------------------- converters ----
         const int ct = threadIdx.x - 192;
         if (mbar_wait(bar(C::Q_FULL), 0, abort, &g_tc_error)) {
-            if (a.split) {
-                split_tile(sg + C::OFF_QHI, sg + C::OFF_QLO, C::Q_BYTES, ct, 128);
-                fence_proxy_async_smem();
-            }
+            split_tile(sg + C::OFF_QHI, sg + C::OFF_QLO, C::Q_BYTES, ct, 128, a.split);
+            fence_proxy_async_smem();
             mbar_arrive(bar(C::Q_READY));
             for (int j = 0; j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
                 if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, &g_tc_error)) break;
-                if (a.split) {
+                {
                     uint8_t *kh = sg + C::OFF_K + ks * 2 * C::KV_BYTES;
-                    split_tile(kh, kh + C::KV_BYTES, C::KV_BYTES, ct, 128);
+                    split_tile(kh, kh + C::KV_BYTES, C::KV_BYTES, ct, 128, a.split);
                     fence_proxy_async_smem();
                 }
                 mbar_arrive(bar(C::K_READY + ks));
                 if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, &g_tc_error)) break;
-                if (a.split) {
+                {
                     uint8_t *vh = sg + C::OFF_V + vs * 2 * C::KV_BYTES;
-                    split_tile(vh, vh + C::KV_BYTES, C::KV_BYTES, ct, 128);
+                    split_tile(vh, vh + C::KV_BYTES, C::KV_BYTES, ct, 128, a.split);
                     fence_proxy_async_smem();
                 }
                 mbar_arrive(bar(C::V_READY + vs));
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                         hi[x] = tf32_rna(pc);
                         lo[x] = tf32_rna(pc - __uint_as_float(hi[x]));
                     } else {
-                        hi[x] = __float_as_uint(pc);
+                        hi[x] = tf32_rna(pc);
                     }
                 }
                 tmem_st32(tl + C::col_s(bb) + 32 * c, hi);
@@ -457,39 +458,6 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 
 // ------------------------------------------------------------------- host side -------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void *ptr = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    });
-    return fn;
-}
-
-bool stride_ok(int64_t size, int64_t stride) { return size <= 1 || (stride % 4 == 0 && stride > 0); }
-
-// A 4-D map over (D, rows, heads, batch) of a strided float32 tensor; box = 32 x box_rows.
-int make_tmap(CUtensorMap *m, const float *base, int64_t D, int64_t rows, int64_t heads, int64_t batch,
-              const int64_t *st, int box_rows, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
-    auto fn = encode_fn();
-    if (!fn) return fail(DC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    // A size-1 dim's stride is never used; give it a legal value.
-    int64_t rs = rows > 1 ? st[2] : 4, hs = heads > 1 ? st[1] : 4, bs = batch > 1 ? st[0] : 4;
-    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)(rows > 0 ? rows : 1), (cuuint64_t)heads, (cuuint64_t)batch};
-    cuuint64_t strides[3] = {(cuuint64_t)rs * 4, (cuuint64_t)hs * 4, (cuuint64_t)bs * 4};
-    cuuint32_t box[4] = {32, (cuuint32_t)box_rows, 1, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(DC_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
-    return DC_OK;
-}
-
 template <class C>
 int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     CUtensorMap tq, tk, tv;
@@ -522,9 +490,9 @@ bool aligned16(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 bool tc_forward_supported(const AttnProblem &p) {
     if (p.E != p.Ev || (p.E != 64 && p.E != 128)) return false;
     if (p.qs[3] != 1 || p.ks[3] != 1 || p.vs[3] != 1) return false;
-    if (!stride_ok(p.L, p.qs[2]) || !stride_ok(p.H, p.qs[1]) || !stride_ok(p.B, p.qs[0])) return false;
-    if (!stride_ok(p.S, p.ks[2]) || !stride_ok(p.Hkv, p.ks[1]) || !stride_ok(p.B, p.ks[0])) return false;
-    if (!stride_ok(p.S, p.vs[2]) || !stride_ok(p.Hkv, p.vs[1]) || !stride_ok(p.B, p.vs[0])) return false;
+    if (!tma_stride_ok(p.L, p.qs[2]) || !tma_stride_ok(p.H, p.qs[1]) || !tma_stride_ok(p.B, p.qs[0])) return false;
+    if (!tma_stride_ok(p.S, p.ks[2]) || !tma_stride_ok(p.Hkv, p.ks[1]) || !tma_stride_ok(p.B, p.ks[0])) return false;
+    if (!tma_stride_ok(p.S, p.vs[2]) || !tma_stride_ok(p.Hkv, p.vs[1]) || !tma_stride_ok(p.B, p.vs[0])) return false;
     if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v)) return false;
     if (p.L >= (1ll << 31) || p.S >= (1ll << 31) || p.L == 0 || p.S == 0) return false;
     return true;
@@ -533,11 +501,6 @@ bool tc_forward_supported(const AttnProblem &p) {
 int tc_forward(const AttnProblem &p, int precision, cudaStream_t stream) {
     const int split = precision == DC_PREC_TF32 ? 0 : 1;
     return p.E == 64 ? launch_fwd<Fwd64>(p, split, stream) : launch_fwd<Fwd128>(p, split, stream);
-}
-
-bool tc_backward_supported(const AttnProblem &) { return false; }
-int tc_backward(const AttnProblem &, const AttnGrads &, int, cudaStream_t) {
-    return fail(DC_ERR_UNSUPPORTED, "tensor-core backward is not built");
 }
 
 int device_error(int reset) {

@@ -286,7 +286,7 @@ int dc_sdpa_bwd(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tens
         return st;
     g.delta = static_cast<float *>(ws.ptr);
     if (p.L > 0 && (st = bwd_delta(p, g, s))) return st;
-    if (precision != DC_PREC_FP32 && tc_backward_supported(p)) return tc_backward(p, g, precision, s);
+    if (precision != DC_PREC_FP32 && tc_backward_supported(p, g)) return tc_backward(p, g, precision, s);
     return simt_backward(p, g, s);
 }
 

@@ -27,11 +27,11 @@ int decode_pick_splits(const AttnProblem &p);
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Ev, int splits);
 int decode_forward(const AttnProblem &p, int splits, void *workspace, cudaStream_t stream);
 
-// tcgen05 tensor-core kernels (attn_tc.cu): head dim 64 or 128, E == Ev, unit-stride rows
-// on 16-byte boundaries.
+// tcgen05 tensor-core kernels (attn_tc.cu, attn_tc_bwd.cu): head dim 64 or 128 (backward:
+// 64), E == Ev, unit-stride rows on 16-byte boundaries.
 bool tc_forward_supported(const AttnProblem &p);
 int tc_forward(const AttnProblem &p, int precision, cudaStream_t stream);
-bool tc_backward_supported(const AttnProblem &p);
+bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g);
 int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream);
 // The tensor-core kernels' device error word (sm100::DeviceError); -1 if it cannot be read.
 int device_error(int reset);
