@@ -4,37 +4,36 @@
 // 64 and 128 with a warp-specialised kernel; one CTA computes a 128-row query tile of one
 // (batch, head):
 //
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of BN keys into rings of
-//               shared-memory stages (128-byte swizzle, 4-D tensor maps over the caller's
-//               strided (B, H, L, E) views, zero fill past the sequence end).
-//   warps 6-9   converters (3xTF32): split each landed fp32 tile x into hi = tf32(x) in
-//               place and lo = tf32(x - hi) beside it, so that a*b ~ ah*bh + ah*bl + al*bh
-//               keeps fp32-class accuracy on the TF32 tensor cores.
-//   warp 5      MMA issuer: S = Q K^T into TMEM (two S buffers), then O += P V with P read
-//               from TMEM (A operand) and V from shared memory (MN-major B operand, which for
-//               tf32 must use the 32-byte-atom 128-byte swizzle). Issue
-//               order S0, S1, PV0, S2, PV1, ... so the tensor core works on S(j+1) while
-//               the softmax warps handle block j.
-//   warps 0-3   softmax: thread t owns query row t (TMEM lane t). Online softmax in base 2
-//               with DenseCore's rules (a block whose running max is -inf adds nothing,
-//               :218-226); P is written back to TMEM as tf32 hi/lo over the consumed S
-//               columns. The running max moves only when it grows by more than 2^8 (the sum
-//               and the output share the stale max, so the result is unchanged).
-//               Each block's P V goes to a fresh TMEM accumulator (a handful of tensor-core
-//               accumulation steps, whose internal rounding is coarser than fp32); the
-//               softmax threads fold it into the running output with fp32 adds, one block
-//               behind, while the tensor core works on the next block. Finalisation as the
-//               reference: max -inf -> 0, sum 0 -> 1, out = acc/sum, lse = max + log(sum)
-//               (:258-271).
+//   warp 8      TMA producer: the Q tile once, then K and V tiles of BN keys into 3-stage
+//               shared-memory rings (4-D tensor maps over the caller's strided (B, H, L, E)
+//               views, zero fill past the sequence end). K uses the 128-byte swizzle (K-major
+//               B operand); V uses the 32-byte-atom 128-byte swizzle, the only layout tf32
+//               accepts for an MN-major operand.
+//   warps 10-13 converters: Q goes into TMEM as tf32 hi / lo (the A operand of S = Q K^T, so
+//               the S MMAs read only K from shared memory); each landed K / V tile x is split
+//               in place into hi = tf32(x) and lo = tf32(x - hi) (3xTF32: a*b ~ ah*bh + ah*bl
+//               + al*bh keeps fp32-class accuracy on the TF32 tensor cores).
+//   warp 9      MMA issuer (one thread, descriptors precomputed): S_j = Q K_j^T into one of
+//               two TMEM buffers, then O_blk = P_{j-1} V_{j-1} with P read from TMEM; issue
+//               order S0, S1, PV0, S2, PV1, ... so the tensor core computes S_{j+1} while the
+//               softmax warps work on block j.
+//   warps 0-7   softmax, two threads per query row (TMEM lane), each owning half of the
+//               block's columns and half of the output row (in registers). Online softmax in
+//               base 2 with DenseCore's rules: a block whose running max is -inf adds nothing
+//               (:218-226); the row max is shared between the pair through shared memory;
+//               the running max moves only when it grows by more than 2^8 (sum and output
+//               share the stale max, so the result is unchanged). P goes back to TMEM as tf32
+//               hi / lo over the consumed S columns. Each block's P V lands in a fresh TMEM
+//               accumulator (a few tensor-core accumulation steps, whose internal rounding is
+//               coarser than fp32) that the pair folds into its registers in fp32. Finalisation
+//               as the reference: max -inf -> 0, sum 0 -> 1, out = acc/sum, lse = max +
+//               log(sum) (:258-271).
 //
-// Every mbarrier wait is bounded (sm100::mbar_wait); a wait that times out sets a device
+// Every mbarrier wait is bounded (sm100::mbar_wait); a wait that times out sets the device
 // error word and the CTA unwinds, frees its TMEM and exits.
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <math.h>
-
-#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -57,65 +56,132 @@ template <int D_, int BN_, int KST_, int VST_>
 struct FwdCfg {
     static constexpr int D = D_, BN = BN_, KST = KST_, VST = VST_;
     static constexpr int BM = 128;
-    static constexpr int CHUNKS = D / 32;  // 128-byte column chunks of a row
+    static constexpr int CHUNKS = D / 32;   // 128-byte column chunks of a row
+    static constexpr int HB = BN / 2;       // S columns per softmax thread
+    static constexpr int HD = D / 2;        // output columns per softmax thread
     static constexpr uint32_t Q_CHUNK = BM * 128;
     static constexpr uint32_t KV_CHUNK = BN * 128;
     static constexpr uint32_t Q_BYTES = BM * D * 4;
     static constexpr uint32_t KV_BYTES = BN * D * 4;
-    static constexpr uint32_t OFF_QHI = 0;
-    static constexpr uint32_t OFF_QLO = Q_BYTES;
-    static constexpr uint32_t OFF_K = 2 * Q_BYTES;
-    static constexpr uint32_t OFF_V = OFF_K + KST * 2 * KV_BYTES;
-    static constexpr uint32_t OFF_BAR = OFF_V + VST * 2 * KV_BYTES;
-    // Barrier indices.
+    static constexpr uint32_t KV_STAGE = 2 * KV_BYTES;  // hi, lo
+    static constexpr uint32_t OFF_K = 0;
+    static constexpr uint32_t OFF_V = OFF_K + KST * KV_STAGE;
+    static constexpr uint32_t OFF_XMAX = OFF_V + VST * KV_STAGE;     // float [2][2][BM]
+    static constexpr uint32_t OFF_XSUM = OFF_XMAX + 2 * 2 * BM * 4;  // float [2][BM]
+    static constexpr uint32_t OFF_BAR = OFF_XSUM + 2 * BM * 4;
     static constexpr int Q_FULL = 0, Q_READY = 1, K_FULL = 2, K_READY = K_FULL + KST,
                          K_EMPTY = K_READY + KST, V_FULL = K_EMPTY + KST, V_READY = V_FULL + VST,
                          V_EMPTY = V_READY + VST, S_FULL = V_EMPTY + VST, P_FULL = S_FULL + 2,
-                         PV_DONE = P_FULL + 2, OB_FREE = PV_DONE + 2, DRAIN = OB_FREE + 2,
-                         NBAR = DRAIN + 1;
+                         PV_DONE = P_FULL + 2, OB_FREE = PV_DONE + 1, XCH = OB_FREE + 1,
+                         XSUM = XCH + 2, DRAIN = XSUM + 1, NBAR = DRAIN + 1;
     static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
-    // TMEM: the running output (fp32, folded by CUDA cores), two per-block P V accumulators,
-    // then two (S / P_hi, P_lo) buffers.
-    static constexpr uint32_t COL_O = 0;
-    __host__ __device__ static constexpr uint32_t col_ob(int b) { return D + b * D; }
+    // TMEM: Q hi | Q lo | 2 x (S / P hi, P lo) | O_blk
+    static constexpr uint32_t COL_QHI = 0, COL_QLO = D, COL_OB = 2 * D + 4 * BN;
     static constexpr uint32_t COLS_USED = 3 * D + 4 * BN;
-    static constexpr uint32_t TMEM_COLS = COLS_USED <= 128 ? 128 : COLS_USED <= 256 ? 256 : 512;
-    static constexpr int THREADS = 320;
+    static constexpr uint32_t TMEM_COLS = COLS_USED <= 256 ? 256 : 512;
+    static constexpr int SOFTMAX_THREADS = 256;
+    static constexpr int W_PROD = 8, W_MMA = 9, W_CVT = 10;
+    static constexpr int THREADS = 448;
     static constexpr uint32_t IDESC_S = idesc_tf32(128, BN, 0, 0);
     static constexpr uint32_t IDESC_O = idesc_tf32(128, D, 0, 1);
-    __host__ __device__ static constexpr uint32_t col_s(int b) { return 3 * D + b * 2 * BN; }
-    __host__ __device__ static constexpr uint32_t col_plo(int b) { return 3 * D + b * 2 * BN + BN; }
+    __host__ __device__ static constexpr uint32_t col_s(int b) { return 2 * D + b * 2 * BN; }
+    __host__ __device__ static constexpr uint32_t col_plo(int b) { return 2 * D + b * 2 * BN + BN; }
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(COLS_USED <= 512, "tensor memory budget");
+    static_assert(Q_BYTES <= KST * KV_STAGE, "the raw Q tile is staged in the K ring");
+    static_assert(HB == 16 || HB == 32, "softmax half-block width");
 };
 
 struct TcFwdArgs {
     AttnProblem p;
-    int split;  // 1: 3xTF32, 0: single-pass TF32
     int num_q_tiles;
     float scale_log2;
+    int *err;
 };
 
-// hi = tf32(x) in place and, when split, lo = tf32(x - hi) at the same offset of the lo
-// buffer. Single-pass TF32 rounds to nearest here rather than letting the tensor core drop
-// the low mantissa bits (which would bias every operand toward zero).
-__device__ __forceinline__ void split_tile(uint8_t *hi, uint8_t *lo, uint32_t bytes, int t, int nt, int split) {
-    float4 *h = reinterpret_cast<float4 *>(hi);
-    float4 *l = reinterpret_cast<float4 *>(lo);
-    for (uint32_t i = t; i < bytes / 16; i += nt) {
-        float4 x = h[i];
-        uint32_t a0 = tf32_rna(x.x), a1 = tf32_rna(x.y), a2 = tf32_rna(x.z), a3 = tf32_rna(x.w);
-        float4 hv = make_float4(__uint_as_float(a0), __uint_as_float(a1), __uint_as_float(a2),
-                                __uint_as_float(a3));
-        h[i] = hv;
-        if (split)
-            l[i] = make_float4(__uint_as_float(tf32_rna(x.x - hv.x)), __uint_as_float(tf32_rna(x.y - hv.y)),
-                               __uint_as_float(tf32_rna(x.z - hv.z)), __uint_as_float(tf32_rna(x.w - hv.w)));
+// tcgen05.ld / st of 16 or 32 consecutive columns of this thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
+    tmem_ld32(taddr, r);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_st<32>(uint32_t taddr, const uint32_t (&r)[32]) {
+    tmem_st32(taddr, r);
+}
+template <>
+__device__ __forceinline__ void tmem_st<16>(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// hi = tf32(x) in place and, with SPLIT, lo = tf32(x - hi) `lo_off` bytes further.
+// Single-pass TF32 rounds to nearest here rather than letting the tensor core drop the low
+// mantissa bits (which would bias every operand toward zero).
+template <bool SPLIT>
+__device__ __forceinline__ void split_tile(uint8_t *hi, uint32_t lo_off, uint32_t bytes, int t) {
+    for (uint32_t i = t; i < bytes / 16; i += 128) {
+        float4 *ph = reinterpret_cast<float4 *>(hi) + i;
+        const float4 x = *ph;
+        float4 hv;
+        hv.x = __uint_as_float(tf32_rna(x.x));
+        hv.y = __uint_as_float(tf32_rna(x.y));
+        hv.z = __uint_as_float(tf32_rna(x.z));
+        hv.w = __uint_as_float(tf32_rna(x.w));
+        *ph = hv;
+        if (SPLIT) {
+            float4 lv;
+            lv.x = __uint_as_float(tf32_rna(x.x - hv.x));
+            lv.y = __uint_as_float(tf32_rna(x.y - hv.y));
+            lv.z = __uint_as_float(tf32_rna(x.z - hv.z));
+            lv.w = __uint_as_float(tf32_rna(x.w - hv.w));
+            *(reinterpret_cast<float4 *>(hi + lo_off) + i) = lv;
+        }
     }
 }
 
-template <class C>
+// Row `row` of a raw 128-byte-swizzled tile (rows of 128-byte chunks, chunk stride
+// `chunk_bytes`) into TMEM: tf32 hi at col_hi and, with SPLIT, lo at col_lo.
+template <int CHUNKS, bool SPLIT>
+__device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_bytes, int row, uint32_t tlane,
+                                            uint32_t col_hi, uint32_t col_lo) {
+#pragma unroll
+    for (int c = 0; c < CHUNKS; c++) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            const float4 x =
+                *reinterpret_cast<const float4 *>(raw + c * chunk_bytes + row * 128 + ((g ^ (row & 7)) * 16));
+            const float v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                hi[4 * g + e] = tf32_rna(v[e]);
+                if (SPLIT) lo[4 * g + e] = tf32_rna(v[e] - __uint_as_float(hi[4 * g + e]));
+            }
+        }
+        tmem_st32(tlane + col_hi + 32 * c, hi);
+        if (SPLIT) tmem_st32(tlane + col_lo + 32 * c, lo);
+    }
+}
+
+template <class C, bool SPLIT>
 __global__ void __launch_bounds__(C::THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                        const __grid_constant__ CUtensorMap tmv, const TcFwdArgs a) {
@@ -133,6 +199,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
     volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
+    int *err = a.err;
 
     if (threadIdx.x == 0) {
         mbar_init(bar(C::Q_FULL), 1);
@@ -149,19 +216,22 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(bar(C::S_FULL + s), 1);
-            mbar_init(bar(C::P_FULL + s), 128);
-            mbar_init(bar(C::PV_DONE + s), 1);
-            mbar_init(bar(C::OB_FREE + s), 128);
+            mbar_init(bar(C::P_FULL + s), C::SOFTMAX_THREADS);
         }
+        mbar_init(bar(C::PV_DONE), 1);
+        mbar_init(bar(C::OB_FREE), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::XCH), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::XCH + 1), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::XSUM), C::SOFTMAX_THREADS);
         mbar_init(bar(C::DRAIN), 1);
         *abort = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == C::W_MMA) {
         tmem_alloc(smem_addr(tmem_slot), C::TMEM_COLS);
         tmem_relinquish();
     }
-    if (warp == 4 && lane == 0) {
+    if (warp == C::W_PROD && lane == 0) {
         prefetch_tmap(&tmq);
         prefetch_tmap(&tmk);
         prefetch_tmap(&tmv);
@@ -171,33 +241,28 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == C::W_PROD) {
         // ------------------------------------------------------------ TMA producer ----
         if (lane == 0) {
             int k_issued = -1, v_issued = -1;
+            // The raw Q tile lands in the K ring; the converters move it into TMEM.
             mbar_expect_tx(bar(C::Q_FULL), C::Q_BYTES);
             for (int c = 0; c < C::CHUNKS; c++)
-                tma_load_4d(&tmq, sb + C::OFF_QHI + c * C::Q_CHUNK, bar(C::Q_FULL), 32 * c, (int)q0,
-                            (int)h, (int)b);
-            for (int j = 0; j < nblk; j++) {
+                tma_load_4d(&tmq, sb + C::OFF_K + c * C::Q_CHUNK, bar(C::Q_FULL), 32 * c, (int)q0, (int)h, (int)b);
+            bool ok = mbar_wait(bar(C::Q_READY), 0, abort, err);
+            for (int j = 0; ok && j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
-                if (j >= C::KST &&
-                    !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, &g_tc_error))
-                    break;
+                if (j >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, err)) break;
                 mbar_expect_tx(bar(C::K_FULL + ks), C::KV_BYTES);
-                const uint32_t kd = sb + C::OFF_K + ks * 2 * C::KV_BYTES;
+                const uint32_t kd = sb + C::OFF_K + ks * C::KV_STAGE;
                 for (int c = 0; c < C::CHUNKS; c++)
-                    tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN,
-                                (int)hk, (int)b);
+                    tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
                 k_issued = j;
-                if (j >= C::VST &&
-                    !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, &g_tc_error))
-                    break;
+                if (j >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, err)) break;
                 mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
-                const uint32_t vd = sb + C::OFF_V + vs * 2 * C::KV_BYTES;
+                const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
                 for (int c = 0; c < C::CHUNKS; c++)
-                    tma_load_4d(&tmv, vd + c * C::KV_CHUNK, bar(C::V_FULL + vs), 32 * c, j * C::BN,
-                                (int)hk, (int)b);
+                    tma_load_4d(&tmv, vd + c * C::KV_CHUNK, bar(C::V_FULL + vs), 32 * c, j * C::BN, (int)hk, (int)b);
                 v_issued = j;
             }
             if (*abort) {
@@ -210,140 +275,135 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     mbar_wait(bar(C::V_FULL + j % C::VST), (j / C::VST) & 1, &never, nullptr);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == C::W_MMA) {
         // -------------------------------------------------------------- MMA issuer ----
         if (lane == 0) {
-            const uint32_t qhi = sb + C::OFF_QHI, qlo = sb + C::OFF_QLO;
-            bool ok = mbar_wait(bar(C::Q_READY), 0, abort, &g_tc_error);
-            tc_fence_after();
-            for (int j = 0; ok && j <= nblk; j++) {
-                if (j < nblk) {
-                    const int bb = j & 1, ks = j % C::KST;
-                    if (!mbar_wait(bar(C::K_READY + ks), (j / C::KST) & 1, abort, &g_tc_error)) break;
-                    if (j >= 2 && !mbar_wait(bar(C::PV_DONE + bb), ((j - 2) >> 1) & 1, abort, &g_tc_error))
-                        break;
-                    tc_fence_after();
-                    const uint32_t khi = sb + C::OFF_K + ks * 2 * C::KV_BYTES, klo = khi + C::KV_BYTES;
-                    const uint32_t d_s = tmem + C::col_s(bb);
-                    if (a.split) {  // cross terms Qhi Klo + Qlo Khi first, then Qhi Khi
-#pragma unroll
-                        for (int kk = 0; kk < C::D / 8; kk++) {
-                            const uint32_t oq = (kk >> 2) * C::Q_CHUNK + (kk & 3) * 32;
-                            const uint32_t ok_ = (kk >> 2) * C::KV_CHUNK + (kk & 3) * 32;
-                            mma_tf32_ss(d_s, sdesc_sw128(qhi + oq, 16, 1024), sdesc_sw128(klo + ok_, 16, 1024),
-                                        C::IDESC_S, kk > 0 ? 1u : 0u);
-                            mma_tf32_ss(d_s, sdesc_sw128(qlo + oq, 16, 1024), sdesc_sw128(khi + ok_, 16, 1024),
-                                        C::IDESC_S, 1);
-                        }
-                    }
-#pragma unroll
-                    for (int kk = 0; kk < C::D / 8; kk++) {
-                        const uint32_t oq = (kk >> 2) * C::Q_CHUNK + (kk & 3) * 32;
-                        const uint32_t ok_ = (kk >> 2) * C::KV_CHUNK + (kk & 3) * 32;
-                        mma_tf32_ss(d_s, sdesc_sw128(qhi + oq, 16, 1024), sdesc_sw128(khi + ok_, 16, 1024),
-                                    C::IDESC_S, (a.split || kk > 0) ? 1u : 0u);
-                    }
-                    tc_commit(bar(C::S_FULL + bb));
-                    tc_commit(bar(C::K_EMPTY + ks));
-                }
-                if (j >= 1) {
-                    // O_blk(jp) = P(jp) V(jp) in a fresh accumulator: few tensor-core
-                    // accumulation steps per block; the CUDA cores fold blocks in fp32.
-                    const int jp = j - 1, bp = jp & 1, vs = jp % C::VST;
-                    if (!mbar_wait(bar(C::P_FULL + bp), (jp >> 1) & 1, abort, &g_tc_error)) break;
-                    if (!mbar_wait(bar(C::V_READY + vs), (jp / C::VST) & 1, abort, &g_tc_error)) break;
-                    if (jp >= 2 && !mbar_wait(bar(C::OB_FREE + bp), ((jp - 2) >> 1) & 1, abort, &g_tc_error))
-                        break;
-                    tc_fence_after();
-                    const uint32_t vhi = sb + C::OFF_V + vs * 2 * C::KV_BYTES, vlo = vhi + C::KV_BYTES;
-                    const uint32_t d_o = tmem + C::col_ob(bp);
-                    const uint32_t a_hi = tmem + C::col_s(bp), a_lo = tmem + C::col_plo(bp);
-                    if (a.split) {  // the small cross terms first, then the main products
-#pragma unroll
-                        for (int kk = 0; kk < C::BN / 8; kk++) {
-                            const uint64_t bv = sdesc_mn_sw128_32b(vhi + kk * 1024, C::KV_CHUNK, 512);
-                            mma_tf32_ts(d_o, a_hi + kk * 8, sdesc_mn_sw128_32b(vlo + kk * 1024, C::KV_CHUNK, 512),
-                                        C::IDESC_O, kk > 0 ? 1u : 0u);
-                            mma_tf32_ts(d_o, a_lo + kk * 8, bv, C::IDESC_O, 1);
-                        }
-                    }
+            // Descriptors of stage 0; stage and k-step offsets go into the address field.
+            const uint64_t kdesc0 = sdesc_sw128(sb + C::OFF_K, 16, 1024);
+            const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
+            const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO, d_ob = tmem + C::COL_OB;
+            auto issue_pv = [&](int i) -> bool {
+                const int bi = i & 1, vs = i % C::VST;
+                if (!mbar_wait(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) return false;
+                if (!mbar_wait(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) return false;
+                if (i >= 1 && !mbar_wait(bar(C::OB_FREE), (i - 1) & 1, abort, err)) return false;
+                tc_fence_after();
+                const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
+                const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
+                if (SPLIT) {  // the small cross terms first, then the main products
 #pragma unroll
                     for (int kk = 0; kk < C::BN / 8; kk++) {
-                        const uint64_t bv = sdesc_mn_sw128_32b(vhi + kk * 1024, C::KV_CHUNK, 512);
-                        mma_tf32_ts(d_o, a_hi + kk * 8, bv, C::IDESC_O, (a.split || kk > 0) ? 1u : 0u);
+                        mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
+                                    kk > 0 ? 1u : 0u);
+                        mma_tf32_ts(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
                     }
-                    tc_commit(bar(C::PV_DONE + bp));
-                    tc_commit(bar(C::V_EMPTY + vs));
+                }
+#pragma unroll
+                for (int kk = 0; kk < C::BN / 8; kk++)
+                    mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
+                tc_commit(bar(C::PV_DONE));
+                tc_commit(bar(C::V_EMPTY + vs));
+                return true;
+            };
+            bool ok = mbar_wait(bar(C::Q_READY), 0, abort, err);
+            tc_fence_after();
+            for (int j = 0; ok && j < nblk; j++) {
+                const int bb = j & 1, ks = j % C::KST;
+                if (!mbar_wait(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
+                // S buffer bb held P_{j-2}, read by PV_{j-2}.
+                if (j >= 2 && !mbar_wait(bar(C::PV_DONE), (j - 2) & 1, abort, err)) break;
+                tc_fence_after();
+                const uint64_t kd = kdesc0 + ((ks * C::KV_STAGE) >> 4);
+                const uint32_t d_s = tmem + C::col_s(bb);
+                if (SPLIT) {  // Qhi Klo + Qlo Khi first, then Qhi Khi
+#pragma unroll
+                    for (int kk = 0; kk < C::D / 8; kk++) {
+                        const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
+                        mma_tf32_ts(d_s, q_hi + kk * 8, kd + ((C::KV_BYTES >> 4) + off), C::IDESC_S, kk > 0 ? 1u : 0u);
+                        mma_tf32_ts(d_s, q_lo + kk * 8, kd + off, C::IDESC_S, 1u);
+                    }
+                }
+#pragma unroll
+                for (int kk = 0; kk < C::D / 8; kk++) {
+                    const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
+                    mma_tf32_ts(d_s, q_hi + kk * 8, kd + off, C::IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(bar(C::S_FULL + bb));
+                tc_commit(bar(C::K_EMPTY + ks));
+                if (j >= 1 && !issue_pv(j - 1)) {
+                    ok = false;
+                    break;
                 }
             }
+            if (ok && nblk > 0) issue_pv(nblk - 1);
             // Every MMA issued so far completes before TMEM is released.
             tc_commit(bar(C::DRAIN));
             volatile int never = 0;
             mbar_wait(bar(C::DRAIN), 0, &never, nullptr);
         }
-    } else if (warp >= 6) {
+    } else if (warp >= C::W_CVT) {
         // --------------------------------------------------------------- converters ----
-        const int ct = threadIdx.x - 192;
-        if (mbar_wait(bar(C::Q_FULL), 0, abort, &g_tc_error)) {
-            split_tile(sg + C::OFF_QHI, sg + C::OFF_QLO, C::Q_BYTES, ct, 128, a.split);
-            fence_proxy_async_smem();
+        const int ct = threadIdx.x - 32 * C::W_CVT;
+        const int quad = warp & 3;
+        if (mbar_wait(bar(C::Q_FULL), 0, abort, err)) {
+            row_to_tmem<C::CHUNKS, SPLIT>(sg + C::OFF_K, C::Q_CHUNK, quad * 32 + lane,
+                                          tmem + ((uint32_t)(quad * 32) << 16), C::COL_QHI, C::COL_QLO);
+            tmem_wait_st();
+            tc_fence_before();
             mbar_arrive(bar(C::Q_READY));
             for (int j = 0; j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
-                if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, &g_tc_error)) break;
-                {
-                    uint8_t *kh = sg + C::OFF_K + ks * 2 * C::KV_BYTES;
-                    split_tile(kh, kh + C::KV_BYTES, C::KV_BYTES, ct, 128, a.split);
-                    fence_proxy_async_smem();
-                }
+                if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, err)) break;
+                split_tile<SPLIT>(sg + C::OFF_K + ks * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
+                fence_proxy_async_smem();
                 mbar_arrive(bar(C::K_READY + ks));
-                if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, &g_tc_error)) break;
-                {
-                    uint8_t *vh = sg + C::OFF_V + vs * 2 * C::KV_BYTES;
-                    split_tile(vh, vh + C::KV_BYTES, C::KV_BYTES, ct, 128, a.split);
-                    fence_proxy_async_smem();
-                }
+                if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, err)) break;
+                split_tile<SPLIT>(sg + C::OFF_V + vs * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
+                fence_proxy_async_smem();
                 mbar_arrive(bar(C::V_READY + vs));
             }
         }
     } else {
         // ------------------------------------------------------------------ softmax ----
-        const int row = threadIdx.x;
+        const int row = threadIdx.x & 127, half = threadIdx.x >> 7;
         const int64_t qrow = q0 + row;
         const bool row_ok = qrow < p.L;
-        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        float *xmax = reinterpret_cast<float *>(sg + C::OFF_XMAX);  // [2][2][BM]
+        float *xsum = reinterpret_cast<float *>(sg + C::OFF_XSUM);  // [2][BM]
         float m = -INFINITY, l = 0.0f;
+        float o[C::HD];
+#pragma unroll
+        for (int x = 0; x < C::HD; x++) o[x] = 0.0f;
         bool ok = true;
         for (int j = 0; j < nblk; j++) {
             const int bb = j & 1;
-            if (!mbar_wait(bar(C::S_FULL + bb), (j >> 1) & 1, abort, &g_tc_error)) {
+            if (!mbar_wait(bar(C::S_FULL + bb), (j >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float s[C::BN];
-#pragma unroll
-            for (int c = 0; c < C::BN / 32; c++) {
-                uint32_t r[32];
-                tmem_ld32(tl + C::col_s(bb) + 32 * c, r);
+            float s[C::HB];
+            {
+                uint32_t r[C::HB];
+                tmem_ld<C::HB>(tl + C::col_s(bb) + half * C::HB, r);
                 tmem_wait_ld();
 #pragma unroll
-                for (int x = 0; x < 32; x++) s[32 * c + x] = __uint_as_float(r[x]);
+                for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(r[x]);
             }
-            const int64_t k0 = (int64_t)j * C::BN;
+            const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
             // Rows past L (zero-filled by TMA) are computed but never stored.
-            const bool edge = (k0 + C::BN > p.S) || (p.causal && k0 + C::BN - 1 > q0) ||
-                              p.mask_kind != MASK_NONE;
+            const bool edge = (k0 + C::HB > p.S) || (p.causal && k0 + C::HB - 1 > q0) || p.mask_kind != MASK_NONE;
             float bmax = -INFINITY;
             if (!edge) {
 #pragma unroll
-                for (int c = 0; c < C::BN; c++) {
+                for (int c = 0; c < C::HB; c++) {
                     s[c] *= a.scale_log2;
                     bmax = fmaxf(bmax, s[c]);
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < C::BN; c++) {
+                for (int c = 0; c < C::HB; c++) {
                     const int64_t key = k0 + c;
                     float x = s[c] * a.scale_log2;
                     if (!row_ok || key >= p.S || (p.causal && key > qrow))
@@ -354,109 +414,104 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     bmax = fmaxf(bmax, x);
                 }
             }
+            // The block's row max, shared with the partner thread (the other half) through
+            // shared memory and an mbarrier (a bounded wait, unlike bar.sync).
+            xmax[(bb * 2 + half) * C::BM + row] = bmax;
+            mbar_arrive(bar(C::XCH + bb));
+            if (!mbar_wait(bar(C::XCH + bb), (j >> 1) & 1, abort, err)) {
+                ok = false;
+                break;
+            }
+            bmax = fmaxf(bmax, xmax[(bb * 2 + (half ^ 1)) * C::BM + row]);
             const float m_new = fmaxf(m, bmax);
             const bool rescale = m_new > m + 8.0f;
             float corr = 1.0f;
             if (rescale) {
-                corr = exp2f(m - m_new);
+                corr = ex2_approx(m - m_new);
                 m = m_new;
             }
             const bool dead = (m == -INFINITY);
             float rs = 0.0f;
+            uint32_t phi[C::HB], plo[C::HB];
 #pragma unroll
-            for (int c = 0; c < C::BN / 32; c++) {
-                uint32_t hi[32], lo[32];
-#pragma unroll
-                for (int x = 0; x < 32; x++) {
-                    const float pc = dead ? 0.0f : exp2f(s[32 * c + x] - m);
-                    rs += pc;
-                    if (a.split) {
-                        hi[x] = tf32_rna(pc);
-                        lo[x] = tf32_rna(pc - __uint_as_float(hi[x]));
-                    } else {
-                        hi[x] = tf32_rna(pc);
-                    }
-                }
-                tmem_st32(tl + C::col_s(bb) + 32 * c, hi);
-                if (a.split) tmem_st32(tl + C::col_plo(bb) + 32 * c, lo);
+            for (int c = 0; c < C::HB; c++) {
+                const float pc = dead ? 0.0f : ex2_approx(s[c] - m);
+                rs += pc;
+                phi[c] = tf32_rna(pc);
+                if (SPLIT) plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
             }
+            tmem_st<C::HB>(tl + C::col_s(bb) + half * C::HB, phi);
+            if (SPLIT) tmem_st<C::HB>(tl + C::col_plo(bb) + half * C::HB, plo);
             l = fmaf(l, corr, rs);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::P_FULL + bb));
-            // Fold the previous block: O = (O + O_blk(j-1)) * corr, in fp32 on the CUDA cores
-            // (O_blk(j-1) and O are both relative to the previous max; corr moves them to m).
+            // Fold the previous block: o = (o + O_blk(j-1)) * corr (both relative to the
+            // previous max; corr moves them to m).
             if (j >= 1) {
-                const int jp = j - 1, bp = jp & 1;
-                if (!mbar_wait(bar(C::PV_DONE + bp), (jp >> 1) & 1, abort, &g_tc_error)) {
+                if (!mbar_wait(bar(C::PV_DONE), (j - 1) & 1, abort, err)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < C::CHUNKS; c++) {
-                    uint32_t ob[32], o[32];
-                    tmem_ld32(tl + C::col_ob(bp) + 32 * c, ob);
-                    if (jp >= 1) tmem_ld32(tl + C::COL_O + 32 * c, o);
+                for (int c = 0; c < C::HD / 32; c++) {
+                    uint32_t r[32];
+                    tmem_ld32(tl + C::COL_OB + half * C::HD + 32 * c, r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int x = 0; x < 32; x++) {
-                        const float acc = jp >= 1 ? __uint_as_float(o[x]) + __uint_as_float(ob[x])
-                                                  : __uint_as_float(ob[x]);
-                        o[x] = __float_as_uint(acc * corr);
-                    }
-                    tmem_st32(tl + C::COL_O + 32 * c, o);
+                    for (int x = 0; x < 32; x++) o[32 * c + x] = (o[32 * c + x] + __uint_as_float(r[x])) * corr;
                 }
-                tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(bar(C::OB_FREE + bp));
+                mbar_arrive(bar(C::OB_FREE));
             }
         }
         if (ok && nblk > 0) {
-            ok = mbar_wait(bar(C::PV_DONE + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort, &g_tc_error);
+            ok = mbar_wait(bar(C::PV_DONE), (nblk - 1) & 1, abort, err);
             tc_fence_after();
         }
         const bool read_o = __all_sync(0xffffffffu, ok) && nblk > 0;
         const bool aborted = __any_sync(0xffffffffu, *abort != 0);
-        if (!aborted) {
+        if (read_o) {
+#pragma unroll
+            for (int c = 0; c < C::HD / 32; c++) {
+                uint32_t r[32];
+                tmem_ld32(tl + C::COL_OB + half * C::HD + 32 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int x = 0; x < 32; x++) o[32 * c + x] += __uint_as_float(r[x]);
+            }
+        }
+        // The row sum: this half's part plus the partner's.
+        xsum[half * C::BM + row] = l;
+        mbar_arrive(bar(C::XSUM));
+        const bool have_sum = mbar_wait(bar(C::XSUM), 0, abort, err);
+        l += xsum[(half ^ 1) * C::BM + row];
+        if (!aborted && have_sum && row_ok) {
             const float lfin = l == 0.0f ? 1.0f : l;
             const float mnat = m == -INFINITY ? 0.0f : m * LN2;
             const float inv = 1.0f / lfin;
-            float *orow = p.out + b * p.os[0] + h * p.os[1] + qrow * p.os[2];
-            const int last = (nblk - 1) & 1;
+            float *orow = p.out + b * p.os[0] + h * p.os[1] + qrow * p.os[2] + (int64_t)half * C::HD * p.os[3];
+            if (p.os[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15u) == 0) {
 #pragma unroll
-            for (int c = 0; c < C::CHUNKS; c++) {
-                uint32_t ob[32], o[32];
-                if (read_o) {
-                    tmem_ld32(tl + C::col_ob(last) + 32 * c, ob);
-                    if (nblk >= 2) tmem_ld32(tl + C::COL_O + 32 * c, o);
-                    tmem_wait_ld();
-                } else {
+                for (int x = 0; x < C::HD; x += 4)
+                    *reinterpret_cast<float4 *>(orow + x) =
+                        make_float4(o[x] * inv, o[x + 1] * inv, o[x + 2] * inv, o[x + 3] * inv);
+            } else {
 #pragma unroll
-                    for (int x = 0; x < 32; x++) ob[x] = 0u;
-                }
-                if (row_ok) {
-#pragma unroll
-                    for (int x = 0; x < 32; x++) {
-                        const float acc = (read_o && nblk >= 2) ? __uint_as_float(o[x]) + __uint_as_float(ob[x])
-                                                                : __uint_as_float(ob[x]);
-                        orow[(32 * c + x) * p.os[3]] = acc * inv;
-                    }
-                }
+                for (int x = 0; x < C::HD; x++) orow[x * p.os[3]] = o[x] * inv;
             }
-            if (row_ok) p.lse[b * p.ls[0] + h * p.ls[1] + qrow * p.ls[2]] = mnat + logf(lfin);
+            if (half == 0) p.lse[b * p.ls[0] + h * p.ls[1] + qrow * p.ls[2]] = mnat + logf(lfin);
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == C::W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
-
-// ------------------------------------------------------------------- host side -------
 
 template <class C>
 int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
@@ -468,24 +523,31 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     if (st) return st;
     TcFwdArgs a;
     a.p = p;
-    a.split = split;
     a.num_q_tiles = (int)((p.L + C::BM - 1) / C::BM);
     a.scale_log2 = p.scale * LOG2E;
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::SMEM);
+    a.err = device_error_word();
+    if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
+    auto kernel = split ? attn_fwd_tc_kernel<C, true> : attn_fwd_tc_kernel<C, false>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
     dim3 grid((unsigned)a.num_q_tiles, (unsigned)p.H, (unsigned)p.B);
     KernelTrace tr(C::D == 64 ? "fwd_tc_d64" : "fwd_tc_d128", stream);
-    attn_fwd_tc_kernel<C><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);
+    kernel<<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);
     return check_launch("attn_fwd_tc");
 }
 
-using Fwd64 = FwdCfg<64, 64, 2, 2>;
-using Fwd128 = FwdCfg<128, 32, 2, 1>;
+using Fwd64 = FwdCfg<64, 64, 3, 3>;
+using Fwd128 = FwdCfg<128, 32, 3, 3>;
 
 bool aligned16(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 }  // namespace
+
+int *device_error_word() {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_tc_error) != cudaSuccess) return nullptr;
+    return static_cast<int *>(ptr);
+}
 
 bool tc_forward_supported(const AttnProblem &p) {
     if (p.E != p.Ev || (p.E != 64 && p.E != 128)) return false;

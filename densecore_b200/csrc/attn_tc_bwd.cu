@@ -33,9 +33,6 @@
 #include "trace.h"
 
 namespace dc {
-
-extern __device__ int g_tc_error;
-
 namespace {
 
 using namespace sm100;
@@ -108,25 +105,39 @@ __device__ __forceinline__ void split_tile(uint8_t *hi, uint32_t lo_off, uint32_
 }
 
 // D[tmem] (+)= A x B over the three tf32 passes (cross terms first): A in TMEM (hi, lo
-// columns), B in shared memory (hi, lo descriptors built by `bdesc(kk, lo)`).
-template <class BDesc>
-__device__ __forceinline__ void mma3_ts(uint32_t d, uint32_t a_hi, uint32_t a_lo, int ksteps, BDesc bdesc,
-                                        uint32_t idesc, bool accumulate, int split) {
-    if (split) {
-        for (int kk = 0; kk < ksteps; kk++) {
-            mma_tf32_ts(d, a_hi + kk * 8, bdesc(kk, true), idesc, (accumulate || kk > 0) ? 1u : 0u);
-            mma_tf32_ts(d, a_lo + kk * 8, bdesc(kk, false), idesc, 1u);
+// columns), B in shared memory: `bhi` is the descriptor of the hi tile, the lo tile sits
+// BLK_BYTES further, and k-step kk starts OFF(kk) 16-byte units into the tile.
+template <bool SPLIT, int KSTEPS, class Off>
+__device__ __forceinline__ void mma3_ts(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t bhi, Off off,
+                                        uint32_t idesc, bool accumulate) {
+    constexpr uint32_t LO = BLK_BYTES >> 4;
+    if (SPLIT) {
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; kk++) {
+            mma_tf32_ts(d, a_hi + kk * 8, bhi + (LO + off(kk)), idesc, (accumulate || kk > 0) ? 1u : 0u);
+            mma_tf32_ts(d, a_lo + kk * 8, bhi + off(kk), idesc, 1u);
         }
     }
-    for (int kk = 0; kk < ksteps; kk++)
-        mma_tf32_ts(d, a_hi + kk * 8, bdesc(kk, false), idesc, (accumulate || split || kk > 0) ? 1u : 0u);
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; kk++)
+        mma_tf32_ts(d, a_hi + kk * 8, bhi + off(kk), idesc, (accumulate || SPLIT || kk > 0) ? 1u : 0u);
 }
+// k-step offsets (16-byte units): K-major 128-byte swizzle (8 tf32 = 32 bytes per k-step,
+// 4 k-steps per 128-byte chunk) and MN-major 32-byte-atom swizzle (8 rows = 1024 bytes).
+struct KOff {
+    __device__ __forceinline__ uint32_t operator()(int kk) const {
+        return (uint32_t)(((kk >> 2) * BLK_CHUNK + (kk & 3) * 32) >> 4);
+    }
+};
+struct MnOff {
+    __device__ __forceinline__ uint32_t operator()(int kk) const { return (uint32_t)(kk * 64); }
+};
 
 struct TcBwdArgs {
     AttnProblem p;
     AttnGrads g;
-    int split;
     float scale_log2;
+    int *err;
 };
 
 // ==================================================================== dK / dV ========
@@ -148,6 +159,7 @@ constexpr uint32_t C_KHI = 0, C_KLO = 64, C_VHI = 128, C_VLO = 192, C_S = 256, C
 static_assert(SMEM <= 232448, "smem");
 }  // namespace kv
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_qmn,
@@ -212,10 +224,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_4d(&tm_k, sb + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 tma_load_4d(&tm_v, sb + RES_BYTES + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
             }
-            bool ok = mbar_wait(bar(KV_READY), 0, abort, &g_tc_error);
+            bool ok = mbar_wait(bar(KV_READY), 0, abort, a.err);
             for (int i = 0; ok && i < nblk; i++) {
                 const int s = i % NST;
-                if (i >= NST && !mbar_wait(bar(ST_EMPTY + s), ((i / NST) - 1) & 1, abort, &g_tc_error)) break;
+                if (i >= NST && !mbar_wait(bar(ST_EMPTY + s), ((i / NST) - 1) & 1, abort, a.err)) break;
                 int64_t h, q0;
                 blk_coords(i, h, q0);
                 const uint32_t st = sb + OFF_STAGE + s * STAGE_BYTES;
@@ -238,36 +250,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 5) {
         // ------------------------------------------------------------------ MMA ------
         if (lane == 0) {
-            bool ok = mbar_wait(bar(KV_READY), 0, abort, &g_tc_error);
+            bool ok = mbar_wait(bar(KV_READY), 0, abort, a.err);
             tc_fence_after();
             for (int i = 0; ok && i < nblk; i++) {
                 const int s = i % NST;
                 const uint32_t st = sb + OFF_STAGE + s * STAGE_BYTES;
-                if (!mbar_wait(bar(ST_READY + s), (i / NST) & 1, abort, &g_tc_error)) break;
+                if (!mbar_wait(bar(ST_READY + s), (i / NST) & 1, abort, a.err)) break;
                 // The S / dP columns hold the previous block's P^T and dS^T until its
                 // gradient MMAs finish.
-                if (i >= 1 && !mbar_wait(bar(BLK_DONE), (i - 1) & 1, abort, &g_tc_error)) break;
+                if (i >= 1 && !mbar_wait(bar(BLK_DONE), (i - 1) & 1, abort, a.err)) break;
                 tc_fence_after();
-                auto kdesc = [&](uint32_t base) {
-                    return [=](int kk, bool lo) {
-                        return sdesc_sw128(base + (lo ? BLK_BYTES : 0) + (kk >> 2) * BLK_CHUNK + (kk & 3) * 32, 16,
-                                           1024);
-                    };
-                };
-                mma3_ts(tmem + C_S, tmem + C_KHI, tmem + C_KLO, D / 8, kdesc(st + ST_QK), IDESC_S, false, a.split);
-                mma3_ts(tmem + C_DP, tmem + C_VHI, tmem + C_VLO, D / 8, kdesc(st + ST_DOK), IDESC_S, false, a.split);
+                mma3_ts<SPLIT, D / 8>(tmem + C_S, tmem + C_KHI, tmem + C_KLO, sdesc_sw128(st + ST_QK, 16, 1024), KOff(),
+                                      IDESC_S, false);
+                mma3_ts<SPLIT, D / 8>(tmem + C_DP, tmem + C_VHI, tmem + C_VLO, sdesc_sw128(st + ST_DOK, 16, 1024),
+                                      KOff(), IDESC_S, false);
                 tc_commit(bar(S_FULL));
-                if (!mbar_wait(bar(P_FULL), i & 1, abort, &g_tc_error)) break;
+                if (!mbar_wait(bar(P_FULL), i & 1, abort, a.err)) break;
                 const bool first = (i % FOLD) == 0;
-                if (first && i >= FOLD && !mbar_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, &g_tc_error)) break;
+                if (first && i >= FOLD && !mbar_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, a.err)) break;
                 tc_fence_after();
-                auto mdesc = [&](uint32_t base) {
-                    return [=](int kk, bool lo) {
-                        return sdesc_mn_sw128_32b(base + (lo ? BLK_BYTES : 0) + kk * 1024, BLK_CHUNK, 512);
-                    };
-                };
-                mma3_ts(tmem + C_DV, tmem + C_S, tmem + C_PLO, BLK / 8, mdesc(st + ST_DOMN), IDESC_G, !first, a.split);
-                mma3_ts(tmem + C_DK, tmem + C_DP, tmem + C_DSLO, BLK / 8, mdesc(st + ST_QMN), IDESC_G, !first, a.split);
+                mma3_ts<SPLIT, BLK / 8>(tmem + C_DV, tmem + C_S, tmem + C_PLO,
+                                        sdesc_mn_sw128_32b(st + ST_DOMN, BLK_CHUNK, 512), MnOff(), IDESC_G, !first);
+                mma3_ts<SPLIT, BLK / 8>(tmem + C_DK, tmem + C_DP, tmem + C_DSLO,
+                                        sdesc_mn_sw128_32b(st + ST_QMN, BLK_CHUNK, 512), MnOff(), IDESC_G, !first);
                 tc_commit(bar(BLK_DONE));
                 tc_commit(bar(ST_EMPTY + s));
             }
@@ -281,21 +286,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int quad = warp & 3;  // this warp's TMEM lane quadrant
         const int row = quad * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        if (mbar_wait(bar(KV_FULL), 0, abort, &g_tc_error)) {
-            row_to_tmem(sg, row, tl, C_KHI, C_KLO, a.split);
-            row_to_tmem(sg + RES_BYTES, row, tl, C_VHI, C_VLO, a.split);
+        if (mbar_wait(bar(KV_FULL), 0, abort, a.err)) {
+            row_to_tmem(sg, row, tl, C_KHI, C_KLO, SPLIT);
+            row_to_tmem(sg + RES_BYTES, row, tl, C_VHI, C_VLO, SPLIT);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(KV_READY));
             for (int i = 0; i < nblk; i++) {
                 const int s = i % NST;
-                if (!mbar_wait(bar(ST_FULL + s), (i / NST) & 1, abort, &g_tc_error)) break;
+                if (!mbar_wait(bar(ST_FULL + s), (i / NST) & 1, abort, a.err)) break;
                 {
                     uint8_t *st = sg + OFF_STAGE + s * STAGE_BYTES;
-                    split_tile(st + ST_QK, BLK_BYTES, BLK_BYTES, ct, a.split);
-                    split_tile(st + ST_QMN, BLK_BYTES, BLK_BYTES, ct, a.split);
-                    split_tile(st + ST_DOK, BLK_BYTES, BLK_BYTES, ct, a.split);
-                    split_tile(st + ST_DOMN, BLK_BYTES, BLK_BYTES, ct, a.split);
+                    split_tile(st + ST_QK, BLK_BYTES, BLK_BYTES, ct, SPLIT);
+                    split_tile(st + ST_QMN, BLK_BYTES, BLK_BYTES, ct, SPLIT);
+                    split_tile(st + ST_DOK, BLK_BYTES, BLK_BYTES, ct, SPLIT);
+                    split_tile(st + ST_DOMN, BLK_BYTES, BLK_BYTES, ct, SPLIT);
                     fence_proxy_async_smem();
                 }
                 mbar_arrive(bar(ST_READY + s));
@@ -322,7 +327,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (i + 1 < nblk) load_rows(i + 1, lse_next, del_next);
             int64_t h, q0;
             blk_coords(i, h, q0);
-            if (!mbar_wait(bar(S_FULL), i & 1, abort, &g_tc_error)) {
+            if (!mbar_wait(bar(S_FULL), i & 1, abort, a.err)) {
                 ok = false;
                 break;
             }
@@ -344,9 +349,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     valid = key_ok && q < p.L && !(p.causal && key > q);
                     if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
                 }
-                const float pc = valid ? exp2f(x - lse_c) : 0.0f;
+                const float pc = valid ? ex2_approx(x - lse_c) : 0.0f;
                 const float ds = pc * (__uint_as_float(dr[c]) - del_c);
-                if (a.split) {
+                if (SPLIT) {
                     phi[c] = tf32_rna(pc);
                     plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
                     sr[c] = tf32_rna(ds);
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             tmem_st32(tl + C_S, phi);
             tmem_st32(tl + C_DP, sr);
-            if (a.split) {
+            if (SPLIT) {
                 tmem_st32(tl + C_PLO, plo);
                 tmem_st32(tl + C_DSLO, dr);
             }
@@ -367,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_arrive(bar(P_FULL));
             if ((i % FOLD) == FOLD - 1 || i == nblk - 1) {
                 // Fold this chain of block accumulators into the fp32 accumulators.
-                if (!mbar_wait(bar(BLK_DONE), i & 1, abort, &g_tc_error)) {
+                if (!mbar_wait(bar(BLK_DONE), i & 1, abort, a.err)) {
                     ok = false;
                     break;
                 }
@@ -421,6 +426,7 @@ static_assert(2 * RES_BYTES <= 2 * STAGE_BYTES, "resident staging fits in stages
 static_assert(SMEM <= 232448, "smem");
 }  // namespace qq
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_kk, const __grid_constant__ CUtensorMap tm_kmn,
@@ -473,10 +479,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_4d(&tm_q, sb + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 tma_load_4d(&tm_do, sb + RES_BYTES + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
             }
-            bool ok = mbar_wait(bar(QD_READY), 0, abort, &g_tc_error);
+            bool ok = mbar_wait(bar(QD_READY), 0, abort, a.err);
             for (int j = 0; ok && j < nblk; j++) {
                 const int s = j % NST;
-                if (j >= NST && !mbar_wait(bar(ST_EMPTY + s), ((j / NST) - 1) & 1, abort, &g_tc_error)) break;
+                if (j >= NST && !mbar_wait(bar(ST_EMPTY + s), ((j / NST) - 1) & 1, abort, a.err)) break;
                 const uint32_t st = sb + s * STAGE_BYTES;
                 mbar_expect_tx(bar(ST_FULL + s), 3 * BLK_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
@@ -495,33 +501,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp == 5) {
         if (lane == 0) {
-            bool ok = mbar_wait(bar(QD_READY), 0, abort, &g_tc_error);
+            bool ok = mbar_wait(bar(QD_READY), 0, abort, a.err);
             tc_fence_after();
             for (int j = 0; ok && j < nblk; j++) {
                 const int s = j % NST;
                 const uint32_t st = sb + s * STAGE_BYTES;
-                if (!mbar_wait(bar(ST_READY + s), (j / NST) & 1, abort, &g_tc_error)) break;
-                if (j >= 1 && !mbar_wait(bar(BLK_DONE), (j - 1) & 1, abort, &g_tc_error)) break;
+                if (!mbar_wait(bar(ST_READY + s), (j / NST) & 1, abort, a.err)) break;
+                if (j >= 1 && !mbar_wait(bar(BLK_DONE), (j - 1) & 1, abort, a.err)) break;
                 tc_fence_after();
-                auto kdesc = [&](uint32_t base) {
-                    return [=](int kk, bool lo) {
-                        return sdesc_sw128(base + (lo ? BLK_BYTES : 0) + (kk >> 2) * BLK_CHUNK + (kk & 3) * 32, 16,
-                                           1024);
-                    };
-                };
-                mma3_ts(tmem + C_S, tmem + C_QHI, tmem + C_QLO, D / 8, kdesc(st + ST_KK), IDESC_S, false, a.split);
-                mma3_ts(tmem + C_DP, tmem + C_DOHI, tmem + C_DOLO, D / 8, kdesc(st + ST_VK), IDESC_S, false, a.split);
+                mma3_ts<SPLIT, D / 8>(tmem + C_S, tmem + C_QHI, tmem + C_QLO, sdesc_sw128(st + ST_KK, 16, 1024), KOff(),
+                                      IDESC_S, false);
+                mma3_ts<SPLIT, D / 8>(tmem + C_DP, tmem + C_DOHI, tmem + C_DOLO, sdesc_sw128(st + ST_VK, 16, 1024),
+                                      KOff(), IDESC_S, false);
                 tc_commit(bar(S_FULL));
-                if (!mbar_wait(bar(DS_FULL), j & 1, abort, &g_tc_error)) break;
+                if (!mbar_wait(bar(DS_FULL), j & 1, abort, a.err)) break;
                 const bool first = (j % FOLD) == 0;
-                if (first && j >= FOLD && !mbar_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, &g_tc_error)) break;
+                if (first && j >= FOLD && !mbar_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, a.err)) break;
                 tc_fence_after();
-                auto mdesc = [&](uint32_t base) {
-                    return [=](int kk, bool lo) {
-                        return sdesc_mn_sw128_32b(base + (lo ? BLK_BYTES : 0) + kk * 1024, BLK_CHUNK, 512);
-                    };
-                };
-                mma3_ts(tmem + C_DQB, tmem + C_DP, tmem + C_DSLO, BLK / 8, mdesc(st + ST_KMN), IDESC_G, !first, a.split);
+                mma3_ts<SPLIT, BLK / 8>(tmem + C_DQB, tmem + C_DP, tmem + C_DSLO,
+                                        sdesc_mn_sw128_32b(st + ST_KMN, BLK_CHUNK, 512), MnOff(), IDESC_G, !first);
                 tc_commit(bar(BLK_DONE));
                 tc_commit(bar(ST_EMPTY + s));
             }
@@ -534,20 +532,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        if (mbar_wait(bar(QD_FULL), 0, abort, &g_tc_error)) {
-            row_to_tmem(sg, row, tl, C_QHI, C_QLO, a.split);
-            row_to_tmem(sg + RES_BYTES, row, tl, C_DOHI, C_DOLO, a.split);
+        if (mbar_wait(bar(QD_FULL), 0, abort, a.err)) {
+            row_to_tmem(sg, row, tl, C_QHI, C_QLO, SPLIT);
+            row_to_tmem(sg + RES_BYTES, row, tl, C_DOHI, C_DOLO, SPLIT);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(QD_READY));
             for (int j = 0; j < nblk; j++) {
                 const int s = j % NST;
-                if (!mbar_wait(bar(ST_FULL + s), (j / NST) & 1, abort, &g_tc_error)) break;
+                if (!mbar_wait(bar(ST_FULL + s), (j / NST) & 1, abort, a.err)) break;
                 {
                     uint8_t *st = sg + s * STAGE_BYTES;
-                    split_tile(st + ST_KK, BLK_BYTES, BLK_BYTES, ct, a.split);
-                    split_tile(st + ST_KMN, BLK_BYTES, BLK_BYTES, ct, a.split);
-                    split_tile(st + ST_VK, BLK_BYTES, BLK_BYTES, ct, a.split);
+                    split_tile(st + ST_KK, BLK_BYTES, BLK_BYTES, ct, SPLIT);
+                    split_tile(st + ST_KMN, BLK_BYTES, BLK_BYTES, ct, SPLIT);
+                    split_tile(st + ST_VK, BLK_BYTES, BLK_BYTES, ct, SPLIT);
                     fence_proxy_async_smem();
                 }
                 mbar_arrive(bar(ST_READY + s));
@@ -563,7 +561,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bool ok = true;
         for (int j = 0; j < nblk; j++) {
             const int64_t kb0 = (int64_t)j * BLK;
-            if (!mbar_wait(bar(S_FULL), j & 1, abort, &g_tc_error)) {
+            if (!mbar_wait(bar(S_FULL), j & 1, abort, a.err)) {
                 ok = false;
                 break;
             }
@@ -582,9 +580,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     valid = row_ok && key < p.S && !(p.causal && key > q);
                     if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
                 }
-                const float pc = valid ? exp2f(x - lse2) : 0.0f;
+                const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
                 const float ds = pc * (__uint_as_float(dr[c]) - del);
-                if (a.split) {
+                if (SPLIT) {
                     sr[c] = tf32_rna(ds);
                     dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
                 } else {
@@ -592,12 +590,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             tmem_st32(tl + C_DP, sr);
-            if (a.split) tmem_st32(tl + C_DSLO, dr);
+            if (SPLIT) tmem_st32(tl + C_DSLO, dr);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(DS_FULL));
             if ((j % FOLD) == FOLD - 1 || j == nblk - 1) {
-                if (!mbar_wait(bar(BLK_DONE), j & 1, abort, &g_tc_error)) {
+                if (!mbar_wait(bar(BLK_DONE), j & 1, abort, a.err)) {
                     ok = false;
                     break;
                 }
@@ -667,8 +665,10 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     TcBwdArgs a;
     a.p = p;
     a.g = g;
-    a.split = precision == DC_PREC_TF32 ? 0 : 1;
     a.scale_log2 = p.scale * LOG2E;
+    a.err = device_error_word();
+    if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
+    const bool split = precision != DC_PREC_TF32;
     // grad_out shares q's shape but has its own strides.
     const int64_t *dos = g.dos;
     CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
@@ -680,12 +680,12 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     if (!st) st = make_tmap(&tdomn, g.dout, D, p.L, p.H, p.B, dos, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (st) return st;
     if (p.S > 0) {
-        cudaError_t e = cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)kv::SMEM);
+        auto kernel = split ? attn_bwd_dkdv_tc_kernel<true> : attn_bwd_dkdv_tc_kernel<false>;
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
         dim3 grid((unsigned)((p.S + TILE - 1) / TILE), (unsigned)p.Hkv, (unsigned)p.B);
         KernelTrace tr("bwd_dkdv_tc", stream);
-        attn_bwd_dkdv_tc_kernel<<<grid, THREADS, kv::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
+        kernel<<<grid, THREADS, kv::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
         if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
     }
     if (p.L > 0) {
@@ -696,12 +696,12 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         if (!st) st = make_tmap(&tkmn, p.k, D, p.S, p.Hkv, p.B, p.ks, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (!st) st = make_tmap(&tvk, p.v, D, p.S, p.Hkv, p.B, p.vs, BLK);
         if (st) return st;
-        cudaError_t e = cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)qq::SMEM);
+        auto kernel = split ? attn_bwd_dq_tc_kernel<true> : attn_bwd_dq_tc_kernel<false>;
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
         dim3 grid((unsigned)((p.L + TILE - 1) / TILE), (unsigned)p.H, (unsigned)p.B);
         KernelTrace tr("bwd_dq_tc", stream);
-        attn_bwd_dq_tc_kernel<<<grid, THREADS, qq::SMEM, stream>>>(tq, tdo, tkk, tkmn, tvk, a);
+        kernel<<<grid, THREADS, qq::SMEM, stream>>>(tq, tdo, tkk, tkmn, tvk, a);
         if ((st = check_launch("attn_bwd_dq_tc"))) return st;
     }
     return DC_OK;

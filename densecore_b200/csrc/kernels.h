@@ -35,5 +35,7 @@ bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g);
 int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream);
 // The tensor-core kernels' device error word (sm100::DeviceError); -1 if it cannot be read.
 int device_error(int reset);
+// Device address of that word (passed to the kernels), or nullptr.
+int *device_error_word();
 
 }  // namespace dc

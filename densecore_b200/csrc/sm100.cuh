@@ -209,6 +209,13 @@ __device__ __forceinline__ uint64_t sdesc_mn_sw128_32b(uint32_t saddr, uint32_t 
     return d;
 }
 
+// 2^x with the hardware approximation (MUFU.EX2, ~2 ulp, results below 2^-126 flushed to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ---------------------------------------------------------------- TF32 ------------
 // Round to the nearest TF32 value (ties away from zero); the low 13 mantissa bits become 0.
 __device__ __forceinline__ uint32_t tf32_rna(float x) {
