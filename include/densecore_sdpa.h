@@ -139,7 +139,7 @@ DC_API int dc_kernel_timing(int enable);
 DC_API int dc_kernel_timing_report(char *buf, size_t len, int reset);
 
 /* Device-side status of the tensor-core kernels: 0, or 1 when a kernel gave up on a wait
- * that did not complete within its bound (2 s); that CTA then unwound without writing its
+ * that did not complete within its bound (1 s); that CTA then unwound without writing its
  * outputs. Synchronises with the device. reset != 0 clears the status. -1 on a CUDA error. */
 DC_API int dc_device_status(int reset);
 
