@@ -412,16 +412,19 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             }
             const bool dead = (m == -INFINITY);
             float rs = 0.0f;
-            uint32_t phi[C::HB], plo[C::HB];
 #pragma unroll
-            for (int c = 0; c < C::HB; c++) {
-                const float pc = dead ? 0.0f : ex2_approx(s[c] - m);
-                rs += pc;
-                phi[c] = tf32_rna(pc);
-                if (SPLIT) plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
+            for (int r0 = 0; r0 < C::HB; r0 += 16) {  // P in 16-column pieces
+                uint32_t phi[16], plo[16];
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    const float pc = dead ? 0.0f : ex2_approx(s[r0 + c] - m);
+                    rs += pc;
+                    phi[c] = tf32_rna(pc);
+                    if (SPLIT) plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
+                }
+                tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
+                if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);
             }
-            tmem_st<C::HB>(tl + C::col_s(bb) + half * C::HB, phi);
-            if (SPLIT) tmem_st<C::HB>(tl + C::col_plo(bb) + half * C::HB, plo);
             l = fmaf(l, corr, rs);
             tmem_wait_st();
             tc_fence_before();
@@ -435,12 +438,12 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < C::HD / 32; c++) {
-                    uint32_t r[32];
-                    tmem_ld32(tl + C::COL_OB + half * C::HD + 32 * c, r);
+                for (int c = 0; c < C::HD / 16; c++) {
+                    uint32_t r[16];
+                    tmem_ld16(tl + C::COL_OB + half * C::HD + 16 * c, r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int x = 0; x < 32; x++) o[32 * c + x] = (o[32 * c + x] + __uint_as_float(r[x])) * corr;
+                    for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(r[x])) * corr;
                 }
                 tc_fence_before();
                 mbar_arrive(bar(C::OB_FREE));

@@ -364,12 +364,12 @@ __global__ void __maxnreg__(128)
             }
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < CHUNKS; c++) {
-                uint32_t r[32];
-                tmem_ld32(tl + col + 32 * c, r);
+            for (int c = 0; c < D / 16; c++) {
+                uint32_t r[16];
+                tmem_ld16(tl + col + 16 * c, r);
                 tmem_wait_ld();
 #pragma unroll
-                for (int x = 0; x < 32; x++) acc[32 * c + x] += __uint_as_float(r[x]);
+                for (int x = 0; x < 16; x++) acc[16 * c + x] += __uint_as_float(r[x]);
             }
             tc_fence_before();
             mbar_arrive(bar(BLK_FREE));
@@ -414,13 +414,8 @@ __global__ void __maxnreg__(128)
                 uint32_t sr[16], dr[16], phi[16], plo[16];
                 tmem_ld16(tl + c_s(bb) + 16 * hf, sr);
                 tmem_ld16(tl + c_dp(bb) + 16 * hf, dr);
-                float lse2[16], del[16];
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const float4 u = rows[4 * hf + c], w = rows[BLK / 4 + 4 * hf + c];
-                    lse2[4 * c] = u.x, lse2[4 * c + 1] = u.y, lse2[4 * c + 2] = u.z, lse2[4 * c + 3] = u.w;
-                    del[4 * c] = w.x, del[4 * c + 1] = w.y, del[4 * c + 2] = w.z, del[4 * c + 3] = w.w;
-                }
+                const float *lse2 = reinterpret_cast<const float *>(rows) + 16 * hf;
+                const float *del = reinterpret_cast<const float *>(rows) + BLK + 16 * hf;
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
@@ -642,12 +637,12 @@ __global__ void __maxnreg__(128)
             }
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < CHUNKS; c++) {
-                uint32_t r[32];
-                tmem_ld32(tl + C_DQB + 32 * c, r);
+            for (int c = 0; c < D / 16; c++) {
+                uint32_t r[16];
+                tmem_ld16(tl + C_DQB + 16 * c, r);
                 tmem_wait_ld();
 #pragma unroll
-                for (int x = 0; x < 32; x++) dq[32 * c + x] += __uint_as_float(r[x]);
+                for (int x = 0; x < 16; x++) dq[16 * c + x] += __uint_as_float(r[x]);
             }
             tc_fence_before();
             mbar_arrive(bar(BLK_FREE));
@@ -671,27 +666,30 @@ __global__ void __maxnreg__(128)
             const int64_t kb0 = (int64_t)j * BLK;
             if (!mbar_wait(bar(S_FULL + bb), (j >> 1) & 1, abort, err)) break;
             tc_fence_after();
-            uint32_t sr[32], dr[32];
-            tmem_ld32(tl + c_s(bb), sr);
-            tmem_ld32(tl + c_dp(bb), dr);
-            tmem_wait_ld();
             const bool edge = !row_ok || kb0 + BLK > p.S || (p.causal && kb0 + BLK - 1 > q0) || p.mask_kind != MASK_NONE;
 #pragma unroll
-            for (int c = 0; c < BLK; c++) {
-                float x = __uint_as_float(sr[c]) * a.scale_log2;
-                bool valid = true;
-                if (edge) {
-                    const int64_t key = kb0 + c;
-                    valid = row_ok && key < p.S && !(p.causal && key > q);
-                    if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
+            for (int hf = 0; hf < 2; hf++) {  // 16 key columns at a time
+                uint32_t sr[16], dr[16];
+                tmem_ld16(tl + c_s(bb) + 16 * hf, sr);
+                tmem_ld16(tl + c_dp(bb) + 16 * hf, dr);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    float x = __uint_as_float(sr[c]) * a.scale_log2;
+                    bool valid = true;
+                    if (edge) {
+                        const int64_t key = kb0 + 16 * hf + c;
+                        valid = row_ok && key < p.S && !(p.causal && key > q);
+                        if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
+                    }
+                    const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
+                    const float ds = pc * (__uint_as_float(dr[c]) - del);
+                    sr[c] = tf32_rna(ds);
+                    if (SPLIT) dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
                 }
-                const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
-                const float ds = pc * (__uint_as_float(dr[c]) - del);
-                sr[c] = tf32_rna(ds);
-                if (SPLIT) dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
+                tmem_st16(tl + c_dp(bb) + 16 * hf, sr);
+                if (SPLIT) tmem_st16(tl + c_dslo(bb) + 16 * hf, dr);
             }
-            tmem_st32(tl + c_dp(bb), sr);
-            if (SPLIT) tmem_st32(tl + c_dslo(bb), dr);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(DS_FULL + bb));

@@ -233,11 +233,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 // ---------------------------------------------------------------- TF32 ------------
-// Round to the nearest TF32 value (ties away from zero); the low 13 mantissa bits become 0.
+// Round to the nearest TF32 value, ties away from zero (what cvt.rna.tf32.f32 computes): on
+// the sign-magnitude encoding, add half a TF32 ulp (bit 12) to the magnitude and clear the 13
+// low mantissa bits. A carry into the exponent gives the next power of two, as rounding
+// should; +-Inf and NaN come out unchanged. Two integer ops on the full-rate ALU pipe instead
+// of a conversion instruction.
 __device__ __forceinline__ uint32_t tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
+    return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 
 }  // namespace sm100
