@@ -21,7 +21,7 @@ DC_PREC_3XTF32, DC_PREC_TF32, DC_PREC_FP32 = 0, 1, 2
 
 # Every entry point include/densecore_sdpa.h declares.
 EXPORTS = ("dc_sdpa_fwd", "dc_sdpa_bwd_workspace_size", "dc_sdpa_bwd", "dc_sdpa_decode_workspace_size",
-           "dc_sdpa_decode_default_splits", "dc_sdpa_decode", "dc_attn_merge", "dc_attn_probs",
+           "dc_sdpa_decode_default_splits", "dc_sdpa_decode", "dc_sdpa_decode_noalloc", "dc_attn_merge", "dc_attn_probs",
            "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report", "dc_device_status")
 
 
@@ -62,6 +62,8 @@ def load():
         L.dc_sdpa_decode_default_splits.restype = i
         L.dc_sdpa_decode.argtypes = [_P, _P, _P, _P, i, d, i, _P, _P, vp, sz, vp]
         L.dc_sdpa_decode.restype = i
+        L.dc_sdpa_decode_noalloc.argtypes = [_P, _P, _P, _P, i, d, i, _P, _P, vp]
+        L.dc_sdpa_decode_noalloc.restype = i
         L.dc_attn_merge.argtypes = [_P, _P, _P, _P, vp]
         L.dc_attn_merge.restype = i
         L.dc_attn_probs.argtypes = [_P, _P, _P, _P, i, i, d, i, _P, vp]

@@ -11,6 +11,7 @@
 #include <math.h>
 
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -181,6 +182,41 @@ int pick_forward_path(const AttnProblem &p, int precision) {
 }
 
 }  // namespace
+
+// Scratch of dc_sdpa_decode_noalloc: the table of split partials (Ev accumulators, the running
+// max and the running sum per split) lives in this fixed device array instead of caller or
+// stream-ordered memory. Nothing in it has to start at zero: the split kernel writes every
+// slot of the table before the combine kernel reads it, so the array's contents at module
+// load are never used.
+static __device__ __align__(256) float g_decode_scratch[DC_DECODE_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+
+constexpr int kScratchDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_addr[kScratchDevices];
+
+// Device address of g_decode_scratch on the current device. The lookup runs once per device,
+// with that device current (it may load the library's module there), and is cached.
+int decode_scratch(void **ptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "decode scratch: current device");
+    if (dev < 0 || dev >= kScratchDevices)
+        return fail(DC_ERR_UNSUPPORTED, "decode scratch: device ordinal " + std::to_string(dev) +
+                                            " is above " + std::to_string(kScratchDevices - 1));
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void *addr = nullptr;
+        e = cudaGetSymbolAddress(&addr, g_decode_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "decode scratch: cudaGetSymbolAddress");
+        g_scratch_addr[dev] = addr;
+    }
+    *ptr = g_scratch_addr[dev];
+    return DC_OK;
+}
+
+}  // namespace
 }  // namespace dc
 
 using namespace dc;
@@ -331,6 +367,44 @@ int dc_sdpa_decode(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t
                      "decode workspace")))
         return st;
     return decode_forward(p, splits, ws.ptr, s);
+}
+
+// The split-KV decode of dc_sdpa_decode with its partials in g_decode_scratch. It exists for
+// callers that must not have the library allocate: a serving loop that has reserved the
+// device's free memory for its KV cache up front (a hidden cudaMallocAsync would then fail or
+// eat into the cache), and hosts reaching the library through a plain C FFI that own no
+// allocator and cannot hand over a workspace. Everything else matches dc_sdpa_decode.
+int dc_sdpa_decode_noalloc(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                           const dc_tensor_t *mask, int has_scale, double scale, int num_splits,
+                           dc_tensor_t *out, dc_tensor_t *lse, void *stream) {
+    AttnProblem p;
+    int st = fill_problem(q, k, v, 0, has_scale, scale, p);
+    if (!st) st = fill_mask(mask, p);
+    if (!st) st = check_out(out, lse, p);
+    if (st) return st;
+    if (p.L != 1) return fail(DC_ERR_VALUE, "decode takes a query length of 1");
+    p.out = static_cast<float *>(out->data);
+    p.lse = static_cast<float *>(lse->data);
+    copy_strides(out, p.os, 4);
+    copy_strides(lse, p.ls, 3);
+    if (!decode_supported(p))
+        return fail(DC_ERR_UNSUPPORTED,
+                    "decode needs head dim 64 or 128, E == Ev, unit-stride rows on 16-byte "
+                    "boundaries; use dc_sdpa_fwd");
+    if (p.B == 0 || p.H == 0) return DC_OK;
+    const int splits = num_splits > 0 ? (num_splits > 1024 ? 1024 : num_splits) : decode_pick_splits(p);
+    const size_t need = decode_workspace_bytes(p.B, p.H, p.Ev, splits);
+    if (need > (size_t)DC_DECODE_NOALLOC_SCRATCH_BYTES)
+        return fail(DC_ERR_VALUE,
+                    "dc_sdpa_decode_noalloc: " + std::to_string(splits) + " splits over " +
+                        std::to_string(p.B * p.H) + " (batch, head) rows need " +
+                        std::to_string(need) + " bytes of scratch, more than its fixed " +
+                        std::to_string((size_t)DC_DECODE_NOALLOC_SCRATCH_BYTES) +
+                        "; pass fewer splits or call dc_sdpa_decode with a workspace");
+    if ((st = device_ok())) return st;
+    void *scratch = nullptr;
+    if ((st = decode_scratch(&scratch))) return st;
+    return decode_forward(p, splits, scratch, static_cast<cudaStream_t>(stream));
 }
 
 int dc_attn_merge(dc_tensor_t *out_acc, dc_tensor_t *lse_acc, const dc_tensor_t *out_part,

@@ -9,6 +9,7 @@
  *   dc_sdpa_fwd   <- _flash_attention           src/lib.rs:609-638 (-> torch_attention::forward)
  *   dc_sdpa_bwd   <- _flash_attention_backward  src/lib.rs:640-683 (-> torch_attention::backward)
  *   dc_sdpa_decode   q_len == 1 case of _flash_attention (torch_attention.rs:157, q_split -> 1)
+ *   dc_sdpa_decode_noalloc  the same with a static scratch array (no reference counterpart)
  *   dc_attn_merge    logsumexp merge of partial results (ring attention; no CPU counterpart)
  *   dc_attn_probs    softmax(scale*QK^T + mask) averaged over heads: the need_weights output of
  *                    multi_head_attention_forward (python/densecore/functional.py:456-461)
@@ -111,6 +112,27 @@ DC_API int dc_sdpa_decode(const dc_tensor_t *q, const dc_tensor_t *k, const dc_t
                    const dc_tensor_t *mask, int has_scale, double scale, int num_splits,
                    dc_tensor_t *out, dc_tensor_t *lse, void *workspace, size_t workspace_bytes,
                    void *stream);
+
+/* Fixed size of the device scratch dc_sdpa_decode_noalloc holds per device: 8 MiB, enough for
+ * the default split count (148 SMs) of up to 16131 (batch, head) rows at head dim 128. */
+#define DC_DECODE_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* dc_sdpa_decode that allocates no device memory: the split partials go to a static device
+ * array of DC_DECODE_NOALLOC_SCRATCH_BYTES in the library instead of a workspace. For callers
+ * that cannot let the library allocate (device memory reserved up front for a KV cache; C
+ * hosts with no allocator to hand a workspace from). No counterpart in the reference: its CPU
+ * path allocates its scratch on the heap per call.
+ *  - A request whose partials need more than DC_DECODE_NOALLOC_SCRATCH_BYTES
+ *    (B*H*splits*(Ev+2)*4 bytes) fails with DC_ERR_VALUE before anything is launched.
+ *  - There is one scratch array per device, shared by every call on that device: calls whose
+ *    kernels overlap in time (different streams, or host threads without ordering between
+ *    them) overwrite each other's partials. Order them, e.g. on one stream.
+ *  - The first call on a device looks up the array's address (cudaGetSymbolAddress, which
+ *    may load the module); make that first call before any stream capture begins.
+ * Results are those of dc_sdpa_decode with the same num_splits. */
+DC_API int dc_sdpa_decode_noalloc(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                                  const dc_tensor_t *mask, int has_scale, double scale,
+                                  int num_splits, dc_tensor_t *out, dc_tensor_t *lse, void *stream);
 
 /* In-place logsumexp merge of a partial attention result into an accumulator over the same
  * rows: lse = log(exp(lse_acc) + exp(lse_part)), out_acc = out_acc*exp(lse_acc - lse) +
