@@ -13,7 +13,9 @@ Workloads (synthetic seeded inputs of each config's sha
 
 Scaling is weak: under torchrun every rank runs the full workload on its own GPU (its shard of
 a global batch N times larger); there is no data-path collective. ``value`` = work of all
-ranks / max-over-ranks device time.
+ranks / max-over-ranks device time. The exception is long_causal_fwd on N > 1 GPUs: the ranks
+share one sequence through ring attention (zig-zag shards, NCCL send/recv of K/V blocks,
+logsumexp merge), so scaling is strong and ``value`` = the sequence's work / max device time.
 """
 from __future__ import annotations
 
@@ -292,9 +294,23 @@ def main():
     dc.set_sdpa_precision(args.precision)
     _lib.load()
 
-    q, k, v, g, mask = make_inputs(w, device, seed=1234 + rank)
+    # Config 4 on several GPUs is sequence-parallel (ring attention over zig-zag shards of one
+    # sequence: strong scaling); every other run gives each rank a whole workload (weak scaling).
+    ring = None
+    if w["cfg"] == 4 and world > 1:
+        from densecore_b200.ring import RingAttention, zigzag_shard
+        full = make_inputs(w, device, seed=1234)
+        q, k, v = (zigzag_shard(t, rank, world) for t in full[:3])
+        g, mask = None, None
+        del full
+        ring = RingAttention(q.shape, k.shape, device, causal=True)
+    else:
+        q, k, v, g, mask = make_inputs(w, device, seed=1234 + rank)
     causal = w["causal"]
-    if w["cfg"] == 5:
+    if ring is not None:
+        def step():
+            ring(q, k, v)
+    elif w["cfg"] == 5:
         splits = _lib.load().dc_sdpa_decode_default_splits(q.shape[0], q.shape[1], k.shape[2])
         ws = torch.empty(_lib.load().dc_sdpa_decode_workspace_size(q.shape[0], q.shape[1], v.shape[3], splits),
                          dtype=torch.uint8, device=device)
@@ -342,7 +358,8 @@ def main():
         ms_max = float(t.item())
     amount, unit = work(w)
     scale = 1e9 if unit == "GB/s" else 1e12
-    value = world * amount / (ms_max / 1e3) / scale
+    ranks_work = 1 if ring is not None else world  # strong scaling: the ranks share one workload
+    value = ranks_work * amount / (ms_max / 1e3) / scale
 
     # Roofline of the dominant kernel (largest total device time in the timed region).
     pk = peaks()
@@ -352,6 +369,10 @@ def main():
         kname, (launches, total_ms) = dom
         per_launch = kernel_work(w, kname)
         avg_ms = total_ms / max(launches, 1)
+        if ring is not None:
+            # Ring launches differ in size; per step the rank's forward launches together do
+            # 1/world of the sequence's algorithmic flops.
+            per_launch = amount / world / (launches / args.steps)
         if unit == "GB/s":
             achieved = per_launch / (avg_ms / 1e3) / 1e9
             peak, ru, bound = pk["hbm"], "GB/s", "hbm"
@@ -373,7 +394,7 @@ def main():
     # End to end through the public API with pinned host buffers; copies in the timed region.
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist)
+        e2e = run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring)
 
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -381,12 +402,15 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+                "scaling": "strong" if ring is not None else "weak",
                 "vs_baseline": None, "dtype": "f32" if args.precision == "fp32" else args.precision,
                 "data": "synthetic (seeded N(0,1) of the config's shape)",
                 "config": {"workload": name, "baseline_cfg": w["cfg"], "shape_q": list(w["q"]),
                            "shape_kv": list(w["kv"]), "causal": causal, "mask": w["mask"],
-                           "per_rank": "full workload (weak scaling)", "parallelism": f"dp{world}",
+                           "per_rank": ("zig-zag sequence shard (ring attention, NCCL send/recv)"
+                                        if ring is not None else "full workload (weak scaling)"),
+                           "parallelism": f"ring{world}" if ring is not None else f"dp{world}",
                            "precision": args.precision, "l2": "flushed (256 MB write) before every timed step"},
                 "roofline": roofline, "kernels": {k_: {"launches": v_[0], "total_ms": v_[1]}
                                                   for k_, v_ in kernels.items()},
@@ -397,14 +421,16 @@ def main():
         dist.destroy_process_group()
 
 
-def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist):
+def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
     import densecore_b200 as dc
     ins = [q, k, v] + ([g] if g is not None else [])
     if w["cfg"] == 5:
         ins = [q]  # the KV cache is device-resident state; a decode step brings its query
     host_in = [t.detach().cpu().pin_memory() for t in ins]
     dev_in = [torch.empty_like(t) for t in ins]
-    if w["cfg"] == 5:
+    if ring is not None:
+        outs_shape = [tuple(q.shape)]
+    elif w["cfg"] == 5:
         outs_shape = [(w["q"][0], w["q"][1], 1, w["kv"][3])]
     elif w["bwd"]:
         outs_shape = [tuple(w["q"]), tuple(w["q"]), tuple(w["kv"]), tuple(w["kv"])]
@@ -415,7 +441,9 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist):
     def step():
         for h, d in zip(host_in, dev_in):
             d.copy_(h, non_blocking=True)
-        if w["cfg"] == 5:
+        if ring is not None:
+            res = [ring(*dev_in)[0]]
+        elif w["cfg"] == 5:
             res = [dc.scaled_dot_product_attention(dev_in[0], k, v)]
         elif w["bwd"]:
             tq, tk, tv = (t.requires_grad_(True) for t in dev_in[:3])
@@ -448,6 +476,8 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist):
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    if ring is not None:
+        world = 1  # the ranks share one sequence
     return {"value": world * amount / (ms / 1e3) / scale, "unit": "GB/s" if scale == 1e9 else "TFLOP/s",
             "ms_per_step": ms, "h2d_bytes_per_step": sum(t.numel() * 4 for t in host_in),
             "d2h_bytes_per_step": sum(t.numel() * 4 for t in host_out)}
