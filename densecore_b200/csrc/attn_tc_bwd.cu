@@ -3,30 +3,32 @@
 // Replaces DenseCore's torch_attention::backward (src/torch_attention.rs:291-468), which per
 // (q block, kv block) recomputes P = exp(scale*S + mask - lse) (:338-380) and accumulates
 //   dV += P^T dO, dP = dO V^T, dS = P (dP - delta), dQ += scale dS K, dK += scale dS^T Q
-// (:381-446), with delta = sum(dO * O) per row (:327-330, computed by bwd_delta_kernel).
+// (:381-446), with delta = sum(dO * O) per row (:327-330).
 //
-// Two kernels, so every accumulator has one owner and no atomics are needed:
+// Three launches:
 //
-//   dkdv: a CTA owns 128 keys of one (batch, kv head). K and V are the A operands: tf32 hi in
-//         TMEM, lo in shared memory. 32-row blocks of Q and dO stream through shared memory,
-//         each in two layouts (128-byte swizzle for the K-major use, 32-byte-atom swizzle for
-//         the MN-major use that tf32 requires). Per block i: S^T = K Q^T and dP^T = V dO^T
-//         into one of two TMEM buffers; the softmax threads (one per key) turn them into P^T
-//         and dS^T (tf32 hi / lo, in place); then dV_blk += P^T dO and dK_blk += dS^T Q.
-//         Issue order S0, S1, G0, S2, G1, ... keeps the tensor core busy while the softmax
-//         threads work. Fold threads add the block accumulators into fp32 registers every
-//         FOLD blocks (the tensor core's accumulation is coarser than fp32 over long chains).
+//   prep: one pass over q, grad_out, out, k and v (HBM-bound). Writes TF32 hi = tf32(x) and
+//         lo = tf32(x - hi) copies of q, grad_out, k and v into contiguous scratch (3xTF32:
+//         a*b ~ ah*bl + al*bh + ah*bh), delta per query row, and lse in base 2. The tensor-core
+//         kernels then load ready operands with TMA and never convert on the critical path;
+//         they also accept inputs of any strides.
+//   dkdv: a CTA owns 128 keys of one (batch, kv head). K and V are the A operands: hi in TMEM,
+//         lo in shared memory. 32-row blocks of Q and dO (hi and lo, each in the K-major
+//         128-byte swizzle and in the MN-major 32-byte-atom swizzle that tf32 requires) stream
+//         through a 2-stage ring. Per block i: S^T = K Q^T and dP^T = V dO^T into one of two
+//         TMEM buffers; eight softmax warps (two per TMEM lane quadrant, 16 query columns
+//         each) turn them into P^T and dS^T (hi / lo, in place); then dV_blk += P^T dO and
+//         dK_blk += dS^T Q. Issue order S0, S1, G0, S2, G1, ... keeps the tensor core busy
+//         while the softmax warps work. The same warps add the block accumulators into fp32
+//         registers every FOLD blocks (the tensor core's accumulation is coarser than fp32
+//         over long chains): the first four keep dV, the other four dK.
 //   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi in
-//         TMEM, lo in shared memory); 32-key blocks of K (two layouts) and V stream through
-//         shared memory. Per block: S = Q K^T and dP = dO V^T, dS in TMEM, dQ_blk += dS K;
-//         the fold threads keep dQ in fp32 registers.
+//         TMEM, lo in shared memory); 32-key blocks of K (two layouts) and V stream through a
+//         3-stage ring. Per block: S = Q K^T and dP = dO V^T, dS in TMEM, dQ_blk += dS K,
+//         folded into fp32 registers (each softmax warp keeps 32 of the 64 dQ columns).
 //
-// Roles: warps 0-3 softmax (one TMEM lane each); fold warps (dq: 4-7 for dQ; dkdv: 4-7 for
-// dV and 8-11 for dK, one lane each); converter warps (fp32 -> tf32 hi / lo; per-block lse and
-// delta into shared memory; dq: four, which also load Q / dO into TMEM; dkdv: two, the
-// softmax warps load K / V); one TMA producer warp; one MMA issuer warp (also the TMEM owner).
-// No SM sub-partition holds more than four warps, so a thread may use 128 registers. Every
-// wait is bounded; on a timeout the kernel records an error and unwinds.
+// Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer (one
+// thread; it also owns TMEM). Every wait is bounded; a timeout records an error and unwinds.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -48,6 +50,9 @@ constexpr int CHUNKS = D / 32;
 constexpr int TILE = 128;    // rows owned by a CTA (the MMA M)
 constexpr int BLK = 32;      // streamed rows per step (the MMA N of S / dP, the K of the rest)
 constexpr int FOLD = 2;      // blocks per tensor-core accumulation chain
+constexpr int THREADS = 320; // 8 softmax / fold warps, producer, MMA issuer
+constexpr int W_PROD = 8, W_MMA = 9;
+constexpr unsigned FULL = 0xffffffffu;
 
 constexpr uint32_t RES_BYTES = TILE * D * 4;      // one resident fp32 tile (32 KB)
 constexpr uint32_t RES_CHUNK = TILE * 128;        // 16 KB per 32-column chunk
@@ -102,81 +107,138 @@ __device__ __forceinline__ void mma_g(uint32_t d, uint32_t a_hi, uint32_t a_lo, 
         mma_tf32_ts(d, a_hi + kk * 8, b_hi + mnoff(kk), IDESC_G, (accumulate || SPLIT || kk > 0) ? 1u : 0u);
 }
 
-// Row `row` of a raw 128-byte-swizzled TILE-row tile: tf32 hi into TMEM (col_hi, this lane)
-// and, with SPLIT, lo into `lo` at the same swizzled position. A full warp calls it.
-template <bool SPLIT>
-__device__ __forceinline__ void row_split(const uint8_t *raw, uint8_t *lo, int row, uint32_t tlane,
-                                          uint32_t col_hi) {
+// Row `row` of a 128-byte-swizzled TILE-row tile in shared memory into TMEM columns
+// [col, col + 64) of this thread's lane. A full warp calls it.
+__device__ __forceinline__ void row_to_tmem(const uint8_t *tile, int row, uint32_t tlane, uint32_t col) {
 #pragma unroll
     for (int c = 0; c < CHUNKS; c++) {
-        uint32_t hi[32];
+        uint32_t v[32];
 #pragma unroll
         for (int g = 0; g < 8; g++) {
-            const uint32_t off = c * RES_CHUNK + row * 128 + ((g ^ (row & 7)) * 16);
-            const float4 x = *reinterpret_cast<const float4 *>(raw + off);
-            const float v[4] = {x.x, x.y, x.z, x.w};
-            float4 lv;
-            float *lp = &lv.x;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                hi[4 * g + e] = tf32_rna(v[e]);
-                lp[e] = __uint_as_float(tf32_rna(v[e] - __uint_as_float(hi[4 * g + e])));
-            }
-            if (SPLIT) *reinterpret_cast<float4 *>(lo + off) = lv;
+            const uint4 x = *reinterpret_cast<const uint4 *>(tile + c * RES_CHUNK + row * 128 + ((g ^ (row & 7)) * 16));
+            v[4 * g] = x.x;
+            v[4 * g + 1] = x.y;
+            v[4 * g + 2] = x.z;
+            v[4 * g + 3] = x.w;
         }
-        tmem_st32(tlane + col_hi + 32 * c, hi);
+        tmem_st32(tlane + col + 32 * c, v);
     }
 }
 
-// hi = tf32(x) in place and, with SPLIT, lo = tf32(x - hi) BLK_BYTES further, over a tile
-// (NT threads).
-template <bool SPLIT, int NT = 128>
-__device__ __forceinline__ void split_tile(uint8_t *hi, int t) {
-    for (uint32_t i = t; i < BLK_BYTES / 16; i += NT) {
-        float4 *ph = reinterpret_cast<float4 *>(hi) + i;
-        const float4 x = *ph;
-        float4 hv;
-        hv.x = __uint_as_float(tf32_rna(x.x));
-        hv.y = __uint_as_float(tf32_rna(x.y));
-        hv.z = __uint_as_float(tf32_rna(x.z));
-        hv.w = __uint_as_float(tf32_rna(x.w));
-        *ph = hv;
-        if (SPLIT) {
-            float4 lv;
-            lv.x = __uint_as_float(tf32_rna(x.x - hv.x));
-            lv.y = __uint_as_float(tf32_rna(x.y - hv.y));
-            lv.z = __uint_as_float(tf32_rna(x.z - hv.z));
-            lv.w = __uint_as_float(tf32_rna(x.w - hv.w));
-            *(reinterpret_cast<float4 *>(hi + BLK_BYTES) + i) = lv;
-        }
+// A bounded mbarrier wait whose outcome every lane of the warp shares, so that the
+// warp-collective tcgen05.ld / st and shuffles after it run converged.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err) {
+    return __all_sync(FULL, mbar_wait(bar, parity, abort, err));
+}
+
+// Adds 16 TMEM columns of this lane into acc[0..15].
+__device__ __forceinline__ void fold16(uint32_t taddr, float *acc) {
+    uint32_t r[16];
+    tmem_ld16(taddr, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int x = 0; x < 16; x++) acc[x] += __uint_as_float(r[x]);
+}
+
+// Writes n (multiple of 4) floats of acc * mul to a row with element stride `inner`.
+template <int N>
+__device__ __forceinline__ void store_row(float *dst, int64_t inner, const float *acc, float mul) {
+    if (inner == 1 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#pragma unroll
+        for (int c = 0; c < N; c += 4)
+            *reinterpret_cast<float4 *>(dst + c) =
+                make_float4(acc[c] * mul, acc[c + 1] * mul, acc[c + 2] * mul, acc[c + 3] * mul);
+    } else {
+#pragma unroll
+        for (int c = 0; c < N; c++) dst[c * inner] = acc[c] * mul;
     }
 }
 
 struct TcBwdArgs {
     AttnProblem p;
     AttnGrads g;
+    const float *lse2;  // (B*H, L) lse * log2(e), written by the pre-pass
     float scale_log2;
     int *err;
 };
 
+// ================================================================= pre-pass ==========
+struct PrepArgs {
+    AttnProblem p;
+    AttnGrads g;
+    float *qhl, *dohl, *khl, *vhl;  // [S2][B][heads][rows][64] contiguous: hi, then lo
+    float *lse2;                    // [B*H][L]
+    int split;
+    int vec;  // every input row is 16-byte aligned with unit inner stride
+};
+
+__device__ __forceinline__ float4 load4(const float *row, int64_t inner, int j, int vec) {
+    if (vec) return *reinterpret_cast<const float4 *>(row + 4 * j);
+    return make_float4(row[(4 * j) * inner], row[(4 * j + 1) * inner], row[(4 * j + 2) * inner],
+                       row[(4 * j + 3) * inner]);
+}
+
+__device__ __forceinline__ void split_store(float *hl, int64_t at, int64_t lo_off, float4 x, int split) {
+    float4 h;
+    h.x = __uint_as_float(tf32_rna(x.x));
+    h.y = __uint_as_float(tf32_rna(x.y));
+    h.z = __uint_as_float(tf32_rna(x.z));
+    h.w = __uint_as_float(tf32_rna(x.w));
+    *reinterpret_cast<float4 *>(hl + at) = h;
+    if (split) {
+        float4 l;
+        l.x = __uint_as_float(tf32_rna(x.x - h.x));
+        l.y = __uint_as_float(tf32_rna(x.y - h.y));
+        l.z = __uint_as_float(tf32_rna(x.z - h.z));
+        l.w = __uint_as_float(tf32_rna(x.w - h.w));
+        *reinterpret_cast<float4 *>(hl + lo_off + at) = l;
+    }
+}
+
+// 16 lanes per row of 64: rows of (q, grad_out, out) first, then rows of (k, v).
+__global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
+    const AttnProblem &p = a.p;
+    const int64_t rows_a = p.B * p.H * p.L, rows_b = p.B * p.Hkv * p.S;
+    const int64_t r = (int64_t)blockIdx.x * 16 + threadIdx.x / 16;
+    const int j = threadIdx.x & 15;
+    const unsigned half_mask = 0xFFFFu << (threadIdx.x & 16);
+    if (r < rows_a) {
+        const int64_t l = r % p.L, bh = r / p.L, h = bh % p.H, b = bh / p.H;
+        const float4 q4 = load4(p.q + b * p.qs[0] + h * p.qs[1] + l * p.qs[2], p.qs[3], j, a.vec);
+        const float4 d4 = load4(a.g.dout + b * a.g.dos[0] + h * a.g.dos[1] + l * a.g.dos[2], a.g.dos[3], j, a.vec);
+        const float4 o4 = load4(p.out + b * p.os[0] + h * p.os[1] + l * p.os[2], p.os[3], j, a.vec);
+        float s = fmaf(d4.w, o4.w, fmaf(d4.z, o4.z, fmaf(d4.y, o4.y, d4.x * o4.x)));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(half_mask, s, o);
+        split_store(a.qhl, r * D + 4 * j, rows_a * D, q4, a.split);
+        split_store(a.dohl, r * D + 4 * j, rows_a * D, d4, a.split);
+        if (j == 0) {
+            a.g.delta[r] = s;
+            a.lse2[r] = p.lse[b * p.ls[0] + h * p.ls[1] + l * p.ls[2]] * LOG2E;
+        }
+    } else if (r < rows_a + rows_b) {
+        const int64_t rr = r - rows_a;
+        const int64_t sidx = rr % p.S, bh = rr / p.S, hk = bh % p.Hkv, b = bh / p.Hkv;
+        const float4 k4 = load4(p.k + b * p.ks[0] + hk * p.ks[1] + sidx * p.ks[2], p.ks[3], j, a.vec);
+        const float4 v4 = load4(p.v + b * p.vs[0] + hk * p.vs[1] + sidx * p.vs[2], p.vs[3], j, a.vec);
+        split_store(a.khl, rr * D + 4 * j, rows_b * D, k4, a.split);
+        split_store(a.vhl, rr * D + 4 * j, rows_b * D, v4, a.split);
+    }
+}
+
 // ==================================================================== dK / dV ========
 namespace kv {
 constexpr int NST = 2;
-// 16 warps (4 per SM sub-partition, so up to 128 registers per thread).
-constexpr int THREADS = 512;
-constexpr int W_DVF = 4, W_DKF = 8, W_CVT = 12, N_CVT = 64, W_PROD = 14, W_MMA = 15;
-// stage: Q_K hi, lo | Q_MN hi, lo | dO_K hi, lo | dO_MN hi, lo (8 KB each) | lse2[32], delta[32]
-constexpr uint32_t ST_QK = 0, ST_QMN = 2 * BLK_BYTES, ST_DOK = 4 * BLK_BYTES, ST_DOMN = 6 * BLK_BYTES,
-                   ST_ROWS = 8 * BLK_BYTES;
-constexpr uint32_t STAGE_BYTES = 8 * BLK_BYTES + 1024;  // 1024-byte aligned stages
+// stage: Q_K hi, lo | Q_MN hi, lo | dO_K hi, lo | dO_MN hi, lo (8 KB each)
+constexpr uint32_t ST_QK = 0, ST_QMN = 2 * BLK_BYTES, ST_DOK = 4 * BLK_BYTES, ST_DOMN = 6 * BLK_BYTES;
+constexpr uint32_t STAGE_BYTES = 8 * BLK_BYTES;  // 64 KB, 1024-byte aligned
 constexpr uint32_t OFF_KLO = NST * STAGE_BYTES, OFF_VLO = OFF_KLO + RES_BYTES;
 constexpr uint32_t OFF_BAR = OFF_VLO + RES_BYTES;
 // G_DONE[b]: the gradient MMAs that read buffer b finished (guards its reuse); CHAIN_DONE:
 // the last gradient MMAs of an accumulation chain finished (the fold may read); BLK_FREE: the
 // fold has read the block accumulators (the next chain may overwrite them).
-enum { KV_FULL, KV_READY, ST_FULL, ST_READY = ST_FULL + NST, ST_EMPTY = ST_READY + NST,
-       S_FULL = ST_EMPTY + NST, P_FULL = S_FULL + 2, G_DONE = P_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE,
-       DRAIN, NBAR };
+enum { KV_FULL, KV_READY, ST_FULL, ST_EMPTY = ST_FULL + NST, S_FULL = ST_EMPTY + NST, P_FULL = S_FULL + 2,
+       G_DONE = P_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE, DRAIN, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
 // TMEM: K hi | V hi | 2 x (S^T / P^T hi, P^T lo, dP^T / dS^T hi, dS^T lo) | dV_blk | dK_blk
@@ -185,12 +247,15 @@ __device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 128;
 __device__ __forceinline__ constexpr uint32_t c_plo(int b) { return 160 + b * 128; }
 __device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 192 + b * 128; }
 __device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 224 + b * 128; }
-static_assert(2 * RES_BYTES <= STAGE_BYTES, "the raw K / V tiles are staged in stage 0");
+static_assert(2 * RES_BYTES <= STAGE_BYTES, "K / V hi are staged in stage 0");
 static_assert(SMEM <= 232448, "smem");
 }  // namespace kv
 
+// tm_k / tm_v: (64, S, Hkv, S2*B) over the hi / lo copies (lo at batch B + b), box 128 rows;
+// tm_q* / tm_do*: (64, L, H, S2*B), box 32 rows, K-major (128-byte swizzle) or MN-major
+// (32-byte-atom swizzle).
 template <bool SPLIT>
-__global__ void __maxnreg__(128)
+__global__ void __maxnreg__(168)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_qmn,
                             const __grid_constant__ CUtensorMap tm_dok, const __grid_constant__ CUtensorMap tm_domn,
@@ -203,6 +268,7 @@ __global__ void __maxnreg__(128)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
     const int64_t hk = blockIdx.y, b = blockIdx.z, k0 = (int64_t)blockIdx.x * TILE;
+    const int lo_b = (int)(p.B + b);  // batch coordinate of the lo copies
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
     const int64_t r_begin = p.causal ? min(k0, p.L) : 0;
     const int qb_first = (int)(r_begin / BLK);
@@ -219,20 +285,18 @@ __global__ void __maxnreg__(128)
 
     if (threadIdx.x == 0) {
         mbar_init(bar(KV_FULL), 1);
-        mbar_init(bar(KV_READY), 128);
+        mbar_init(bar(KV_READY), 256);
         for (int s = 0; s < NST; s++) {
             mbar_init(bar(ST_FULL + s), 1);
-            mbar_init(bar(ST_READY + s), N_CVT);
             mbar_init(bar(ST_EMPTY + s), 1);
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(bar(S_FULL + s), 1);
-            mbar_init(bar(P_FULL + s), 128);
+            mbar_init(bar(P_FULL + s), 256);
+            mbar_init(bar(G_DONE + s), 1);
         }
-        mbar_init(bar(G_DONE), 1);
-        mbar_init(bar(G_DONE + 1), 1);
         mbar_init(bar(CHAIN_DONE), 1);
-        mbar_init(bar(BLK_FREE), 256);  // both fold groups
+        mbar_init(bar(BLK_FREE), 256);
         mbar_init(bar(DRAIN), 1);
         *abort = 0;
         fence_mbar_init();
@@ -250,11 +314,15 @@ __global__ void __maxnreg__(128)
         // ---------------------------------------------------------------- producer ----
         if (lane == 0) {
             int issued = -1;
-            // K and V of the CTA, raw, into stage 0 (K at 0, V at RES_BYTES).
-            mbar_expect_tx(bar(KV_FULL), 2 * RES_BYTES);
+            // K and V hi into stage 0 (K at 0, V at RES_BYTES); lo straight to their slots.
+            mbar_expect_tx(bar(KV_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
             for (int c = 0; c < CHUNKS; c++) {
                 tma_load_4d(&tm_k, sb + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 tma_load_4d(&tm_v, sb + RES_BYTES + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                if (SPLIT) {
+                    tma_load_4d(&tm_k, sb + OFF_KLO + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                    tma_load_4d(&tm_v, sb + OFF_VLO + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                }
             }
             bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
             for (int i = 0; ok && i < nblk; i++) {
@@ -262,17 +330,24 @@ __global__ void __maxnreg__(128)
                 if (i >= NST && !mbar_wait(bar(ST_EMPTY + s), ((i / NST) - 1) & 1, abort, err)) break;
                 int64_t h, q0;
                 blk_coords(i, h, q0);
-                const uint32_t st = sb + s * STAGE_BYTES;
-                mbar_expect_tx(bar(ST_FULL + s), 4 * BLK_BYTES);
+                const uint32_t st = sb + s * STAGE_BYTES, fb = bar(ST_FULL + s);
+                mbar_expect_tx(fb, (SPLIT ? 8 : 4) * BLK_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
-                    tma_load_4d(&tm_qk, st + ST_QK + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_qmn, st + ST_QMN + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_dok, st + ST_DOK + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_domn, st + ST_DOMN + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, (int)q0, (int)h, (int)b);
+                    const uint32_t o = c * BLK_CHUNK;
+                    tma_load_4d(&tm_qk, st + ST_QK + o, fb, 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_qmn, st + ST_QMN + o, fb, 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_dok, st + ST_DOK + o, fb, 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_domn, st + ST_DOMN + o, fb, 32 * c, (int)q0, (int)h, (int)b);
+                    if (SPLIT) {
+                        tma_load_4d(&tm_qk, st + ST_QK + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
+                        tma_load_4d(&tm_qmn, st + ST_QMN + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
+                        tma_load_4d(&tm_dok, st + ST_DOK + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
+                        tma_load_4d(&tm_domn, st + ST_DOMN + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
+                    }
                 }
                 issued = i;
             }
-            if (*abort) {
+            if (*abort) {  // let the copies in flight land before the CTA exits
                 volatile int never = 0;
                 mbar_wait(bar(KV_FULL), 0, &never, nullptr);
                 for (int i = max(0, issued - NST + 1); i <= issued; i++)
@@ -304,7 +379,7 @@ __global__ void __maxnreg__(128)
             for (int i = 0; ok && i < nblk; i++) {
                 const int s = i % NST, bb = i & 1;
                 const uint32_t st = sb + s * STAGE_BYTES;
-                if (!mbar_wait(bar(ST_READY + s), (i / NST) & 1, abort, err)) break;
+                if (!mbar_wait(bar(ST_FULL + s), (i / NST) & 1, abort, err)) break;
                 // Buffer bb holds P^T / dS^T of block i-2 until its gradient MMAs finish.
                 if (i >= 2 && !mbar_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
                 tc_fence_after();
@@ -321,132 +396,107 @@ __global__ void __maxnreg__(128)
             volatile int never = 0;
             mbar_wait(bar(DRAIN), 0, &never, nullptr);
         }
-    } else if (warp >= W_CVT) {
-        // ------------------------------------------------------------- converters -----
-        const int ct = threadIdx.x - 32 * W_CVT;
-        if (mbar_wait(bar(KV_READY), 0, abort, err)) {  // stage 0 is free of the raw K / V
-            for (int i = 0; i < nblk; i++) {
-                const int s = i % NST;
-                if (!mbar_wait(bar(ST_FULL + s), (i / NST) & 1, abort, err)) break;
-                uint8_t *st = sg + s * STAGE_BYTES;
-                split_tile<SPLIT, N_CVT>(st + ST_QK, ct);
-                split_tile<SPLIT, N_CVT>(st + ST_QMN, ct);
-                split_tile<SPLIT, N_CVT>(st + ST_DOK, ct);
-                split_tile<SPLIT, N_CVT>(st + ST_DOMN, ct);
-                if (ct < BLK) {  // this block's lse (in base 2) and delta, one row per thread
-                    int64_t h, q0;
-                    blk_coords(i, h, q0);
-                    const int64_t q = q0 + ct;
-                    float *rows = reinterpret_cast<float *>(st + ST_ROWS);
-                    rows[ct] = q < p.L ? p.lse[b * p.ls[0] + h * p.ls[1] + q * p.ls[2]] * LOG2E : 0.0f;
-                    rows[BLK + ct] = q < p.L ? a.g.delta[(b * p.H + h) * p.L + q] : 0.0f;
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(bar(ST_READY + s));
-            }
-        }
-    } else if (warp >= W_DVF) {
-        // ------------------------------------------ fold: fp32 dV (4-7) and dK (8-11) --
-        const bool is_dk = warp >= W_DKF;
-        const int row = threadIdx.x - 32 * (is_dk ? W_DKF : W_DVF);  // key row (lane quadrant warp & 3)
+    } else {
+        // ---------------------------------- P^T and dS^T, then the fp32 dV / dK folds ----
+        const int quad = warp & 3, half = warp >> 2;  // lane quadrant; query-column half / dV or dK
+        const int row = quad * 32 + lane;             // key row of this CTA
         const int64_t key = k0 + row;
-        const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const uint32_t col = is_dk ? C_DK : C_DV;
+        const bool key_ok = key < p.S;
+        const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+        const int cb = half * 16;  // this thread's query columns of a block
         float acc[D];
 #pragma unroll
         for (int x = 0; x < D; x++) acc[x] = 0.0f;
-        bool ok = true;
+        bool ok = warp_wait(bar(KV_FULL), 0, abort, err);
+        if (ok) {  // K (half 0) or V (half 1) hi rows into TMEM
+            row_to_tmem(sg + half * RES_BYTES, row, tl, half ? C_VHI : C_KHI);
+            tmem_wait_st();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(bar(KV_READY));
+        }
         const int nchain = (nblk + FOLD - 1) / FOLD;
-        for (int ch = 0; ch < nchain; ch++) {
-            if (!mbar_wait(bar(CHAIN_DONE), ch & 1, abort, err)) {
+        int folded = 0;
+        auto fold = [&]() -> bool {
+            if (!warp_wait(bar(CHAIN_DONE), folded & 1, abort, err)) return false;
+            tc_fence_after();
+            const uint32_t col = half ? C_DK : C_DV;
+#pragma unroll
+            for (int c = 0; c < D / 16; c++) fold16(tl + col + 16 * c, acc + 16 * c);
+            tc_fence_before();
+            mbar_arrive(bar(BLK_FREE));
+            folded++;
+            return true;
+        };
+        // Lanes 0-15 hold this half's 16 lse values (base 2) of block i, lanes 16-31 its deltas.
+        auto rowvals = [&](int i) -> float {
+            int64_t h, q0;
+            blk_coords(i, h, q0);
+            const int64_t q = q0 + cb + (lane & 15);
+            if (q >= p.L) return 0.0f;
+            const int64_t idx = (b * p.H + h) * p.L + q;
+            return lane < 16 ? a.lse2[idx] : a.g.delta[idx];
+        };
+        float cur = (ok && nblk > 0) ? rowvals(0) : 0.0f;
+        for (int i = 0; ok && i < nblk; i++) {
+            const int bb = i & 1;
+            int64_t h, q0;
+            blk_coords(i, h, q0);
+            const float nxt = i + 1 < nblk ? rowvals(i + 1) : 0.0f;
+            if (!warp_wait(bar(S_FULL + bb), (i >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < D / 16; c++) {
-                uint32_t r[16];
-                tmem_ld16(tl + col + 16 * c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int x = 0; x < 16; x++) acc[16 * c + x] += __uint_as_float(r[x]);
-            }
-            tc_fence_before();
-            mbar_arrive(bar(BLK_FREE));
-        }
-        const bool aborted = __any_sync(0xffffffffu, *abort != 0);
-        if (ok && !aborted && key < p.S) {
-            if (is_dk) {
-                float *dkr = a.g.dk + b * a.g.dks[0] + hk * a.g.dks[1] + key * a.g.dks[2];
-#pragma unroll
-                for (int c = 0; c < D; c++) dkr[c * a.g.dks[3]] = acc[c] * p.scale;
-            } else {
-                float *dvr = a.g.dv + b * a.g.dvs[0] + hk * a.g.dvs[1] + key * a.g.dvs[2];
-#pragma unroll
-                for (int c = 0; c < D; c++) dvr[c * a.g.dvs[3]] = acc[c];
-            }
-        }
-    } else {
-        // ---------------------------------------------------------- P^T and dS^T ------
-        const int row = threadIdx.x;  // key row of this CTA
-        const int64_t key = k0 + row;
-        const bool key_ok = key < p.S;
-        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-        // First, this CTA's K and V rows into TMEM (hi) and shared memory (lo).
-        if (!mbar_wait(bar(KV_FULL), 0, abort, err)) goto done;
-        row_split<SPLIT>(sg, sg + OFF_KLO, row, tl, C_KHI);
-        row_split<SPLIT>(sg + RES_BYTES, sg + OFF_VLO, row, tl, C_VHI);
-        tmem_wait_st();
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(bar(KV_READY));
-        for (int i = 0; i < nblk; i++) {
-            const int s = i % NST, bb = i & 1;
-            int64_t h, q0;
-            blk_coords(i, h, q0);
-            if (!mbar_wait(bar(S_FULL + bb), (i >> 1) & 1, abort, err)) break;
-            if (!mbar_wait(bar(ST_READY + s), (i / NST) & 1, abort, err)) break;  // lse / delta visible
-            tc_fence_after();
-            const float4 *rows = reinterpret_cast<const float4 *>(sg + s * STAGE_BYTES + ST_ROWS);
             const bool edge = !key_ok || q0 + BLK > p.L || (p.causal && key > q0) || p.mask_kind != MASK_NONE;
+            uint32_t sr[16], dr[16], phi[16], plo[16];
+            tmem_ld16(tl + c_s(bb) + cb, sr);
+            tmem_ld16(tl + c_dp(bb) + cb, dr);
+            tmem_wait_ld();
 #pragma unroll
-            for (int hf = 0; hf < 2; hf++) {  // 16 query columns at a time
-                uint32_t sr[16], dr[16], phi[16], plo[16];
-                tmem_ld16(tl + c_s(bb) + 16 * hf, sr);
-                tmem_ld16(tl + c_dp(bb) + 16 * hf, dr);
-                const float *lse2 = reinterpret_cast<const float *>(rows) + 16 * hf;
-                const float *del = reinterpret_cast<const float *>(rows) + BLK + 16 * hf;
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    float x = __uint_as_float(sr[c]) * a.scale_log2;
-                    bool valid = true;
-                    if (edge) {
-                        const int64_t q = q0 + 16 * hf + c;
-                        valid = key_ok && q < p.L && !(p.causal && key > q);
-                        if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
-                    }
-                    const float pc = valid ? ex2_approx(x - lse2[c]) : 0.0f;
-                    const float ds = pc * (__uint_as_float(dr[c]) - del[c]);
-                    phi[c] = tf32_rna(pc);
-                    sr[c] = tf32_rna(ds);
-                    if (SPLIT) {
-                        plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
-                        dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
-                    }
+            for (int c = 0; c < 16; c++) {
+                const float lse2 = __shfl_sync(FULL, cur, c), del = __shfl_sync(FULL, cur, 16 + c);
+                float x = __uint_as_float(sr[c]) * a.scale_log2;
+                bool valid = true;
+                if (edge) {
+                    const int64_t q = q0 + cb + c;
+                    valid = key_ok && q < p.L && !(p.causal && key > q);
+                    if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
                 }
-                tmem_st16(tl + c_s(bb) + 16 * hf, phi);
-                tmem_st16(tl + c_dp(bb) + 16 * hf, sr);
+                const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
+                const float ds = pc * (__uint_as_float(dr[c]) - del);
+                phi[c] = tf32_rna(pc);
+                sr[c] = tf32_rna(ds);
                 if (SPLIT) {
-                    tmem_st16(tl + c_plo(bb) + 16 * hf, plo);
-                    tmem_st16(tl + c_dslo(bb) + 16 * hf, dr);
+                    plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
+                    dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
                 }
+            }
+            tmem_st16(tl + c_s(bb) + cb, phi);
+            tmem_st16(tl + c_dp(bb) + cb, sr);
+            if (SPLIT) {
+                tmem_st16(tl + c_plo(bb) + cb, plo);
+                tmem_st16(tl + c_dslo(bb) + cb, dr);
             }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(P_FULL + bb));
+            cur = nxt;
+            // The chain that ended with block i-1 completes while this block was in softmax.
+            if (i >= 1 && ((i - 1) % FOLD) == FOLD - 1 && !fold()) ok = false;
         }
-    done:;
+        while (ok && folded < nchain)
+            if (!fold()) ok = false;
+        const bool aborted = __any_sync(FULL, *abort != 0);
+        if (ok && !aborted && key_ok) {
+            if (half) {
+                float *dkr = a.g.dk + b * a.g.dks[0] + hk * a.g.dks[1] + key * a.g.dks[2];
+                store_row<D>(dkr, a.g.dks[3], acc, p.scale);
+            } else {
+                float *dvr = a.g.dv + b * a.g.dvs[0] + hk * a.g.dvs[1] + key * a.g.dvs[2];
+                store_row<D>(dvr, a.g.dvs[3], acc, 1.0f);
+            }
+        }
     }
 
     tc_fence_before();
@@ -460,15 +510,13 @@ __global__ void __maxnreg__(128)
 // ========================================================================= dQ ========
 namespace qq {
 constexpr int NST = 3;
-constexpr int THREADS = 448;
-constexpr int W_FOLD = 4, W_PROD = 8, W_MMA = 9, W_CVT = 10;
 // stage: K_K hi, lo | K_MN hi, lo | V_K hi, lo  (8 KB each)
 constexpr uint32_t ST_KK = 0, ST_KMN = 2 * BLK_BYTES, ST_VK = 4 * BLK_BYTES;
 constexpr uint32_t STAGE_BYTES = 6 * BLK_BYTES;  // 48 KB
 constexpr uint32_t OFF_QLO = NST * STAGE_BYTES, OFF_DOLO = OFF_QLO + RES_BYTES;
 constexpr uint32_t OFF_BAR = OFF_DOLO + RES_BYTES;
-enum { QD_FULL, QD_READY, ST_FULL, ST_READY = ST_FULL + NST, ST_EMPTY = ST_READY + NST, S_FULL = ST_EMPTY + NST,
-       DS_FULL = S_FULL + 2, G_DONE = DS_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE, DRAIN, NBAR };
+enum { QD_FULL, QD_READY, ST_FULL, ST_EMPTY = ST_FULL + NST, S_FULL = ST_EMPTY + NST, DS_FULL = S_FULL + 2,
+       G_DONE = DS_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE, DRAIN, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
 // TMEM: Q hi | dO hi | 2 x (S, dP / dS hi, dS lo) | dQ_blk
@@ -476,12 +524,14 @@ constexpr uint32_t C_QHI = 0, C_DOHI = 64, C_DQB = 320, TCOLS = 512;
 __device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 96; }
 __device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 160 + b * 96; }
 __device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 192 + b * 96; }
-static_assert(2 * RES_BYTES <= 2 * STAGE_BYTES, "the raw Q / dO tiles are staged in stages 0-1");
+static_assert(2 * RES_BYTES <= 2 * STAGE_BYTES, "Q / dO hi are staged in stages 0-1");
 static_assert(SMEM <= 232448, "smem");
 }  // namespace qq
 
+// tm_q / tm_do: (64, L, H, S2*B), box 128 rows; tm_kk / tm_kmn / tm_vk: (64, S, Hkv, S2*B),
+// box 32 rows.
 template <bool SPLIT>
-__global__ void __maxnreg__(128)
+__global__ void __maxnreg__(168)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_kk, const __grid_constant__ CUtensorMap tm_kmn,
                           const __grid_constant__ CUtensorMap tm_vk, const TcBwdArgs a) {
@@ -493,6 +543,7 @@ __global__ void __maxnreg__(128)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
     const int64_t h = blockIdx.y, b = blockIdx.z, hk = h / p.group;
+    const int lo_b = (int)(p.B + b);
     const int64_t q0 = (int64_t)blockIdx.x * TILE;
     const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
     const int nblk = (int)((kv_end + BLK - 1) / BLK);
@@ -503,20 +554,18 @@ __global__ void __maxnreg__(128)
 
     if (threadIdx.x == 0) {
         mbar_init(bar(QD_FULL), 1);
-        mbar_init(bar(QD_READY), 128);
+        mbar_init(bar(QD_READY), 256);
         for (int s = 0; s < NST; s++) {
             mbar_init(bar(ST_FULL + s), 1);
-            mbar_init(bar(ST_READY + s), 128);
             mbar_init(bar(ST_EMPTY + s), 1);
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(bar(S_FULL + s), 1);
-            mbar_init(bar(DS_FULL + s), 128);
+            mbar_init(bar(DS_FULL + s), 256);
+            mbar_init(bar(G_DONE + s), 1);
         }
-        mbar_init(bar(G_DONE), 1);
-        mbar_init(bar(G_DONE + 1), 1);
         mbar_init(bar(CHAIN_DONE), 1);
-        mbar_init(bar(BLK_FREE), 128);
+        mbar_init(bar(BLK_FREE), 256);
         mbar_init(bar(DRAIN), 1);
         *abort = 0;
         fence_mbar_init();
@@ -533,21 +582,31 @@ __global__ void __maxnreg__(128)
     if (warp == W_PROD) {
         if (lane == 0) {
             int issued = -1;
-            mbar_expect_tx(bar(QD_FULL), 2 * RES_BYTES);
+            mbar_expect_tx(bar(QD_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
             for (int c = 0; c < CHUNKS; c++) {
                 tma_load_4d(&tm_q, sb + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 tma_load_4d(&tm_do, sb + RES_BYTES + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                if (SPLIT) {
+                    tma_load_4d(&tm_q, sb + OFF_QLO + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                    tma_load_4d(&tm_do, sb + OFF_DOLO + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                }
             }
             bool ok = mbar_wait(bar(QD_READY), 0, abort, err);
             for (int j = 0; ok && j < nblk; j++) {
                 const int s = j % NST;
                 if (j >= NST && !mbar_wait(bar(ST_EMPTY + s), ((j / NST) - 1) & 1, abort, err)) break;
-                const uint32_t st = sb + s * STAGE_BYTES;
-                mbar_expect_tx(bar(ST_FULL + s), 3 * BLK_BYTES);
+                const uint32_t st = sb + s * STAGE_BYTES, fb = bar(ST_FULL + s);
+                mbar_expect_tx(fb, (SPLIT ? 6 : 3) * BLK_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
-                    tma_load_4d(&tm_kk, st + ST_KK + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, j * BLK, (int)hk, (int)b);
-                    tma_load_4d(&tm_kmn, st + ST_KMN + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, j * BLK, (int)hk, (int)b);
-                    tma_load_4d(&tm_vk, st + ST_VK + c * BLK_CHUNK, bar(ST_FULL + s), 32 * c, j * BLK, (int)hk, (int)b);
+                    const uint32_t o = c * BLK_CHUNK;
+                    tma_load_4d(&tm_kk, st + ST_KK + o, fb, 32 * c, j * BLK, (int)hk, (int)b);
+                    tma_load_4d(&tm_kmn, st + ST_KMN + o, fb, 32 * c, j * BLK, (int)hk, (int)b);
+                    tma_load_4d(&tm_vk, st + ST_VK + o, fb, 32 * c, j * BLK, (int)hk, (int)b);
+                    if (SPLIT) {
+                        tma_load_4d(&tm_kk, st + ST_KK + BLK_BYTES + o, fb, 32 * c, j * BLK, (int)hk, lo_b);
+                        tma_load_4d(&tm_kmn, st + ST_KMN + BLK_BYTES + o, fb, 32 * c, j * BLK, (int)hk, lo_b);
+                        tma_load_4d(&tm_vk, st + ST_VK + BLK_BYTES + o, fb, 32 * c, j * BLK, (int)hk, lo_b);
+                    }
                 }
                 issued = j;
             }
@@ -580,7 +639,7 @@ __global__ void __maxnreg__(128)
             for (int j = 0; ok && j < nblk; j++) {
                 const int s = j % NST, bb = j & 1;
                 const uint32_t st = sb + s * STAGE_BYTES;
-                if (!mbar_wait(bar(ST_READY + s), (j / NST) & 1, abort, err)) break;
+                if (!mbar_wait(bar(ST_FULL + s), (j / NST) & 1, abort, err)) break;
                 // Buffer bb holds dS of block j-2 until its gradient MMAs finish.
                 if (j >= 2 && !mbar_wait(bar(G_DONE + bb), ((j - 2) >> 1) & 1, abort, err)) break;
                 tc_fence_after();
@@ -597,102 +656,80 @@ __global__ void __maxnreg__(128)
             volatile int never = 0;
             mbar_wait(bar(DRAIN), 0, &never, nullptr);
         }
-    } else if (warp >= W_CVT) {
-        const int ct = threadIdx.x - 32 * W_CVT;
-        const int quad = warp & 3;
+    } else {
+        // ----------------------------------------------------- dS, then the fp32 dQ fold --
+        const int quad = warp & 3, half = warp >> 2;
         const int row = quad * 32 + lane;
+        const int64_t q = q0 + row;
+        const bool row_ok = q < p.L;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        if (mbar_wait(bar(QD_FULL), 0, abort, err)) {
-            row_split<SPLIT>(sg, sg + OFF_QLO, row, tl, C_QHI);
-            row_split<SPLIT>(sg + RES_BYTES, sg + OFF_DOLO, row, tl, C_DOHI);
+        const int cb = half * 16;  // this thread's key columns of a block
+        float acc[D / 2];          // dQ columns [32 half, 32 half + 32)
+#pragma unroll
+        for (int x = 0; x < D / 2; x++) acc[x] = 0.0f;
+        bool ok = warp_wait(bar(QD_FULL), 0, abort, err);
+        if (ok) {  // Q (half 0) or dO (half 1) hi rows into TMEM
+            row_to_tmem(sg + half * RES_BYTES, row, tl, half ? C_DOHI : C_QHI);
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(bar(QD_READY));
-            for (int j = 0; j < nblk; j++) {
-                const int s = j % NST;
-                if (!mbar_wait(bar(ST_FULL + s), (j / NST) & 1, abort, err)) break;
-                uint8_t *st = sg + s * STAGE_BYTES;
-                split_tile<SPLIT>(st + ST_KK, ct);
-                split_tile<SPLIT>(st + ST_KMN, ct);
-                split_tile<SPLIT>(st + ST_VK, ct);
-                fence_proxy_async_smem();
-                mbar_arrive(bar(ST_READY + s));
-            }
         }
-    } else if (warp >= W_FOLD) {
-        // ------------------------------------------------------------ fold: fp32 dQ ---
-        const int row = threadIdx.x - 32 * W_FOLD;
-        const int64_t q = q0 + row;
-        const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        float dq[D];
-#pragma unroll
-        for (int x = 0; x < D; x++) dq[x] = 0.0f;
-        bool ok = true;
+        const int64_t ridx = (b * p.H + h) * p.L + q;
+        const float lse2 = row_ok ? a.lse2[ridx] : 0.0f;
+        const float del = row_ok ? a.g.delta[ridx] : 0.0f;
         const int nchain = (nblk + FOLD - 1) / FOLD;
-        for (int ch = 0; ch < nchain; ch++) {
-            if (!mbar_wait(bar(CHAIN_DONE), ch & 1, abort, err)) {
+        int folded = 0;
+        auto fold = [&]() -> bool {
+            if (!warp_wait(bar(CHAIN_DONE), folded & 1, abort, err)) return false;
+            tc_fence_after();
+            fold16(tl + C_DQB + 32 * half, acc);
+            fold16(tl + C_DQB + 32 * half + 16, acc + 16);
+            tc_fence_before();
+            mbar_arrive(bar(BLK_FREE));
+            folded++;
+            return true;
+        };
+        for (int j = 0; ok && j < nblk; j++) {
+            const int bb = j & 1;
+            const int64_t kb0 = (int64_t)j * BLK;
+            if (!warp_wait(bar(S_FULL + bb), (j >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < D / 16; c++) {
-                uint32_t r[16];
-                tmem_ld16(tl + C_DQB + 16 * c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int x = 0; x < 16; x++) dq[16 * c + x] += __uint_as_float(r[x]);
-            }
-            tc_fence_before();
-            mbar_arrive(bar(BLK_FREE));
-        }
-        const bool aborted = __any_sync(0xffffffffu, *abort != 0);
-        if (ok && !aborted && q < p.L) {
-            float *dqr = a.g.dq + b * a.g.dqs[0] + h * a.g.dqs[1] + q * a.g.dqs[2];
-#pragma unroll
-            for (int c = 0; c < D; c++) dqr[c * a.g.dqs[3]] = dq[c] * p.scale;
-        }
-    } else {
-        // ---------------------------------------------------------------------- dS ----
-        const int row = threadIdx.x;
-        const int64_t q = q0 + row;
-        const bool row_ok = q < p.L;
-        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-        const float lse2 = row_ok ? p.lse[b * p.ls[0] + h * p.ls[1] + q * p.ls[2]] * LOG2E : 0.0f;
-        const float del = row_ok ? a.g.delta[(b * p.H + h) * p.L + q] : 0.0f;
-        for (int j = 0; j < nblk; j++) {
-            const int bb = j & 1;
-            const int64_t kb0 = (int64_t)j * BLK;
-            if (!mbar_wait(bar(S_FULL + bb), (j >> 1) & 1, abort, err)) break;
-            tc_fence_after();
             const bool edge = !row_ok || kb0 + BLK > p.S || (p.causal && kb0 + BLK - 1 > q0) || p.mask_kind != MASK_NONE;
+            uint32_t sr[16], dr[16];
+            tmem_ld16(tl + c_s(bb) + cb, sr);
+            tmem_ld16(tl + c_dp(bb) + cb, dr);
+            tmem_wait_ld();
 #pragma unroll
-            for (int hf = 0; hf < 2; hf++) {  // 16 key columns at a time
-                uint32_t sr[16], dr[16];
-                tmem_ld16(tl + c_s(bb) + 16 * hf, sr);
-                tmem_ld16(tl + c_dp(bb) + 16 * hf, dr);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    float x = __uint_as_float(sr[c]) * a.scale_log2;
-                    bool valid = true;
-                    if (edge) {
-                        const int64_t key = kb0 + 16 * hf + c;
-                        valid = row_ok && key < p.S && !(p.causal && key > q);
-                        if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
-                    }
-                    const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
-                    const float ds = pc * (__uint_as_float(dr[c]) - del);
-                    sr[c] = tf32_rna(ds);
-                    if (SPLIT) dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
+            for (int c = 0; c < 16; c++) {
+                float x = __uint_as_float(sr[c]) * a.scale_log2;
+                bool valid = true;
+                if (edge) {
+                    const int64_t key = kb0 + cb + c;
+                    valid = row_ok && key < p.S && !(p.causal && key > q);
+                    if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
                 }
-                tmem_st16(tl + c_dp(bb) + 16 * hf, sr);
-                if (SPLIT) tmem_st16(tl + c_dslo(bb) + 16 * hf, dr);
+                const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
+                const float ds = pc * (__uint_as_float(dr[c]) - del);
+                sr[c] = tf32_rna(ds);
+                if (SPLIT) dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
             }
+            tmem_st16(tl + c_dp(bb) + cb, sr);
+            if (SPLIT) tmem_st16(tl + c_dslo(bb) + cb, dr);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(DS_FULL + bb));
+            if (j >= 1 && ((j - 1) % FOLD) == FOLD - 1 && !fold()) ok = false;
+        }
+        while (ok && folded < nchain)
+            if (!fold()) ok = false;
+        const bool aborted = __any_sync(FULL, *abort != 0);
+        if (ok && !aborted && row_ok) {
+            float *dqr = a.g.dq + b * a.g.dqs[0] + h * a.g.dqs[1] + q * a.g.dqs[2] + (int64_t)(32 * half) * a.g.dqs[3];
+            store_row<D / 2>(dqr, a.g.dqs[3], acc, p.scale);
         }
     }
 
@@ -704,59 +741,93 @@ __global__ void __maxnreg__(128)
     }
 }
 
+bool rows_vec(const void *ptr, const int64_t *st) {
+    return st[3] == 1 && st[0] % 4 == 0 && st[1] % 4 == 0 && st[2] % 4 == 0 &&
+           (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0;
+}
+
+struct PoolScratch {
+    void *ptr = nullptr;
+    cudaStream_t stream = nullptr;
+    ~PoolScratch() { pool_free(ptr, stream); }
+};
+
 }  // namespace
 
 bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g) {
-    if (!tc_forward_supported(p) || p.E != D) return false;
-    if (p.L >= (1ll << 31) - TILE) return false;
-    // grad_out is read through TMA as well.
-    if (g.dos[3] != 1 || !tma_stride_ok(p.L, g.dos[2]) || !tma_stride_ok(p.H, g.dos[1]) ||
-        !tma_stride_ok(p.B, g.dos[0]))
-        return false;
-    return (reinterpret_cast<uintptr_t>(g.dout) & 15u) == 0;
+    (void)g;
+    if (p.E != D || p.Ev != D) return false;
+    if (p.L >= (1ll << 31) - TILE || p.S >= (1ll << 31) - TILE) return false;
+    return 2 * p.B < (1ll << 31);
 }
 
 int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
+    const bool split = precision != DC_PREC_TF32;
+    const int64_t S2 = split ? 2 : 1;
+    const int64_t rows_a = p.B * p.H * p.L, rows_b = p.B * p.Hkv * p.S;
+    const size_t bytes = sizeof(float) * (size_t)(S2 * 2 * (rows_a + rows_b) * D + rows_a);
+    PoolScratch ws;
+    ws.stream = stream;
+    int st = pool_alloc(&ws.ptr, bytes, stream);
+    if (st) return st;
+    PrepArgs pa;
+    pa.p = p;
+    pa.g = g;
+    pa.qhl = static_cast<float *>(ws.ptr);
+    pa.dohl = pa.qhl + S2 * rows_a * D;
+    pa.khl = pa.dohl + S2 * rows_a * D;
+    pa.vhl = pa.khl + S2 * rows_b * D;
+    pa.lse2 = pa.vhl + S2 * rows_b * D;
+    pa.split = split ? 1 : 0;
+    pa.vec = rows_vec(p.q, p.qs) && rows_vec(p.k, p.ks) && rows_vec(p.v, p.vs) && rows_vec(g.dout, g.dos) &&
+             rows_vec(p.out, p.os);
+    if (rows_a + rows_b > 0) {
+        KernelTrace tr("bwd_prep", stream);
+        bwd_prep_kernel<<<(unsigned)((rows_a + rows_b + 15) / 16), 256, 0, stream>>>(pa);
+        if ((st = check_launch("bwd_prep"))) return st;
+    }
+
     TcBwdArgs a;
     a.p = p;
     a.g = g;
+    a.lse2 = pa.lse2;
     a.scale_log2 = p.scale * LOG2E;
     a.err = device_error_word();
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
-    const bool split = precision != DC_PREC_TF32;
-    const int64_t *dos = g.dos;  // grad_out shares q's shape but has its own strides
-    int st = DC_OK;
+    // Strides (batch, head, row) of the contiguous hi / lo copies.
+    const int64_t qst[3] = {p.H * p.L * D, p.L * D, D}, kst[3] = {p.Hkv * p.S * D, p.S * D, D};
+    const int64_t nb = S2 * p.B;
     if (p.S > 0) {
         CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
-        st = make_tmap(&tk, p.k, D, p.S, p.Hkv, p.B, p.ks, TILE);
-        if (!st) st = make_tmap(&tv, p.v, D, p.S, p.Hkv, p.B, p.vs, TILE);
-        if (!st) st = make_tmap(&tqk, p.q, D, p.L, p.H, p.B, p.qs, BLK);
-        if (!st) st = make_tmap(&tqmn, p.q, D, p.L, p.H, p.B, p.qs, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-        if (!st) st = make_tmap(&tdok, g.dout, D, p.L, p.H, p.B, dos, BLK);
-        if (!st) st = make_tmap(&tdomn, g.dout, D, p.L, p.H, p.B, dos, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        st = make_tmap(&tk, pa.khl, D, p.S, p.Hkv, nb, kst, TILE);
+        if (!st) st = make_tmap(&tv, pa.vhl, D, p.S, p.Hkv, nb, kst, TILE);
+        if (!st) st = make_tmap(&tqk, pa.qhl, D, p.L, p.H, nb, qst, BLK);
+        if (!st) st = make_tmap(&tqmn, pa.qhl, D, p.L, p.H, nb, qst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        if (!st) st = make_tmap(&tdok, pa.dohl, D, p.L, p.H, nb, qst, BLK);
+        if (!st) st = make_tmap(&tdomn, pa.dohl, D, p.L, p.H, nb, qst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (st) return st;
         auto kernel = split ? attn_bwd_dkdv_tc_kernel<true> : attn_bwd_dkdv_tc_kernel<false>;
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
         dim3 grid((unsigned)((p.S + TILE - 1) / TILE), (unsigned)p.Hkv, (unsigned)p.B);
         KernelTrace tr("bwd_dkdv_tc", stream);
-        kernel<<<grid, kv::THREADS, kv::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
+        kernel<<<grid, THREADS, kv::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
         if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
     }
     if (p.L > 0) {
         CUtensorMap tq, tdo, tkk, tkmn, tvk;
-        st = make_tmap(&tq, p.q, D, p.L, p.H, p.B, p.qs, TILE);
-        if (!st) st = make_tmap(&tdo, g.dout, D, p.L, p.H, p.B, dos, TILE);
-        if (!st) st = make_tmap(&tkk, p.k, D, p.S, p.Hkv, p.B, p.ks, BLK);
-        if (!st) st = make_tmap(&tkmn, p.k, D, p.S, p.Hkv, p.B, p.ks, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-        if (!st) st = make_tmap(&tvk, p.v, D, p.S, p.Hkv, p.B, p.vs, BLK);
+        st = make_tmap(&tq, pa.qhl, D, p.L, p.H, nb, qst, TILE);
+        if (!st) st = make_tmap(&tdo, pa.dohl, D, p.L, p.H, nb, qst, TILE);
+        if (!st) st = make_tmap(&tkk, pa.khl, D, p.S, p.Hkv, nb, kst, BLK);
+        if (!st) st = make_tmap(&tkmn, pa.khl, D, p.S, p.Hkv, nb, kst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        if (!st) st = make_tmap(&tvk, pa.vhl, D, p.S, p.Hkv, nb, kst, BLK);
         if (st) return st;
         auto kernel = split ? attn_bwd_dq_tc_kernel<true> : attn_bwd_dq_tc_kernel<false>;
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
         dim3 grid((unsigned)((p.L + TILE - 1) / TILE), (unsigned)p.H, (unsigned)p.B);
         KernelTrace tr("bwd_dq_tc", stream);
-        kernel<<<grid, qq::THREADS, qq::SMEM, stream>>>(tq, tdo, tkk, tkmn, tvk, a);
+        kernel<<<grid, THREADS, qq::SMEM, stream>>>(tq, tdo, tkk, tkmn, tvk, a);
         if ((st = check_launch("attn_bwd_dq_tc"))) return st;
     }
     return DC_OK;

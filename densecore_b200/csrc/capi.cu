@@ -321,8 +321,9 @@ int dc_sdpa_bwd(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tens
                      "backward workspace")))
         return st;
     g.delta = static_cast<float *>(ws.ptr);
-    if (p.L > 0 && (st = bwd_delta(p, g, s))) return st;
+    // The tensor-core backward computes delta in its own pre-pass.
     if (precision != DC_PREC_FP32 && tc_backward_supported(p, g)) return tc_backward(p, g, precision, s);
+    if (p.L > 0 && (st = bwd_delta(p, g, s))) return st;
     return simt_backward(p, g, s);
 }
 

@@ -27,8 +27,9 @@ int decode_pick_splits(const AttnProblem &p);
 size_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Ev, int splits);
 int decode_forward(const AttnProblem &p, int splits, void *workspace, cudaStream_t stream);
 
-// tcgen05 tensor-core kernels (attn_tc.cu, attn_tc_bwd.cu): head dim 64 or 128 (backward:
-// 64), E == Ev, unit-stride rows on 16-byte boundaries.
+// tcgen05 tensor-core kernels (attn_tc.cu, attn_tc_bwd.cu). Forward: head dim 64 or 128,
+// E == Ev, unit-stride rows on 16-byte boundaries. Backward: E == Ev == 64, any strides (its
+// pre-pass copies the operands into contiguous TF32 hi / lo buffers); it also writes delta.
 bool tc_forward_supported(const AttnProblem &p);
 int tc_forward(const AttnProblem &p, int precision, cudaStream_t stream);
 bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g);
@@ -37,5 +38,10 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
 int device_error(int reset);
 // Device address of that word (passed to the kernels), or nullptr.
 int *device_error_word();
+
+// The library's stream-ordered scratch pool (pool.cu): memory for `bytes` on `stream`'s
+// order of the current device, and its release on the same stream.
+int pool_alloc(void **ptr, size_t bytes, cudaStream_t stream);
+void pool_free(void *ptr, cudaStream_t stream);
 
 }  // namespace dc
