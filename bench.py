@@ -120,7 +120,9 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms. Sampling is live before the
+    timed region starts (the first sample has arrived) and one more sample is taken after it
+    ends, so even a timed region shorter than the sampling period is bracketed by samples."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -128,26 +130,46 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
+        self.first = 0
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
+
+    def _wait_for(self, n, timeout):
+        t0 = time.time()
+        while len(self.lines) < n and time.time() - t0 < timeout and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        self._wait_for(1, 10.0)
+        self.first = max(0, len(self.lines) - 1)  # the last sample before the timed region
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self.proc is None:
+            return
+        self._wait_for(len(self.lines) + 1, 2.0)  # one sample after the timed region
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait()
+        self.reader.join(timeout=5)
+        self.lines = self.lines[self.first:]
 
     def summary(self):
         if not getattr(self, "lines", None):

@@ -15,8 +15,9 @@
 //   dkdv: a CTA owns 128 keys of one (batch, kv head). K and V are the A operands: hi in TMEM,
 //         lo in shared memory. 32-row blocks of Q and dO (hi and lo, each in the K-major
 //         128-byte swizzle and in the MN-major 32-byte-atom swizzle that tf32 requires) stream
-//         through a 2-stage ring. Per block i: S^T = K Q^T and dP^T = V dO^T into one of two
-//         TMEM buffers; eight softmax warps (two per TMEM lane quadrant, 16 query columns
+//         through two rings: the K-major tiles (3 stages) are free once the S / dP MMAs have
+//         read them, the MN-major tiles (2 stages) once the gradient MMAs have. Per block i:
+//         S^T = K Q^T and dP^T = V dO^T into one of two TMEM buffers; eight softmax warps (two per TMEM lane quadrant, 16 query columns
 //         each) turn them into P^T and dS^T (hi / lo, in place); then dV_blk += P^T dO and
 //         dK_blk += dS^T Q. Issue order S0, S1, G0, S2, G1, ... keeps the tensor core busy
 //         while the softmax warps work. The same warps add the block accumulators into fp32
@@ -29,6 +30,8 @@
 //
 // Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer (one
 // thread; it also owns TMEM). Every wait is bounded; a timeout records an error and unwinds.
+// Grids are 1-D and hand out the tiles with the most causal work first (longest-first
+// dispatch keeps the last wave short).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -228,17 +231,21 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
 
 // ==================================================================== dK / dV ========
 namespace kv {
-constexpr int NST = 2;
-// stage: Q_K hi, lo | Q_MN hi, lo | dO_K hi, lo | dO_MN hi, lo (8 KB each)
-constexpr uint32_t ST_QK = 0, ST_QMN = 2 * BLK_BYTES, ST_DOK = 4 * BLK_BYTES, ST_DOMN = 6 * BLK_BYTES;
-constexpr uint32_t STAGE_BYTES = 8 * BLK_BYTES;  // 64 KB, 1024-byte aligned
-constexpr uint32_t OFF_KLO = NST * STAGE_BYTES, OFF_VLO = OFF_KLO + RES_BYTES;
+// Two rings: the K-major tiles (read by the S / dP MMAs only) free their stage as soon as those
+// MMAs finish, so they get three stages; the MN-major tiles (read by the gradient MMAs) two.
+constexpr int NSS = 3, NSG = 2;
+// S stage: Q_K hi, lo | dO_K hi, lo; G stage: Q_MN hi, lo | dO_MN hi, lo (8 KB tiles)
+constexpr uint32_t SS_QK = 0, SS_DOK = 2 * BLK_BYTES, SG_QMN = 0, SG_DOMN = 2 * BLK_BYTES;
+constexpr uint32_t SSTAGE = 4 * BLK_BYTES, GSTAGE = 4 * BLK_BYTES;  // 32 KB, 1024-byte aligned
+constexpr uint32_t OFF_SRING = 0, OFF_GRING = NSS * SSTAGE;
+constexpr uint32_t OFF_KLO = OFF_GRING + NSG * GSTAGE, OFF_VLO = OFF_KLO + RES_BYTES;
 constexpr uint32_t OFF_BAR = OFF_VLO + RES_BYTES;
 // G_DONE[b]: the gradient MMAs that read buffer b finished (guards its reuse); CHAIN_DONE:
 // the last gradient MMAs of an accumulation chain finished (the fold may read); BLK_FREE: the
 // fold has read the block accumulators (the next chain may overwrite them).
-enum { KV_FULL, KV_READY, ST_FULL, ST_EMPTY = ST_FULL + NST, S_FULL = ST_EMPTY + NST, P_FULL = S_FULL + 2,
-       G_DONE = P_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE, DRAIN, NBAR };
+enum { KV_FULL, KV_READY, SS_FULL, SS_EMPTY = SS_FULL + NSS, SG_FULL = SS_EMPTY + NSS, SG_EMPTY = SG_FULL + NSG,
+       S_FULL = SG_EMPTY + NSG, P_FULL = S_FULL + 2, G_DONE = P_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE,
+       DRAIN, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
 // TMEM: K hi | V hi | 2 x (S^T / P^T hi, P^T lo, dP^T / dS^T hi, dS^T lo) | dV_blk | dK_blk
@@ -247,7 +254,7 @@ __device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 128;
 __device__ __forceinline__ constexpr uint32_t c_plo(int b) { return 160 + b * 128; }
 __device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 192 + b * 128; }
 __device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 224 + b * 128; }
-static_assert(2 * RES_BYTES <= STAGE_BYTES, "K / V hi are staged in stage 0");
+static_assert(2 * RES_BYTES <= 2 * SSTAGE, "K / V hi are staged in S stages 0-1");
 static_assert(SMEM <= 232448, "smem");
 }  // namespace kv
 
@@ -267,7 +274,9 @@ __global__ void __maxnreg__(168)
     uint8_t *sg = smem_raw + (sb - raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
-    const int64_t hk = blockIdx.y, b = blockIdx.z, k0 = (int64_t)blockIdx.x * TILE;
+    // Key tiles in ascending order: under causal masking tile 0 sees the most query rows.
+    const int64_t bh_n = p.B * p.Hkv, kt = blockIdx.x / bh_n, bh = blockIdx.x % bh_n;
+    const int64_t hk = bh % p.Hkv, b = bh / p.Hkv, k0 = kt * TILE;
     const int lo_b = (int)(p.B + b);  // batch coordinate of the lo copies
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
     const int64_t r_begin = p.causal ? min(k0, p.L) : 0;
@@ -286,9 +295,13 @@ __global__ void __maxnreg__(168)
     if (threadIdx.x == 0) {
         mbar_init(bar(KV_FULL), 1);
         mbar_init(bar(KV_READY), 256);
-        for (int s = 0; s < NST; s++) {
-            mbar_init(bar(ST_FULL + s), 1);
-            mbar_init(bar(ST_EMPTY + s), 1);
+        for (int s = 0; s < NSS; s++) {
+            mbar_init(bar(SS_FULL + s), 1);
+            mbar_init(bar(SS_EMPTY + s), 1);
+        }
+        for (int s = 0; s < NSG; s++) {
+            mbar_init(bar(SG_FULL + s), 1);
+            mbar_init(bar(SG_EMPTY + s), 1);
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(bar(S_FULL + s), 1);
@@ -313,8 +326,8 @@ __global__ void __maxnreg__(168)
     if (warp == W_PROD) {
         // ---------------------------------------------------------------- producer ----
         if (lane == 0) {
-            int issued = -1;
-            // K and V hi into stage 0 (K at 0, V at RES_BYTES); lo straight to their slots.
+            int issued_s = -1, issued_g = -1;
+            // K and V hi into S stages 0-1 (K at 0, V at RES_BYTES); lo straight to their slots.
             mbar_expect_tx(bar(KV_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
             for (int c = 0; c < CHUNKS; c++) {
                 tma_load_4d(&tm_k, sb + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
@@ -326,32 +339,43 @@ __global__ void __maxnreg__(168)
             }
             bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
             for (int i = 0; ok && i < nblk; i++) {
-                const int s = i % NST;
-                if (i >= NST && !mbar_wait(bar(ST_EMPTY + s), ((i / NST) - 1) & 1, abort, err)) break;
                 int64_t h, q0;
                 blk_coords(i, h, q0);
-                const uint32_t st = sb + s * STAGE_BYTES, fb = bar(ST_FULL + s);
-                mbar_expect_tx(fb, (SPLIT ? 8 : 4) * BLK_BYTES);
+                const int ss = i % NSS, sgi = i % NSG;
+                if (i >= NSS && !mbar_wait(bar(SS_EMPTY + ss), ((i / NSS) - 1) & 1, abort, err)) break;
+                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE, fs = bar(SS_FULL + ss);
+                mbar_expect_tx(fs, (SPLIT ? 4 : 2) * BLK_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
                     const uint32_t o = c * BLK_CHUNK;
-                    tma_load_4d(&tm_qk, st + ST_QK + o, fb, 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_qmn, st + ST_QMN + o, fb, 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_dok, st + ST_DOK + o, fb, 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_domn, st + ST_DOMN + o, fb, 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_qk, sst + SS_QK + o, fs, 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_dok, sst + SS_DOK + o, fs, 32 * c, (int)q0, (int)h, (int)b);
                     if (SPLIT) {
-                        tma_load_4d(&tm_qk, st + ST_QK + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
-                        tma_load_4d(&tm_qmn, st + ST_QMN + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
-                        tma_load_4d(&tm_dok, st + ST_DOK + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
-                        tma_load_4d(&tm_domn, st + ST_DOMN + BLK_BYTES + o, fb, 32 * c, (int)q0, (int)h, lo_b);
+                        tma_load_4d(&tm_qk, sst + SS_QK + BLK_BYTES + o, fs, 32 * c, (int)q0, (int)h, lo_b);
+                        tma_load_4d(&tm_dok, sst + SS_DOK + BLK_BYTES + o, fs, 32 * c, (int)q0, (int)h, lo_b);
                     }
                 }
-                issued = i;
+                issued_s = i;
+                if (i >= NSG && !mbar_wait(bar(SG_EMPTY + sgi), ((i / NSG) - 1) & 1, abort, err)) break;
+                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE, fg = bar(SG_FULL + sgi);
+                mbar_expect_tx(fg, (SPLIT ? 4 : 2) * BLK_BYTES);
+                for (int c = 0; c < CHUNKS; c++) {
+                    const uint32_t o = c * BLK_CHUNK;
+                    tma_load_4d(&tm_qmn, gst + SG_QMN + o, fg, 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_domn, gst + SG_DOMN + o, fg, 32 * c, (int)q0, (int)h, (int)b);
+                    if (SPLIT) {
+                        tma_load_4d(&tm_qmn, gst + SG_QMN + BLK_BYTES + o, fg, 32 * c, (int)q0, (int)h, lo_b);
+                        tma_load_4d(&tm_domn, gst + SG_DOMN + BLK_BYTES + o, fg, 32 * c, (int)q0, (int)h, lo_b);
+                    }
+                }
+                issued_g = i;
             }
             if (*abort) {  // let the copies in flight land before the CTA exits
                 volatile int never = 0;
                 mbar_wait(bar(KV_FULL), 0, &never, nullptr);
-                for (int i = max(0, issued - NST + 1); i <= issued; i++)
-                    mbar_wait(bar(ST_FULL + i % NST), (i / NST) & 1, &never, nullptr);
+                for (int i = max(0, issued_s - NSS + 1); i <= issued_s; i++)
+                    mbar_wait(bar(SS_FULL + i % NSS), (i / NSS) & 1, &never, nullptr);
+                for (int i = max(0, issued_g - NSG + 1); i <= issued_g; i++)
+                    mbar_wait(bar(SG_FULL + i % NSG), (i / NSG) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
@@ -359,33 +383,35 @@ __global__ void __maxnreg__(168)
         if (lane == 0) {
             const uint64_t klo = sdesc_sw128(sb + OFF_KLO, 16, 1024), vlo = sdesc_sw128(sb + OFF_VLO, 16, 1024);
             auto issue_g = [&](int i) -> bool {  // gradients of block i
-                const int s = i % NST, bb = i & 1;
-                const uint32_t st = sb + s * STAGE_BYTES;
+                const int sgi = i % NSG, bb = i & 1;
+                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
                 if (!mbar_wait(bar(P_FULL + bb), (i >> 1) & 1, abort, err)) return false;
                 const bool first = (i % FOLD) == 0;
                 if (first && i >= FOLD && !mbar_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, err)) return false;
+                if (!mbar_wait(bar(SG_FULL + sgi), (i / NSG) & 1, abort, err)) return false;
                 tc_fence_after();
-                mma_g<SPLIT>(tmem + C_DV, tmem + c_s(bb), tmem + c_plo(bb), sdesc_mn_sw128_32b(st + ST_DOMN, BLK_CHUNK, 512),
-                             !first);
+                mma_g<SPLIT>(tmem + C_DV, tmem + c_s(bb), tmem + c_plo(bb),
+                             sdesc_mn_sw128_32b(gst + SG_DOMN, BLK_CHUNK, 512), !first);
                 mma_g<SPLIT>(tmem + C_DK, tmem + c_dp(bb), tmem + c_dslo(bb),
-                             sdesc_mn_sw128_32b(st + ST_QMN, BLK_CHUNK, 512), !first);
+                             sdesc_mn_sw128_32b(gst + SG_QMN, BLK_CHUNK, 512), !first);
                 tc_commit(bar(G_DONE + bb));
                 if ((i % FOLD) == FOLD - 1 || i == nblk - 1) tc_commit(bar(CHAIN_DONE));
-                tc_commit(bar(ST_EMPTY + s));
+                tc_commit(bar(SG_EMPTY + sgi));
                 return true;
             };
             bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
             tc_fence_after();
             for (int i = 0; ok && i < nblk; i++) {
-                const int s = i % NST, bb = i & 1;
-                const uint32_t st = sb + s * STAGE_BYTES;
-                if (!mbar_wait(bar(ST_FULL + s), (i / NST) & 1, abort, err)) break;
+                const int ss = i % NSS, bb = i & 1;
+                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
+                if (!mbar_wait(bar(SS_FULL + ss), (i / NSS) & 1, abort, err)) break;
                 // Buffer bb holds P^T / dS^T of block i-2 until its gradient MMAs finish.
                 if (i >= 2 && !mbar_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_KHI, klo, sdesc_sw128(st + ST_QK, 16, 1024));
-                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_VHI, vlo, sdesc_sw128(st + ST_DOK, 16, 1024));
+                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_KHI, klo, sdesc_sw128(sst + SS_QK, 16, 1024));
+                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_VHI, vlo, sdesc_sw128(sst + SS_DOK, 16, 1024));
                 tc_commit(bar(S_FULL + bb));
+                tc_commit(bar(SS_EMPTY + ss));
                 if (i >= 1 && !issue_g(i - 1)) {
                     ok = false;
                     break;
@@ -542,9 +568,12 @@ __global__ void __maxnreg__(168)
     uint8_t *sg = smem_raw + (sb - raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
-    const int64_t h = blockIdx.y, b = blockIdx.z, hk = h / p.group;
+    // Query tiles in descending order: under causal masking the last tile sees the most keys.
+    const int64_t bh_n = p.B * p.H, ntiles = (p.L + TILE - 1) / TILE;
+    const int64_t qt = ntiles - 1 - blockIdx.x / bh_n, bh = blockIdx.x % bh_n;
+    const int64_t h = bh % p.H, b = bh / p.H, hk = h / p.group;
     const int lo_b = (int)(p.B + b);
-    const int64_t q0 = (int64_t)blockIdx.x * TILE;
+    const int64_t q0 = qt * TILE;
     const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
     const int nblk = (int)((kv_end + BLK - 1) / BLK);
     auto bar = [&](int i) { return sb + OFF_BAR + 8u * (uint32_t)i; };
@@ -758,7 +787,9 @@ bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g) {
     (void)g;
     if (p.E != D || p.Ev != D) return false;
     if (p.L >= (1ll << 31) - TILE || p.S >= (1ll << 31) - TILE) return false;
-    return 2 * p.B < (1ll << 31);
+    // 1-D grids of tiles x heads x batch.
+    const int64_t tiles = (max(p.L, p.S) + TILE - 1) / TILE;
+    return 2 * p.B < (1ll << 31) && tiles * p.H * p.B < (1ll << 31);
 }
 
 int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
@@ -809,7 +840,7 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         auto kernel = split ? attn_bwd_dkdv_tc_kernel<true> : attn_bwd_dkdv_tc_kernel<false>;
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
-        dim3 grid((unsigned)((p.S + TILE - 1) / TILE), (unsigned)p.Hkv, (unsigned)p.B);
+        const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B);
         KernelTrace tr("bwd_dkdv_tc", stream);
         kernel<<<grid, THREADS, kv::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
         if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
@@ -825,7 +856,7 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         auto kernel = split ? attn_bwd_dq_tc_kernel<true> : attn_bwd_dq_tc_kernel<false>;
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
-        dim3 grid((unsigned)((p.L + TILE - 1) / TILE), (unsigned)p.H, (unsigned)p.B);
+        const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B);
         KernelTrace tr("bwd_dq_tc", stream);
         kernel<<<grid, THREADS, qq::SMEM, stream>>>(tq, tdo, tkk, tkmn, tvk, a);
         if ((st = check_launch("attn_bwd_dq_tc"))) return st;
