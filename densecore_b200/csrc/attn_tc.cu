@@ -13,10 +13,11 @@
 //               the S MMAs read only K from shared memory); each landed K / V tile x is split
 //               in place into hi = tf32(x) and lo = tf32(x - hi) (3xTF32: a*b ~ ah*bh + ah*bl
 //               + al*bh keeps fp32-class accuracy on the TF32 tensor cores).
-//   warp 9      MMA issuer (one thread, descriptors precomputed): S_j = Q K_j^T into one of
-//               two TMEM buffers, then O_blk = P_{j-1} V_{j-1} with P read from TMEM; issue
-//               order S0, S1, PV0, S2, PV1, ... so the tensor core computes S_{j+1} while the
-//               softmax warps work on block j.
+//   warps 9, 14 MMA issuers (one thread each, descriptors precomputed): warp 9 issues
+//               S_j = Q K_j^T into one of two TMEM buffers, warp 14 O_blk = P_j V_j with P read
+//               from TMEM. With two issuers one thread's barrier waits overlap the other's
+//               MMAs, and S_{j+1} runs on the tensor core while the softmax warps work on
+//               block j.
 //   warps 0-7   softmax, two threads per query row (TMEM lane), each owning half of the
 //               block's columns and half of the output row (in registers). Online softmax in
 //               base 2 with DenseCore's rules: a block whose running max is -inf adds nothing
@@ -44,6 +45,8 @@
 namespace dc {
 
 __device__ int g_tc_error = 0;
+__device__ long long g_phf[8192];
+#define PH(slot) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_phf[(slot)] = clock64(); } while (0)
 
 namespace {
 
@@ -72,8 +75,9 @@ struct FwdCfg {
     static constexpr int Q_FULL = 0, Q_READY = 1, K_FULL = 2, K_READY = K_FULL + KST,
                          K_EMPTY = K_READY + KST, V_FULL = K_EMPTY + KST, V_READY = V_FULL + VST,
                          V_EMPTY = V_READY + VST, S_FULL = V_EMPTY + VST, P_FULL = S_FULL + 2,
-                         PV_DONE = P_FULL + 2, OB_FREE = PV_DONE + 1, XCH = OB_FREE + 1,
-                         XSUM = XCH + 2, DRAIN = XSUM + 1, NBAR = DRAIN + 1;
+                         PV_DONE = P_FULL + 2, PV_DONE_B = PV_DONE + 1, OB_FREE = PV_DONE_B + 2,
+                         XCH = OB_FREE + 1, XSUM = XCH + 2, DRAIN = XSUM + 1, DRAIN_PV = DRAIN + 1,
+                         NBAR = DRAIN_PV + 1;
     static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
     // TMEM: Q hi | Q lo | 2 x (S / P hi, P lo) | O_blk
@@ -81,8 +85,8 @@ struct FwdCfg {
     static constexpr uint32_t COLS_USED = 3 * D + 4 * BN;
     static constexpr uint32_t TMEM_COLS = COLS_USED <= 256 ? 256 : 512;
     static constexpr int SOFTMAX_THREADS = 256;
-    static constexpr int W_PROD = 8, W_MMA = 9, W_CVT = 10;
-    static constexpr int THREADS = 448;
+    static constexpr int W_PROD = 8, W_MMA = 9, W_CVT = 10, W_PV = 14;
+    static constexpr int THREADS = 480;  // <= 4 warps per SM sub-partition: 128 registers
     static constexpr uint32_t IDESC_S = idesc_tf32(128, BN, 0, 0);
     static constexpr uint32_t IDESC_O = idesc_tf32(128, D, 0, 1);
     __host__ __device__ static constexpr uint32_t col_s(int b) { return 2 * D + b * 2 * BN; }
@@ -162,7 +166,7 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_b
 }
 
 template <class C, bool SPLIT>
-__global__ void __launch_bounds__(C::THREADS, 1)
+__global__ void __maxnreg__(128)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                        const __grid_constant__ CUtensorMap tmv, const TcFwdArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -199,11 +203,14 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             mbar_init(bar(C::P_FULL + s), C::SOFTMAX_THREADS);
         }
         mbar_init(bar(C::PV_DONE), 1);
+        mbar_init(bar(C::PV_DONE_B), 1);
+        mbar_init(bar(C::PV_DONE_B + 1), 1);
         mbar_init(bar(C::OB_FREE), C::SOFTMAX_THREADS);
         mbar_init(bar(C::XCH), C::SOFTMAX_THREADS);
         mbar_init(bar(C::XCH + 1), C::SOFTMAX_THREADS);
         mbar_init(bar(C::XSUM), C::SOFTMAX_THREADS);
         mbar_init(bar(C::DRAIN), 1);
+        mbar_init(bar(C::DRAIN_PV), 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -220,6 +227,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) PH(8000);
 
     if (warp == C::W_PROD) {
         // ------------------------------------------------------------ TMA producer ----
@@ -233,12 +241,14 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             for (int j = 0; ok && j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
                 if (j >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, err)) break;
+                PH(6000 + j);
                 mbar_expect_tx(bar(C::K_FULL + ks), C::KV_BYTES);
                 const uint32_t kd = sb + C::OFF_K + ks * C::KV_STAGE;
                 for (int c = 0; c < C::CHUNKS; c++)
                     tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
                 k_issued = j;
                 if (j >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, err)) break;
+                PH(6100 + j);
                 mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
                 const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
                 for (int c = 0; c < C::CHUNKS; c++)
@@ -256,42 +266,18 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             }
         }
     } else if (warp == C::W_MMA) {
-        // -------------------------------------------------------------- MMA issuer ----
+        // -------------------------------------------------------- MMA issuer: S = Q K^T ----
         if (lane == 0) {
-            // Descriptors of stage 0; stage and k-step offsets go into the address field.
+            // Descriptor of K stage 0; stage and k-step offsets go into the address field.
             const uint64_t kdesc0 = sdesc_sw128(sb + C::OFF_K, 16, 1024);
-            const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
-            const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO, d_ob = tmem + C::COL_OB;
-            auto issue_pv = [&](int i) -> bool {
-                const int bi = i & 1, vs = i % C::VST;
-                if (!mbar_wait(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) return false;
-                if (!mbar_wait(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) return false;
-                if (i >= 1 && !mbar_wait(bar(C::OB_FREE), (i - 1) & 1, abort, err)) return false;
-                tc_fence_after();
-                const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
-                const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
-                if (SPLIT) {  // the small cross terms first, then the main products
-#pragma unroll
-                    for (int kk = 0; kk < C::BN / 8; kk++) {
-                        mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
-                                    kk > 0 ? 1u : 0u);
-                        mma_tf32_ts(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
-                    }
-                }
-#pragma unroll
-                for (int kk = 0; kk < C::BN / 8; kk++)
-                    mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
-                tc_commit(bar(C::PV_DONE));
-                tc_commit(bar(C::V_EMPTY + vs));
-                return true;
-            };
+            const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO;
             bool ok = mbar_wait(bar(C::Q_READY), 0, abort, err);
             tc_fence_after();
             for (int j = 0; ok && j < nblk; j++) {
                 const int bb = j & 1, ks = j % C::KST;
-                if (!mbar_wait(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
                 // S buffer bb held P_{j-2}, read by PV_{j-2}.
-                if (j >= 2 && !mbar_wait(bar(C::PV_DONE), (j - 2) & 1, abort, err)) break;
+                if (j >= 2 && !mbar_wait(bar(C::PV_DONE_B + bb), ((j - 2) >> 1) & 1, abort, err)) break;
+                if (!mbar_wait(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
                 tc_fence_after();
                 const uint64_t kd = kdesc0 + ((ks * C::KV_STAGE) >> 4);
                 const uint32_t d_s = tmem + C::col_s(bb);
@@ -310,18 +296,45 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                 }
                 tc_commit(bar(C::S_FULL + bb));
                 tc_commit(bar(C::K_EMPTY + ks));
-                if (j >= 1 && !issue_pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
             }
-            if (ok && nblk > 0) issue_pv(nblk - 1);
-            // Every MMA issued so far completes before TMEM is released.
+            // Every MMA this thread issued completes before TMEM is released.
             tc_commit(bar(C::DRAIN));
             volatile int never = 0;
             mbar_wait(bar(C::DRAIN), 0, &never, nullptr);
         }
-    } else if (warp >= C::W_CVT) {
+    } else if (warp == C::W_PV) {
+        // ----------------------------------------------------- MMA issuer: O_blk = P V ----
+        if (lane == 0) {
+            const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
+            const uint32_t d_ob = tmem + C::COL_OB;
+            for (int i = 0; i < nblk; i++) {
+                const int bi = i & 1, vs = i % C::VST;
+                if (!mbar_wait(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) break;
+                if (!mbar_wait(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) break;
+                if (i >= 1 && !mbar_wait(bar(C::OB_FREE), (i - 1) & 1, abort, err)) break;
+                tc_fence_after();
+                const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
+                const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
+                if (SPLIT) {  // the small cross terms first, then the main products
+#pragma unroll
+                    for (int kk = 0; kk < C::BN / 8; kk++) {
+                        mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
+                                    kk > 0 ? 1u : 0u);
+                        mma_tf32_ts(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
+                    }
+                }
+#pragma unroll
+                for (int kk = 0; kk < C::BN / 8; kk++)
+                    mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
+                tc_commit(bar(C::PV_DONE));
+                tc_commit(bar(C::PV_DONE_B + bi));
+                tc_commit(bar(C::V_EMPTY + vs));
+            }
+            tc_commit(bar(C::DRAIN_PV));
+            volatile int never = 0;
+            mbar_wait(bar(C::DRAIN_PV), 0, &never, nullptr);
+        }
+    } else if (warp >= C::W_CVT && warp < C::W_PV) {
         // --------------------------------------------------------------- converters ----
         const int ct = threadIdx.x - 32 * C::W_CVT;
         const int quad = warp & 3;
@@ -331,16 +344,21 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::Q_READY));
+            if (ct == 0) PH(8001);
             for (int j = 0; j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
                 if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, err)) break;
+                if (ct == 0) PH(7000 + j * 4);
                 split_tile<SPLIT>(sg + C::OFF_K + ks * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
                 mbar_arrive(bar(C::K_READY + ks));
+                if (ct == 0) PH(7001 + j * 4);
                 if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, err)) break;
+                if (ct == 0) PH(7002 + j * 4);
                 split_tile<SPLIT>(sg + C::OFF_V + vs * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
                 mbar_arrive(bar(C::V_READY + vs));
+                if (ct == 0) PH(7003 + j * 4);
             }
         }
     } else {
@@ -362,6 +380,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                 ok = false;
                 break;
             }
+            if (threadIdx.x == 0) PH(4 + j * 8);
             tc_fence_after();
             float s[C::HB];
             {
@@ -429,6 +448,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::P_FULL + bb));
+            if (threadIdx.x == 0) PH(7 + j * 8);
             // Fold the previous block: o = (o + O_blk(j-1)) * corr (both relative to the
             // previous max; corr moves them to m).
             if (j >= 1) {
@@ -447,6 +467,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                 }
                 tc_fence_before();
                 mbar_arrive(bar(C::OB_FREE));
+                if (threadIdx.x == 0) PH(5000 + j);
             }
         }
         if (ok && nblk > 0) {
@@ -560,3 +581,5 @@ int device_error(int reset) {
 }
 
 }  // namespace dc
+
+extern "C" int dc_read_phases_fwd(long long *out) { return cudaMemcpyFromSymbol(out, dc::g_phf, sizeof(long long) * 8192) == cudaSuccess ? 0 : 1; }

@@ -17,21 +17,25 @@
 //         128-byte swizzle and in the MN-major 32-byte-atom swizzle that tf32 requires) stream
 //         through two rings: the K-major tiles (3 stages) are free once the S / dP MMAs have
 //         read them, the MN-major tiles (2 stages) once the gradient MMAs have. Per block i:
-//         S^T = K Q^T and dP^T = V dO^T into one of two TMEM buffers; eight softmax warps (two per TMEM lane quadrant, 16 query columns
-//         each) turn them into P^T and dS^T (hi / lo, in place); then dV_blk += P^T dO and
-//         dK_blk += dS^T Q. Issue order S0, S1, G0, S2, G1, ... keeps the tensor core busy
-//         while the softmax warps work. The same warps add the block accumulators into fp32
+//         S^T = K Q^T and dP^T = V dO^T into one of two TMEM buffers; eight softmax warps
+//         (two per TMEM lane quadrant, 16 query columns each) turn them into P^T and dS^T
+//         (hi / lo, in place); then dV_blk += P^T dO and dK_blk += dS^T Q. S_{i+1} runs on the
+//         tensor core while the softmax warps work on block i. The same warps add the block
+//         accumulators into fp32
 //         registers every FOLD blocks (the tensor core's accumulation is coarser than fp32
 //         over long chains): the first four keep dV, the other four dK.
 //   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi in
-//         TMEM, lo in shared memory); 32-key blocks of K (two layouts) and V stream through a
-//         3-stage ring. Per block: S = Q K^T and dP = dO V^T, dS in TMEM, dQ_blk += dS K,
+//         TMEM, lo in shared memory); 32-key blocks of K and V (K-major, 4 stages) and of K
+//         (MN-major, 2 stages) stream through two rings. Per block: S = Q K^T and dP = dO V^T, dS in TMEM, dQ_blk += dS K,
 //         folded into fp32 registers (each softmax warp keeps 32 of the 64 dQ columns).
 //
-// Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer (one
-// thread; it also owns TMEM). Every wait is bounded; a timeout records an error and unwinds.
-// Grids are 1-D and hand out the tiles with the most causal work first (longest-first
-// dispatch keeps the last wave short).
+// Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer of S
+// and dP (one thread; it also owns TMEM), warp 10 a second TMA producer (the MN-major ring, so
+// that the K-major ring can run ahead of it), warp 11 MMA issuer of the gradients (so that
+// either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout records an error and
+// unwinds. Grids are 1-D: groups of GROUP_HEADS (batch, head) pairs, and within a group the
+// tiles with the most causal work first. The group keeps the streamed operands of its heads
+// in L2; the order within it keeps the last wave short.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -53,8 +57,9 @@ constexpr int CHUNKS = D / 32;
 constexpr int TILE = 128;    // rows owned by a CTA (the MMA M)
 constexpr int BLK = 32;      // streamed rows per step (the MMA N of S / dP, the K of the rest)
 constexpr int FOLD = 2;      // blocks per tensor-core accumulation chain
-constexpr int THREADS = 320; // 8 softmax / fold warps, producer, MMA issuer
-constexpr int W_PROD = 8, W_MMA = 9;
+constexpr int THREADS = 384; // 8 softmax / fold warps, 2 producers, 2 MMA issuers
+constexpr int W_PROD = 8, W_MMA = 9, W_PROD2 = 10, W_GMMA = 11;
+constexpr int GROUP_HEADS = 16;  // (batch, head) pairs whose tiles are handed out together
 constexpr unsigned FULL = 0xffffffffu;
 
 constexpr uint32_t RES_BYTES = TILE * D * 4;      // one resident fp32 tile (32 KB)
@@ -157,6 +162,16 @@ __device__ __forceinline__ void store_row(float *dst, int64_t inner, const float
     }
 }
 
+// Tile `tile` and (batch, head) pair `bh` of CTA `idx` in the grouped order: idx runs over
+// groups of GROUP_HEADS pairs, inside a group over tiles (outer) and pairs (inner).
+__device__ __forceinline__ void grouped_tile(int64_t idx, int64_t ntiles, int64_t bh_n, int64_t &tile, int64_t &bh) {
+    const int64_t per_group = ntiles * GROUP_HEADS;
+    const int64_t g = idx / per_group, base = g * GROUP_HEADS;
+    const int64_t gsize = min((int64_t)GROUP_HEADS, bh_n - base), r = idx - g * per_group;
+    tile = r / gsize;
+    bh = base + r % gsize;
+}
+
 struct TcBwdArgs {
     AttnProblem p;
     AttnGrads g;
@@ -245,7 +260,7 @@ constexpr uint32_t OFF_BAR = OFF_VLO + RES_BYTES;
 // fold has read the block accumulators (the next chain may overwrite them).
 enum { KV_FULL, KV_READY, SS_FULL, SS_EMPTY = SS_FULL + NSS, SG_FULL = SS_EMPTY + NSS, SG_EMPTY = SG_FULL + NSG,
        S_FULL = SG_EMPTY + NSG, P_FULL = S_FULL + 2, G_DONE = P_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE,
-       DRAIN, NBAR };
+       DRAIN, DRAIN_G, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
 // TMEM: K hi | V hi | 2 x (S^T / P^T hi, P^T lo, dP^T / dS^T hi, dS^T lo) | dV_blk | dK_blk
@@ -275,7 +290,8 @@ __global__ void __maxnreg__(168)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
     // Key tiles in ascending order: under causal masking tile 0 sees the most query rows.
-    const int64_t bh_n = p.B * p.Hkv, kt = blockIdx.x / bh_n, bh = blockIdx.x % bh_n;
+    int64_t kt, bh;
+    grouped_tile(blockIdx.x, (p.S + TILE - 1) / TILE, p.B * p.Hkv, kt, bh);
     const int64_t hk = bh % p.Hkv, b = bh / p.Hkv, k0 = kt * TILE;
     const int lo_b = (int)(p.B + b);  // batch coordinate of the lo copies
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
@@ -311,6 +327,7 @@ __global__ void __maxnreg__(168)
         mbar_init(bar(CHAIN_DONE), 1);
         mbar_init(bar(BLK_FREE), 256);
         mbar_init(bar(DRAIN), 1);
+        mbar_init(bar(DRAIN_G), 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -324,9 +341,9 @@ __global__ void __maxnreg__(168)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == W_PROD) {
-        // ---------------------------------------------------------------- producer ----
+        // ----------------------------------------- producer: K / V, then the K-major ring ----
         if (lane == 0) {
-            int issued_s = -1, issued_g = -1;
+            int issued = -1;
             // K and V hi into S stages 0-1 (K at 0, V at RES_BYTES); lo straight to their slots.
             mbar_expect_tx(bar(KV_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
             for (int c = 0; c < CHUNKS; c++) {
@@ -341,7 +358,7 @@ __global__ void __maxnreg__(168)
             for (int i = 0; ok && i < nblk; i++) {
                 int64_t h, q0;
                 blk_coords(i, h, q0);
-                const int ss = i % NSS, sgi = i % NSG;
+                const int ss = i % NSS;
                 if (i >= NSS && !mbar_wait(bar(SS_EMPTY + ss), ((i / NSS) - 1) & 1, abort, err)) break;
                 const uint32_t sst = sb + OFF_SRING + ss * SSTAGE, fs = bar(SS_FULL + ss);
                 mbar_expect_tx(fs, (SPLIT ? 4 : 2) * BLK_BYTES);
@@ -354,7 +371,23 @@ __global__ void __maxnreg__(168)
                         tma_load_4d(&tm_dok, sst + SS_DOK + BLK_BYTES + o, fs, 32 * c, (int)q0, (int)h, lo_b);
                     }
                 }
-                issued_s = i;
+                issued = i;
+            }
+            if (*abort) {  // let the copies in flight land before the CTA exits
+                volatile int never = 0;
+                mbar_wait(bar(KV_FULL), 0, &never, nullptr);
+                for (int i = max(0, issued - NSS + 1); i <= issued; i++)
+                    mbar_wait(bar(SS_FULL + i % NSS), (i / NSS) & 1, &never, nullptr);
+            }
+        }
+    } else if (warp == W_PROD2) {
+        // ------------------------------------------------ producer: the MN-major ring ----
+        if (lane == 0) {
+            int issued = -1;
+            for (int i = 0; i < nblk; i++) {
+                int64_t h, q0;
+                blk_coords(i, h, q0);
+                const int sgi = i % NSG;
                 if (i >= NSG && !mbar_wait(bar(SG_EMPTY + sgi), ((i / NSG) - 1) & 1, abort, err)) break;
                 const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE, fg = bar(SG_FULL + sgi);
                 mbar_expect_tx(fg, (SPLIT ? 4 : 2) * BLK_BYTES);
@@ -367,28 +400,47 @@ __global__ void __maxnreg__(168)
                         tma_load_4d(&tm_domn, gst + SG_DOMN + BLK_BYTES + o, fg, 32 * c, (int)q0, (int)h, lo_b);
                     }
                 }
-                issued_g = i;
+                issued = i;
+                if (*abort) break;
             }
-            if (*abort) {  // let the copies in flight land before the CTA exits
+            if (*abort) {
                 volatile int never = 0;
-                mbar_wait(bar(KV_FULL), 0, &never, nullptr);
-                for (int i = max(0, issued_s - NSS + 1); i <= issued_s; i++)
-                    mbar_wait(bar(SS_FULL + i % NSS), (i / NSS) & 1, &never, nullptr);
-                for (int i = max(0, issued_g - NSG + 1); i <= issued_g; i++)
+                for (int i = max(0, issued - NSG + 1); i <= issued; i++)
                     mbar_wait(bar(SG_FULL + i % NSG), (i / NSG) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
-        // ------------------------------------------------------------------ MMA ------
+        // ------------------------------------------------------- MMA: S^T and dP^T ------
         if (lane == 0) {
             const uint64_t klo = sdesc_sw128(sb + OFF_KLO, 16, 1024), vlo = sdesc_sw128(sb + OFF_VLO, 16, 1024);
-            auto issue_g = [&](int i) -> bool {  // gradients of block i
+            bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
+            tc_fence_after();
+            for (int i = 0; ok && i < nblk; i++) {
+                const int ss = i % NSS, bb = i & 1;
+                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
+                // Buffer bb holds P^T / dS^T of block i-2 until its gradient MMAs finish.
+                if (i >= 2 && !mbar_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
+                if (!mbar_wait(bar(SS_FULL + ss), (i / NSS) & 1, abort, err)) break;
+                tc_fence_after();
+                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_KHI, klo, sdesc_sw128(sst + SS_QK, 16, 1024));
+                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_VHI, vlo, sdesc_sw128(sst + SS_DOK, 16, 1024));
+                tc_commit(bar(S_FULL + bb));
+                tc_commit(bar(SS_EMPTY + ss));
+            }
+            tc_commit(bar(DRAIN));
+            volatile int never = 0;
+            mbar_wait(bar(DRAIN), 0, &never, nullptr);
+        }
+    } else if (warp == W_GMMA) {
+        // ------------------------------------------------ MMA: dV_blk and dK_blk ------
+        if (lane == 0) {
+            for (int i = 0; i < nblk; i++) {
                 const int sgi = i % NSG, bb = i & 1;
                 const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
-                if (!mbar_wait(bar(P_FULL + bb), (i >> 1) & 1, abort, err)) return false;
+                if (!mbar_wait(bar(P_FULL + bb), (i >> 1) & 1, abort, err)) break;
                 const bool first = (i % FOLD) == 0;
-                if (first && i >= FOLD && !mbar_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, err)) return false;
-                if (!mbar_wait(bar(SG_FULL + sgi), (i / NSG) & 1, abort, err)) return false;
+                if (first && i >= FOLD && !mbar_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, err)) break;
+                if (!mbar_wait(bar(SG_FULL + sgi), (i / NSG) & 1, abort, err)) break;
                 tc_fence_after();
                 mma_g<SPLIT>(tmem + C_DV, tmem + c_s(bb), tmem + c_plo(bb),
                              sdesc_mn_sw128_32b(gst + SG_DOMN, BLK_CHUNK, 512), !first);
@@ -397,32 +449,12 @@ __global__ void __maxnreg__(168)
                 tc_commit(bar(G_DONE + bb));
                 if ((i % FOLD) == FOLD - 1 || i == nblk - 1) tc_commit(bar(CHAIN_DONE));
                 tc_commit(bar(SG_EMPTY + sgi));
-                return true;
-            };
-            bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
-            tc_fence_after();
-            for (int i = 0; ok && i < nblk; i++) {
-                const int ss = i % NSS, bb = i & 1;
-                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
-                if (!mbar_wait(bar(SS_FULL + ss), (i / NSS) & 1, abort, err)) break;
-                // Buffer bb holds P^T / dS^T of block i-2 until its gradient MMAs finish.
-                if (i >= 2 && !mbar_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
-                tc_fence_after();
-                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_KHI, klo, sdesc_sw128(sst + SS_QK, 16, 1024));
-                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_VHI, vlo, sdesc_sw128(sst + SS_DOK, 16, 1024));
-                tc_commit(bar(S_FULL + bb));
-                tc_commit(bar(SS_EMPTY + ss));
-                if (i >= 1 && !issue_g(i - 1)) {
-                    ok = false;
-                    break;
-                }
             }
-            if (ok && nblk > 0) issue_g(nblk - 1);
-            tc_commit(bar(DRAIN));
+            tc_commit(bar(DRAIN_G));
             volatile int never = 0;
-            mbar_wait(bar(DRAIN), 0, &never, nullptr);
+            mbar_wait(bar(DRAIN_G), 0, &never, nullptr);
         }
-    } else {
+    } else if (warp < W_PROD) {
         // ---------------------------------- P^T and dS^T, then the fp32 dV / dK folds ----
         const int quad = warp & 3, half = warp >> 2;  // lane quadrant; query-column half / dV or dK
         const int row = quad * 32 + lane;             // key row of this CTA
@@ -535,14 +567,18 @@ __global__ void __maxnreg__(168)
 
 // ========================================================================= dQ ========
 namespace qq {
-constexpr int NST = 3;
-// stage: K_K hi, lo | K_MN hi, lo | V_K hi, lo  (8 KB each)
-constexpr uint32_t ST_KK = 0, ST_KMN = 2 * BLK_BYTES, ST_VK = 4 * BLK_BYTES;
-constexpr uint32_t STAGE_BYTES = 6 * BLK_BYTES;  // 48 KB
-constexpr uint32_t OFF_QLO = NST * STAGE_BYTES, OFF_DOLO = OFF_QLO + RES_BYTES;
+// Two rings as in dkdv: K-major K and V tiles (S / dP MMAs; 4 stages) and MN-major K tiles
+// (the dQ MMA; 2 stages).
+constexpr int NSS = 4, NSG = 2;
+// S stage: K_K hi, lo | V_K hi, lo; G stage: K_MN hi, lo (8 KB tiles)
+constexpr uint32_t SS_KK = 0, SS_VK = 2 * BLK_BYTES, SG_KMN = 0;
+constexpr uint32_t SSTAGE = 4 * BLK_BYTES, GSTAGE = 2 * BLK_BYTES;  // 32 KB, 16 KB
+constexpr uint32_t OFF_SRING = 0, OFF_GRING = NSS * SSTAGE;
+constexpr uint32_t OFF_QLO = OFF_GRING + NSG * GSTAGE, OFF_DOLO = OFF_QLO + RES_BYTES;
 constexpr uint32_t OFF_BAR = OFF_DOLO + RES_BYTES;
-enum { QD_FULL, QD_READY, ST_FULL, ST_EMPTY = ST_FULL + NST, S_FULL = ST_EMPTY + NST, DS_FULL = S_FULL + 2,
-       G_DONE = DS_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE, DRAIN, NBAR };
+enum { QD_FULL, QD_READY, SS_FULL, SS_EMPTY = SS_FULL + NSS, SG_FULL = SS_EMPTY + NSS, SG_EMPTY = SG_FULL + NSG,
+       S_FULL = SG_EMPTY + NSG, DS_FULL = S_FULL + 2, G_DONE = DS_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE,
+       DRAIN, DRAIN_G, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
 // TMEM: Q hi | dO hi | 2 x (S, dP / dS hi, dS lo) | dQ_blk
@@ -550,7 +586,7 @@ constexpr uint32_t C_QHI = 0, C_DOHI = 64, C_DQB = 320, TCOLS = 512;
 __device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 96; }
 __device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 160 + b * 96; }
 __device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 192 + b * 96; }
-static_assert(2 * RES_BYTES <= 2 * STAGE_BYTES, "Q / dO hi are staged in stages 0-1");
+static_assert(2 * RES_BYTES <= 2 * SSTAGE, "Q / dO hi are staged in S stages 0-1");
 static_assert(SMEM <= 232448, "smem");
 }  // namespace qq
 
@@ -569,8 +605,10 @@ __global__ void __maxnreg__(168)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
     // Query tiles in descending order: under causal masking the last tile sees the most keys.
-    const int64_t bh_n = p.B * p.H, ntiles = (p.L + TILE - 1) / TILE;
-    const int64_t qt = ntiles - 1 - blockIdx.x / bh_n, bh = blockIdx.x % bh_n;
+    const int64_t ntiles = (p.L + TILE - 1) / TILE;
+    int64_t qt, bh;
+    grouped_tile(blockIdx.x, ntiles, p.B * p.H, qt, bh);
+    qt = ntiles - 1 - qt;
     const int64_t h = bh % p.H, b = bh / p.H, hk = h / p.group;
     const int lo_b = (int)(p.B + b);
     const int64_t q0 = qt * TILE;
@@ -584,9 +622,13 @@ __global__ void __maxnreg__(168)
     if (threadIdx.x == 0) {
         mbar_init(bar(QD_FULL), 1);
         mbar_init(bar(QD_READY), 256);
-        for (int s = 0; s < NST; s++) {
-            mbar_init(bar(ST_FULL + s), 1);
-            mbar_init(bar(ST_EMPTY + s), 1);
+        for (int s = 0; s < NSS; s++) {
+            mbar_init(bar(SS_FULL + s), 1);
+            mbar_init(bar(SS_EMPTY + s), 1);
+        }
+        for (int s = 0; s < NSG; s++) {
+            mbar_init(bar(SG_FULL + s), 1);
+            mbar_init(bar(SG_EMPTY + s), 1);
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(bar(S_FULL + s), 1);
@@ -596,6 +638,7 @@ __global__ void __maxnreg__(168)
         mbar_init(bar(CHAIN_DONE), 1);
         mbar_init(bar(BLK_FREE), 256);
         mbar_init(bar(DRAIN), 1);
+        mbar_init(bar(DRAIN_G), 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -609,6 +652,7 @@ __global__ void __maxnreg__(168)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == W_PROD) {
+        // ----------------------------------------- producer: Q / dO, then the K-major ring ----
         if (lane == 0) {
             int issued = -1;
             mbar_expect_tx(bar(QD_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
@@ -622,19 +666,17 @@ __global__ void __maxnreg__(168)
             }
             bool ok = mbar_wait(bar(QD_READY), 0, abort, err);
             for (int j = 0; ok && j < nblk; j++) {
-                const int s = j % NST;
-                if (j >= NST && !mbar_wait(bar(ST_EMPTY + s), ((j / NST) - 1) & 1, abort, err)) break;
-                const uint32_t st = sb + s * STAGE_BYTES, fb = bar(ST_FULL + s);
-                mbar_expect_tx(fb, (SPLIT ? 6 : 3) * BLK_BYTES);
+                const int ss = j % NSS;
+                if (j >= NSS && !mbar_wait(bar(SS_EMPTY + ss), ((j / NSS) - 1) & 1, abort, err)) break;
+                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE, fs = bar(SS_FULL + ss);
+                mbar_expect_tx(fs, (SPLIT ? 4 : 2) * BLK_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
                     const uint32_t o = c * BLK_CHUNK;
-                    tma_load_4d(&tm_kk, st + ST_KK + o, fb, 32 * c, j * BLK, (int)hk, (int)b);
-                    tma_load_4d(&tm_kmn, st + ST_KMN + o, fb, 32 * c, j * BLK, (int)hk, (int)b);
-                    tma_load_4d(&tm_vk, st + ST_VK + o, fb, 32 * c, j * BLK, (int)hk, (int)b);
+                    tma_load_4d(&tm_kk, sst + SS_KK + o, fs, 32 * c, j * BLK, (int)hk, (int)b);
+                    tma_load_4d(&tm_vk, sst + SS_VK + o, fs, 32 * c, j * BLK, (int)hk, (int)b);
                     if (SPLIT) {
-                        tma_load_4d(&tm_kk, st + ST_KK + BLK_BYTES + o, fb, 32 * c, j * BLK, (int)hk, lo_b);
-                        tma_load_4d(&tm_kmn, st + ST_KMN + BLK_BYTES + o, fb, 32 * c, j * BLK, (int)hk, lo_b);
-                        tma_load_4d(&tm_vk, st + ST_VK + BLK_BYTES + o, fb, 32 * c, j * BLK, (int)hk, lo_b);
+                        tma_load_4d(&tm_kk, sst + SS_KK + BLK_BYTES + o, fs, 32 * c, j * BLK, (int)hk, lo_b);
+                        tma_load_4d(&tm_vk, sst + SS_VK + BLK_BYTES + o, fs, 32 * c, j * BLK, (int)hk, lo_b);
                     }
                 }
                 issued = j;
@@ -642,50 +684,77 @@ __global__ void __maxnreg__(168)
             if (*abort) {
                 volatile int never = 0;
                 mbar_wait(bar(QD_FULL), 0, &never, nullptr);
-                for (int j = max(0, issued - NST + 1); j <= issued; j++)
-                    mbar_wait(bar(ST_FULL + j % NST), (j / NST) & 1, &never, nullptr);
+                for (int j = max(0, issued - NSS + 1); j <= issued; j++)
+                    mbar_wait(bar(SS_FULL + j % NSS), (j / NSS) & 1, &never, nullptr);
+            }
+        }
+    } else if (warp == W_PROD2) {
+        // ------------------------------------------------ producer: the MN-major ring ----
+        if (lane == 0) {
+            int issued = -1;
+            for (int j = 0; j < nblk; j++) {
+                const int sgi = j % NSG;
+                if (j >= NSG && !mbar_wait(bar(SG_EMPTY + sgi), ((j / NSG) - 1) & 1, abort, err)) break;
+                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE, fg = bar(SG_FULL + sgi);
+                mbar_expect_tx(fg, (SPLIT ? 2 : 1) * BLK_BYTES);
+                for (int c = 0; c < CHUNKS; c++) {
+                    const uint32_t o = c * BLK_CHUNK;
+                    tma_load_4d(&tm_kmn, gst + SG_KMN + o, fg, 32 * c, j * BLK, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_kmn, gst + SG_KMN + BLK_BYTES + o, fg, 32 * c, j * BLK, (int)hk, lo_b);
+                }
+                issued = j;
+                if (*abort) break;
+            }
+            if (*abort) {
+                volatile int never = 0;
+                for (int j = max(0, issued - NSG + 1); j <= issued; j++)
+                    mbar_wait(bar(SG_FULL + j % NSG), (j / NSG) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
+        // ------------------------------------------------------------ MMA: S and dP ------
         if (lane == 0) {
             const uint64_t qlo = sdesc_sw128(sb + OFF_QLO, 16, 1024), dolo = sdesc_sw128(sb + OFF_DOLO, 16, 1024);
-            auto issue_g = [&](int j) -> bool {
-                const int s = j % NST, bb = j & 1;
-                const uint32_t st = sb + s * STAGE_BYTES;
-                if (!mbar_wait(bar(DS_FULL + bb), (j >> 1) & 1, abort, err)) return false;
-                const bool first = (j % FOLD) == 0;
-                if (first && j >= FOLD && !mbar_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, err)) return false;
-                tc_fence_after();
-                mma_g<SPLIT>(tmem + C_DQB, tmem + c_dp(bb), tmem + c_dslo(bb),
-                             sdesc_mn_sw128_32b(st + ST_KMN, BLK_CHUNK, 512), !first);
-                tc_commit(bar(G_DONE + bb));
-                if ((j % FOLD) == FOLD - 1 || j == nblk - 1) tc_commit(bar(CHAIN_DONE));
-                tc_commit(bar(ST_EMPTY + s));
-                return true;
-            };
             bool ok = mbar_wait(bar(QD_READY), 0, abort, err);
             tc_fence_after();
             for (int j = 0; ok && j < nblk; j++) {
-                const int s = j % NST, bb = j & 1;
-                const uint32_t st = sb + s * STAGE_BYTES;
-                if (!mbar_wait(bar(ST_FULL + s), (j / NST) & 1, abort, err)) break;
+                const int ss = j % NSS, bb = j & 1;
+                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
                 // Buffer bb holds dS of block j-2 until its gradient MMAs finish.
                 if (j >= 2 && !mbar_wait(bar(G_DONE + bb), ((j - 2) >> 1) & 1, abort, err)) break;
+                if (!mbar_wait(bar(SS_FULL + ss), (j / NSS) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_QHI, qlo, sdesc_sw128(st + ST_KK, 16, 1024));
-                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_DOHI, dolo, sdesc_sw128(st + ST_VK, 16, 1024));
+                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_QHI, qlo, sdesc_sw128(sst + SS_KK, 16, 1024));
+                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_DOHI, dolo, sdesc_sw128(sst + SS_VK, 16, 1024));
                 tc_commit(bar(S_FULL + bb));
-                if (j >= 1 && !issue_g(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                tc_commit(bar(SS_EMPTY + ss));
             }
-            if (ok && nblk > 0) issue_g(nblk - 1);
             tc_commit(bar(DRAIN));
             volatile int never = 0;
             mbar_wait(bar(DRAIN), 0, &never, nullptr);
         }
-    } else {
+    } else if (warp == W_GMMA) {
+        // ---------------------------------------------------------------- MMA: dQ_blk ----
+        if (lane == 0) {
+            for (int j = 0; j < nblk; j++) {
+                const int sgi = j % NSG, bb = j & 1;
+                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
+                if (!mbar_wait(bar(DS_FULL + bb), (j >> 1) & 1, abort, err)) break;
+                const bool first = (j % FOLD) == 0;
+                if (first && j >= FOLD && !mbar_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, err)) break;
+                if (!mbar_wait(bar(SG_FULL + sgi), (j / NSG) & 1, abort, err)) break;
+                tc_fence_after();
+                mma_g<SPLIT>(tmem + C_DQB, tmem + c_dp(bb), tmem + c_dslo(bb),
+                             sdesc_mn_sw128_32b(gst + SG_KMN, BLK_CHUNK, 512), !first);
+                tc_commit(bar(G_DONE + bb));
+                if ((j % FOLD) == FOLD - 1 || j == nblk - 1) tc_commit(bar(CHAIN_DONE));
+                tc_commit(bar(SG_EMPTY + sgi));
+            }
+            tc_commit(bar(DRAIN_G));
+            volatile int never = 0;
+            mbar_wait(bar(DRAIN_G), 0, &never, nullptr);
+        }
+    } else if (warp < W_PROD) {
         // ----------------------------------------------------- dS, then the fp32 dQ fold --
         const int quad = warp & 3, half = warp >> 2;
         const int row = quad * 32 + lane;
