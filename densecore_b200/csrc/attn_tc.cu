@@ -401,16 +401,22 @@ __global__ void __maxnreg__(128)
                     bmax = fmaxf(bmax, s[c]);
                 }
             } else {
+                // Column c is key k0 + c: valid below S and, under causal masking, up to qrow.
+                // One bit per column keeps this path as short as the fast one.
+                const int64_t lim = (p.causal ? min(p.S, qrow + 1) : p.S) - k0;
+                const int n = !row_ok || lim <= 0 ? 0 : (lim >= C::HB ? C::HB : (int)lim);
+                const uint32_t vbits = n == 0 ? 0u : (0xFFFFFFFFu >> (32 - n));
+#pragma unroll
+                for (int c = 0; c < C::HB; c++) s[c] *= a.scale_log2;
+                if (p.mask_kind != MASK_NONE) {
+#pragma unroll
+                    for (int c = 0; c < C::HB; c++)
+                        if ((vbits >> c) & 1u) s[c] += mask_value(p, b, h, qrow, k0 + c) * LOG2E;
+                }
 #pragma unroll
                 for (int c = 0; c < C::HB; c++) {
-                    const int64_t key = k0 + c;
-                    float x = s[c] * a.scale_log2;
-                    if (!row_ok || key >= p.S || (p.causal && key > qrow))
-                        x = -INFINITY;
-                    else if (p.mask_kind != MASK_NONE)
-                        x += mask_value(p, b, h, qrow, key) * LOG2E;
-                    s[c] = x;
-                    bmax = fmaxf(bmax, x);
+                    s[c] = ((vbits >> c) & 1u) ? s[c] : -INFINITY;
+                    bmax = fmaxf(bmax, s[c]);
                 }
             }
             // The block's row max, shared with the partner thread (the other half) through

@@ -21,19 +21,21 @@
 //         (two per TMEM lane quadrant, 16 query columns each) turn them into P^T and dS^T
 //         (hi / lo, in place); then dV_blk += P^T dO and dK_blk += dS^T Q. S_{i+1} runs on the
 //         tensor core while the softmax warps work on block i. The same warps add the block
-//         accumulators into fp32
-//         registers every FOLD blocks (the tensor core's accumulation is coarser than fp32
-//         over long chains): the first four keep dV, the other four dK.
+//         accumulators into fp32 registers every FOLD blocks (the tensor core's accumulation is
+//         coarser than fp32 over long chains): the first four keep dV, the other four dK.
 //   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi in
 //         TMEM, lo in shared memory); 32-key blocks of K and V (K-major, 4 stages) and of K
-//         (MN-major, 2 stages) stream through two rings. Per block: S = Q K^T and dP = dO V^T, dS in TMEM, dQ_blk += dS K,
-//         folded into fp32 registers (each softmax warp keeps 32 of the 64 dQ columns).
+//         (MN-major, 2 stages) stream through two rings. Per block: S = Q K^T and dP = dO V^T,
+//         dS in TMEM, dQ_blk += dS K, folded into fp32 registers (each softmax warp keeps 32 of
+//         the 64 dQ columns).
 //
 // Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer of S
 // and dP (one thread; it also owns TMEM), warp 10 a second TMA producer (the MN-major ring, so
 // that the K-major ring can run ahead of it), warp 11 MMA issuer of the gradients (so that
-// either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout records an error and
-// unwinds. Grids are 1-D: groups of GROUP_HEADS (batch, head) pairs, and within a group the
+// either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout
+// records an error and unwinds. The softmax loops stay branch-free per column (validity as a
+// bit mask; a user mask in a separate pass) to keep the hot code small: twelve warps running
+// different loops already crowd the instruction cache. Grids are 1-D: groups of GROUP_HEADS (batch, head) pairs, and within a group the
 // tiles with the most causal work first. The group keeps the streamed operands of its heads
 // in L2; the order within it keeps the last wave short.
 #include <cuda.h>
@@ -137,6 +139,13 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *tile, int row, uint32
 // warp-collective tcgen05.ld / st and shuffles after it run converged.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err) {
     return __all_sync(FULL, mbar_wait(bar, parity, abort, err));
+}
+
+// Bit c set for the columns c of [lo, hi) within 0..15.
+__device__ __forceinline__ uint32_t col_bits(int64_t lo, int64_t hi) {
+    lo = lo < 0 ? 0 : lo;
+    hi = hi > 16 ? 16 : hi;
+    return hi > lo ? ((0xFFFFu >> (16 - (int)(hi - lo))) << (int)lo) : 0u;
 }
 
 // Adds 16 TMEM columns of this lane into acc[0..15].
@@ -511,17 +520,22 @@ __global__ void __maxnreg__(168)
             tmem_ld16(tl + c_s(bb) + cb, sr);
             tmem_ld16(tl + c_dp(bb) + cb, dr);
             tmem_wait_ld();
+            // Column c is query base + c: valid below L and, under causal masking, from `key` on.
+            const int64_t base = q0 + cb;
+            uint32_t vbits = 0xFFFFu;
+            if (edge) vbits = key_ok ? col_bits(p.causal ? key - base : 0, p.L - base) : 0u;
+#pragma unroll
+            for (int c = 0; c < 16; c++) sr[c] = __float_as_uint(__uint_as_float(sr[c]) * a.scale_log2);
+            if (p.mask_kind != MASK_NONE) {
+#pragma unroll
+                for (int c = 0; c < 16; c++)
+                    if ((vbits >> c) & 1u)
+                        sr[c] = __float_as_uint(__uint_as_float(sr[c]) + mask_value(p, b, h, base + c, key) * LOG2E);
+            }
 #pragma unroll
             for (int c = 0; c < 16; c++) {
                 const float lse2 = __shfl_sync(FULL, cur, c), del = __shfl_sync(FULL, cur, 16 + c);
-                float x = __uint_as_float(sr[c]) * a.scale_log2;
-                bool valid = true;
-                if (edge) {
-                    const int64_t q = q0 + cb + c;
-                    valid = key_ok && q < p.L && !(p.causal && key > q);
-                    if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
-                }
-                const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
+                const float pc = ((vbits >> c) & 1u) ? ex2_approx(__uint_as_float(sr[c]) - lse2) : 0.0f;
                 const float ds = pc * (__uint_as_float(dr[c]) - del);
                 phi[c] = tf32_rna(pc);
                 sr[c] = tf32_rna(ds);
@@ -801,16 +815,21 @@ __global__ void __maxnreg__(168)
             tmem_ld16(tl + c_s(bb) + cb, sr);
             tmem_ld16(tl + c_dp(bb) + cb, dr);
             tmem_wait_ld();
+            // Column c is key base + c: valid below S and, under causal masking, up to q.
+            const int64_t base = kb0 + cb;
+            uint32_t vbits = 0xFFFFu;
+            if (edge) vbits = row_ok ? col_bits(0, (p.causal ? min(p.S, q + 1) : p.S) - base) : 0u;
+#pragma unroll
+            for (int c = 0; c < 16; c++) sr[c] = __float_as_uint(__uint_as_float(sr[c]) * a.scale_log2);
+            if (p.mask_kind != MASK_NONE) {
+#pragma unroll
+                for (int c = 0; c < 16; c++)
+                    if ((vbits >> c) & 1u)
+                        sr[c] = __float_as_uint(__uint_as_float(sr[c]) + mask_value(p, b, h, q, base + c) * LOG2E);
+            }
 #pragma unroll
             for (int c = 0; c < 16; c++) {
-                float x = __uint_as_float(sr[c]) * a.scale_log2;
-                bool valid = true;
-                if (edge) {
-                    const int64_t key = kb0 + cb + c;
-                    valid = row_ok && key < p.S && !(p.causal && key > q);
-                    if (valid && p.mask_kind != MASK_NONE) x += mask_value(p, b, h, q, key) * LOG2E;
-                }
-                const float pc = valid ? ex2_approx(x - lse2) : 0.0f;
+                const float pc = ((vbits >> c) & 1u) ? ex2_approx(__uint_as_float(sr[c]) - lse2) : 0.0f;
                 const float ds = pc * (__uint_as_float(dr[c]) - del);
                 sr[c] = tf32_rna(ds);
                 if (SPLIT) dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
