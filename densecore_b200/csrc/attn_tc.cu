@@ -45,8 +45,6 @@
 namespace dc {
 
 __device__ int g_tc_error = 0;
-__device__ long long g_phf[8192];
-#define PH(slot) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_phf[(slot)] = clock64(); } while (0)
 
 namespace {
 
@@ -227,7 +225,6 @@ __global__ void __maxnreg__(128)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (threadIdx.x == 0) PH(8000);
 
     if (warp == C::W_PROD) {
         // ------------------------------------------------------------ TMA producer ----
@@ -241,14 +238,12 @@ __global__ void __maxnreg__(128)
             for (int j = 0; ok && j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
                 if (j >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, err)) break;
-                PH(6000 + j);
                 mbar_expect_tx(bar(C::K_FULL + ks), C::KV_BYTES);
                 const uint32_t kd = sb + C::OFF_K + ks * C::KV_STAGE;
                 for (int c = 0; c < C::CHUNKS; c++)
                     tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
                 k_issued = j;
                 if (j >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, err)) break;
-                PH(6100 + j);
                 mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
                 const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
                 for (int c = 0; c < C::CHUNKS; c++)
@@ -344,21 +339,16 @@ __global__ void __maxnreg__(128)
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::Q_READY));
-            if (ct == 0) PH(8001);
             for (int j = 0; j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
                 if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, err)) break;
-                if (ct == 0) PH(7000 + j * 4);
                 split_tile<SPLIT>(sg + C::OFF_K + ks * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
                 mbar_arrive(bar(C::K_READY + ks));
-                if (ct == 0) PH(7001 + j * 4);
                 if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, err)) break;
-                if (ct == 0) PH(7002 + j * 4);
                 split_tile<SPLIT>(sg + C::OFF_V + vs * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
                 mbar_arrive(bar(C::V_READY + vs));
-                if (ct == 0) PH(7003 + j * 4);
             }
         }
     } else {
@@ -380,7 +370,6 @@ __global__ void __maxnreg__(128)
                 ok = false;
                 break;
             }
-            if (threadIdx.x == 0) PH(4 + j * 8);
             tc_fence_after();
             float s[C::HB];
             {
@@ -454,7 +443,6 @@ __global__ void __maxnreg__(128)
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::P_FULL + bb));
-            if (threadIdx.x == 0) PH(7 + j * 8);
             // Fold the previous block: o = (o + O_blk(j-1)) * corr (both relative to the
             // previous max; corr moves them to m).
             if (j >= 1) {
@@ -473,7 +461,6 @@ __global__ void __maxnreg__(128)
                 }
                 tc_fence_before();
                 mbar_arrive(bar(C::OB_FREE));
-                if (threadIdx.x == 0) PH(5000 + j);
             }
         }
         if (ok && nblk > 0) {
@@ -588,4 +575,3 @@ int device_error(int reset) {
 
 }  // namespace dc
 
-extern "C" int dc_read_phases_fwd(long long *out) { return cudaMemcpyFromSymbol(out, dc::g_phf, sizeof(long long) * 8192) == cudaSuccess ? 0 : 1; }

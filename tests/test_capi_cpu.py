@@ -32,6 +32,18 @@ def test_library_exports_every_declared_symbol():
     assert L.dc_abi_version() == 1
 
 
+def test_library_exports_nothing_undeclared():
+    """Every exported dc_* symbol is part of the header: no debugging or probe entry points."""
+    import subprocess
+    try:
+        out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,
+                             check=True).stdout
+    except (OSError, subprocess.CalledProcessError):
+        pytest.skip("nm is unavailable")
+    exported = {line.split()[-1] for line in out.splitlines() if line.split() and line.split()[-1].startswith("dc_")}
+    assert exported == _declared()
+
+
 def _fake(shape, dtype=_lib.DC_F32, ptr=0x1000):
     v = _lib.DcTensor()
     v.data, v.dtype, v.ndim = ptr, dtype, len(shape)
