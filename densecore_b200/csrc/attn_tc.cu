@@ -73,14 +73,17 @@ struct FwdCfg {
     static constexpr int Q_FULL = 0, Q_READY = 1, K_FULL = 2, K_READY = K_FULL + KST,
                          K_EMPTY = K_READY + KST, V_FULL = K_EMPTY + KST, V_READY = V_FULL + VST,
                          V_EMPTY = V_READY + VST, S_FULL = V_EMPTY + VST, P_FULL = S_FULL + 2,
-                         PV_DONE = P_FULL + 2, PV_DONE_B = PV_DONE + 1, OB_FREE = PV_DONE_B + 2,
-                         XCH = OB_FREE + 1, XSUM = XCH + 2, DRAIN = XSUM + 1, DRAIN_PV = DRAIN + 1,
+                         PV_DONE_B = P_FULL + 2, OB_FREE = PV_DONE_B + 2,
+                         XCH = OB_FREE + 2, XSUM = XCH + 2, DRAIN = XSUM + 1, DRAIN_PV = DRAIN + 1,
                          NBAR = DRAIN_PV + 1;
     static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
-    // TMEM: Q hi | Q lo | 2 x (S / P hi, P lo) | O_blk
+    // TMEM: Q hi | Q lo | 2 x (S / P hi, P lo) | NOB x O_blk. Two O_blk buffers where they fit
+    // (D = 64), so that P_{j+1} V_{j+1} need not wait for the fold of block j.
+    static constexpr int NOB = (4 * D + 4 * BN <= 512) ? 2 : 1;
     static constexpr uint32_t COL_QHI = 0, COL_QLO = D, COL_OB = 2 * D + 4 * BN;
-    static constexpr uint32_t COLS_USED = 3 * D + 4 * BN;
+    static constexpr uint32_t COLS_USED = (2 + NOB) * D + 4 * BN;
+    __host__ __device__ static constexpr uint32_t col_ob(int i) { return COL_OB + (uint32_t)((i % NOB) * D); }
     static constexpr uint32_t TMEM_COLS = COLS_USED <= 256 ? 256 : 512;
     static constexpr int SOFTMAX_THREADS = 256;
     static constexpr int W_PROD = 8, W_MMA = 9, W_CVT = 10, W_PV = 14;
@@ -200,10 +203,10 @@ __global__ void __maxnreg__(128)
             mbar_init(bar(C::S_FULL + s), 1);
             mbar_init(bar(C::P_FULL + s), C::SOFTMAX_THREADS);
         }
-        mbar_init(bar(C::PV_DONE), 1);
         mbar_init(bar(C::PV_DONE_B), 1);
         mbar_init(bar(C::PV_DONE_B + 1), 1);
         mbar_init(bar(C::OB_FREE), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::OB_FREE + 1), C::SOFTMAX_THREADS);
         mbar_init(bar(C::XCH), C::SOFTMAX_THREADS);
         mbar_init(bar(C::XCH + 1), C::SOFTMAX_THREADS);
         mbar_init(bar(C::XSUM), C::SOFTMAX_THREADS);
@@ -301,12 +304,14 @@ __global__ void __maxnreg__(128)
         // ----------------------------------------------------- MMA issuer: O_blk = P V ----
         if (lane == 0) {
             const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
-            const uint32_t d_ob = tmem + C::COL_OB;
             for (int i = 0; i < nblk; i++) {
                 const int bi = i & 1, vs = i % C::VST;
                 if (!mbar_wait(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) break;
                 if (!mbar_wait(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) break;
-                if (i >= 1 && !mbar_wait(bar(C::OB_FREE), (i - 1) & 1, abort, err)) break;
+                // O_blk buffer i % NOB held block i - NOB until the softmax threads folded it.
+                if (i >= C::NOB && !mbar_wait(bar(C::OB_FREE + i % C::NOB), ((i / C::NOB) - 1) & 1, abort, err))
+                    break;
+                const uint32_t d_ob = tmem + C::col_ob(i);
                 tc_fence_after();
                 const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
                 const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
@@ -321,7 +326,6 @@ __global__ void __maxnreg__(128)
 #pragma unroll
                 for (int kk = 0; kk < C::BN / 8; kk++)
                     mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
-                tc_commit(bar(C::PV_DONE));
                 tc_commit(bar(C::PV_DONE_B + bi));
                 tc_commit(bar(C::V_EMPTY + vs));
             }
@@ -446,7 +450,9 @@ __global__ void __maxnreg__(128)
             // Fold the previous block: o = (o + O_blk(j-1)) * corr (both relative to the
             // previous max; corr moves them to m).
             if (j >= 1) {
-                if (!mbar_wait(bar(C::PV_DONE), (j - 1) & 1, abort, err)) {
+                // Per-buffer barrier: with two O_blk buffers PV_j may finish before this wait,
+                // so a single barrier could be two phases ahead of it.
+                if (!mbar_wait(bar(C::PV_DONE_B + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort, err)) {
                     ok = false;
                     break;
                 }
@@ -454,17 +460,17 @@ __global__ void __maxnreg__(128)
 #pragma unroll
                 for (int c = 0; c < C::HD / 16; c++) {
                     uint32_t r[16];
-                    tmem_ld16(tl + C::COL_OB + half * C::HD + 16 * c, r);
+                    tmem_ld16(tl + C::col_ob(j - 1) + half * C::HD + 16 * c, r);
                     tmem_wait_ld();
 #pragma unroll
                     for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(r[x])) * corr;
                 }
                 tc_fence_before();
-                mbar_arrive(bar(C::OB_FREE));
+                mbar_arrive(bar(C::OB_FREE + (j - 1) % C::NOB));
             }
         }
         if (ok && nblk > 0) {
-            ok = mbar_wait(bar(C::PV_DONE), (nblk - 1) & 1, abort, err);
+            ok = mbar_wait(bar(C::PV_DONE_B + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort, err);
             tc_fence_after();
         }
         const bool read_o = __all_sync(0xffffffffu, ok) && nblk > 0;
@@ -473,7 +479,7 @@ __global__ void __maxnreg__(128)
 #pragma unroll
             for (int c = 0; c < C::HD / 32; c++) {
                 uint32_t r[32];
-                tmem_ld32(tl + C::COL_OB + half * C::HD + 32 * c, r);
+                tmem_ld32(tl + C::col_ob(nblk - 1) + half * C::HD + 32 * c, r);
                 tmem_wait_ld();
 #pragma unroll
                 for (int x = 0; x < 32; x++) o[32 * c + x] += __uint_as_float(r[x]);
