@@ -166,7 +166,7 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_b
     }
 }
 
-template <class C, bool SPLIT>
+template <class C, bool SPLIT, bool MASKED>
 __global__ void __maxnreg__(128)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                        const __grid_constant__ CUtensorMap tmv, const TcFwdArgs a) {
@@ -370,6 +370,21 @@ __global__ void __maxnreg__(128)
         bool ok = true;
         for (int j = 0; j < nblk; j++) {
             const int bb = j & 1;
+            const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
+            // Rows past L (zero-filled by TMA) are computed but never stored. Column c is key
+            // k0 + c: valid below S and, under causal masking, up to qrow (one bit per column
+            // keeps the edge path as short as the fast one).
+            const bool edge = MASKED || (k0 + C::HB > p.S) || (p.causal && k0 + C::HB - 1 > q0);
+            uint32_t vbits = 0xFFFFFFFFu;
+            if (edge) {
+                const int64_t lim = (p.causal ? min(p.S, qrow + 1) : p.S) - k0;
+                const int n = !row_ok || lim <= 0 ? 0 : (lim >= C::HB ? C::HB : (int)lim);
+                vbits = n == 0 ? 0u : (0xFFFFFFFFu >> (32 - n));
+            }
+            // The user mask's values for these columns, loaded before the wait for S so that
+            // the wait hides their latency.
+            float mk[MASKED ? C::HB : 1];
+            if constexpr (MASKED) mask_run<C::HB>(p, b, h, qrow, k0, p.ms[3], vbits, mk);
             if (!mbar_wait(bar(C::S_FULL + bb), (j >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
@@ -383,9 +398,6 @@ __global__ void __maxnreg__(128)
 #pragma unroll
                 for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(r[x]);
             }
-            const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
-            // Rows past L (zero-filled by TMA) are computed but never stored.
-            const bool edge = (k0 + C::HB > p.S) || (p.causal && k0 + C::HB - 1 > q0) || p.mask_kind != MASK_NONE;
             float bmax = -INFINITY;
             if (!edge) {
 #pragma unroll
@@ -394,21 +406,11 @@ __global__ void __maxnreg__(128)
                     bmax = fmaxf(bmax, s[c]);
                 }
             } else {
-                // Column c is key k0 + c: valid below S and, under causal masking, up to qrow.
-                // One bit per column keeps this path as short as the fast one.
-                const int64_t lim = (p.causal ? min(p.S, qrow + 1) : p.S) - k0;
-                const int n = !row_ok || lim <= 0 ? 0 : (lim >= C::HB ? C::HB : (int)lim);
-                const uint32_t vbits = n == 0 ? 0u : (0xFFFFFFFFu >> (32 - n));
-#pragma unroll
-                for (int c = 0; c < C::HB; c++) s[c] *= a.scale_log2;
-                if (p.mask_kind != MASK_NONE) {
-#pragma unroll
-                    for (int c = 0; c < C::HB; c++)
-                        if ((vbits >> c) & 1u) s[c] += mask_value(p, b, h, qrow, k0 + c) * LOG2E;
-                }
 #pragma unroll
                 for (int c = 0; c < C::HB; c++) {
-                    s[c] = ((vbits >> c) & 1u) ? s[c] : -INFINITY;
+                    float x = s[c] * a.scale_log2;
+                    if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                    s[c] = ((vbits >> c) & 1u) ? x : -INFINITY;
                     bmax = fmaxf(bmax, s[c]);
                 }
             }
@@ -530,7 +532,9 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     a.scale_log2 = p.scale * LOG2E;
     a.err = device_error_word();
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
-    auto kernel = split ? attn_fwd_tc_kernel<C, true> : attn_fwd_tc_kernel<C, false>;
+    const bool masked = p.mask_kind != MASK_NONE;
+    auto kernel = split ? (masked ? attn_fwd_tc_kernel<C, true, true> : attn_fwd_tc_kernel<C, true, false>)
+                        : (masked ? attn_fwd_tc_kernel<C, false, true> : attn_fwd_tc_kernel<C, false, false>);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
     dim3 grid((unsigned)a.num_q_tiles, (unsigned)p.H, (unsigned)p.B);

@@ -285,7 +285,7 @@ static_assert(SMEM <= 232448, "smem");
 // tm_k / tm_v: (64, S, Hkv, S2*B) over the hi / lo copies (lo at batch B + b), box 128 rows;
 // tm_q* / tm_do*: (64, L, H, S2*B), box 32 rows, K-major (128-byte swizzle) or MN-major
 // (32-byte-atom swizzle).
-template <bool SPLIT>
+template <bool SPLIT, bool MASKED>
 __global__ void __maxnreg__(168)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_qmn,
@@ -510,27 +510,28 @@ __global__ void __maxnreg__(168)
             int64_t h, q0;
             blk_coords(i, h, q0);
             const float nxt = i + 1 < nblk ? rowvals(i + 1) : 0.0f;
+            // Column c is query base + c: valid below L and, under causal masking, from `key` on.
+            const int64_t base = q0 + cb;
+            const bool edge = MASKED || !key_ok || q0 + BLK > p.L || (p.causal && key > q0);
+            uint32_t vbits = 0xFFFFu;
+            if (edge) vbits = key_ok ? col_bits(p.causal ? key - base : 0, p.L - base) : 0u;
+            // The user mask down this key's column, loaded before the wait for S.
+            float mk[MASKED ? 16 : 1];
+            if constexpr (MASKED) mask_run<16>(p, b, h, base, key, p.ms[2], vbits, mk);
             if (!warp_wait(bar(S_FULL + bb), (i >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const bool edge = !key_ok || q0 + BLK > p.L || (p.causal && key > q0) || p.mask_kind != MASK_NONE;
             uint32_t sr[16], dr[16], phi[16], plo[16];
             tmem_ld16(tl + c_s(bb) + cb, sr);
             tmem_ld16(tl + c_dp(bb) + cb, dr);
             tmem_wait_ld();
-            // Column c is query base + c: valid below L and, under causal masking, from `key` on.
-            const int64_t base = q0 + cb;
-            uint32_t vbits = 0xFFFFu;
-            if (edge) vbits = key_ok ? col_bits(p.causal ? key - base : 0, p.L - base) : 0u;
 #pragma unroll
-            for (int c = 0; c < 16; c++) sr[c] = __float_as_uint(__uint_as_float(sr[c]) * a.scale_log2);
-            if (p.mask_kind != MASK_NONE) {
-#pragma unroll
-                for (int c = 0; c < 16; c++)
-                    if ((vbits >> c) & 1u)
-                        sr[c] = __float_as_uint(__uint_as_float(sr[c]) + mask_value(p, b, h, base + c, key) * LOG2E);
+            for (int c = 0; c < 16; c++) {
+                float x = __uint_as_float(sr[c]) * a.scale_log2;
+                if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                sr[c] = __float_as_uint(x);
             }
 #pragma unroll
             for (int c = 0; c < 16; c++) {
@@ -606,7 +607,7 @@ static_assert(SMEM <= 232448, "smem");
 
 // tm_q / tm_do: (64, L, H, S2*B), box 128 rows; tm_kk / tm_kmn / tm_vk: (64, S, Hkv, S2*B),
 // box 32 rows.
-template <bool SPLIT>
+template <bool SPLIT, bool MASKED>
 __global__ void __maxnreg__(168)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_kk, const __grid_constant__ CUtensorMap tm_kmn,
@@ -805,27 +806,28 @@ __global__ void __maxnreg__(168)
         for (int j = 0; ok && j < nblk; j++) {
             const int bb = j & 1;
             const int64_t kb0 = (int64_t)j * BLK;
+            // Column c is key base + c: valid below S and, under causal masking, up to q.
+            const int64_t base = kb0 + cb;
+            const bool edge = MASKED || !row_ok || kb0 + BLK > p.S || (p.causal && kb0 + BLK - 1 > q0);
+            uint32_t vbits = 0xFFFFu;
+            if (edge) vbits = row_ok ? col_bits(0, (p.causal ? min(p.S, q + 1) : p.S) - base) : 0u;
+            // The user mask along this query's row, loaded before the wait for S.
+            float mk[MASKED ? 16 : 1];
+            if constexpr (MASKED) mask_run<16>(p, b, h, q, base, p.ms[3], vbits, mk);
             if (!warp_wait(bar(S_FULL + bb), (j >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const bool edge = !row_ok || kb0 + BLK > p.S || (p.causal && kb0 + BLK - 1 > q0) || p.mask_kind != MASK_NONE;
             uint32_t sr[16], dr[16];
             tmem_ld16(tl + c_s(bb) + cb, sr);
             tmem_ld16(tl + c_dp(bb) + cb, dr);
             tmem_wait_ld();
-            // Column c is key base + c: valid below S and, under causal masking, up to q.
-            const int64_t base = kb0 + cb;
-            uint32_t vbits = 0xFFFFu;
-            if (edge) vbits = row_ok ? col_bits(0, (p.causal ? min(p.S, q + 1) : p.S) - base) : 0u;
 #pragma unroll
-            for (int c = 0; c < 16; c++) sr[c] = __float_as_uint(__uint_as_float(sr[c]) * a.scale_log2);
-            if (p.mask_kind != MASK_NONE) {
-#pragma unroll
-                for (int c = 0; c < 16; c++)
-                    if ((vbits >> c) & 1u)
-                        sr[c] = __float_as_uint(__uint_as_float(sr[c]) + mask_value(p, b, h, q, base + c) * LOG2E);
+            for (int c = 0; c < 16; c++) {
+                float x = __uint_as_float(sr[c]) * a.scale_log2;
+                if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                sr[c] = __float_as_uint(x);
             }
 #pragma unroll
             for (int c = 0; c < 16; c++) {
@@ -916,6 +918,7 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     // Strides (batch, head, row) of the contiguous hi / lo copies.
     const int64_t qst[3] = {p.H * p.L * D, p.L * D, D}, kst[3] = {p.Hkv * p.S * D, p.S * D, D};
     const int64_t nb = S2 * p.B;
+    const bool masked = p.mask_kind != MASK_NONE;
     if (p.S > 0) {
         CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
         st = make_tmap(&tk, pa.khl, D, p.S, p.Hkv, nb, kst, TILE);
@@ -925,7 +928,8 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         if (!st) st = make_tmap(&tdok, pa.dohl, D, p.L, p.H, nb, qst, BLK);
         if (!st) st = make_tmap(&tdomn, pa.dohl, D, p.L, p.H, nb, qst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (st) return st;
-        auto kernel = split ? attn_bwd_dkdv_tc_kernel<true> : attn_bwd_dkdv_tc_kernel<false>;
+        auto kernel = split ? (masked ? attn_bwd_dkdv_tc_kernel<true, true> : attn_bwd_dkdv_tc_kernel<true, false>)
+                            : (masked ? attn_bwd_dkdv_tc_kernel<false, true> : attn_bwd_dkdv_tc_kernel<false, false>);
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
         const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B);
@@ -941,7 +945,8 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         if (!st) st = make_tmap(&tkmn, pa.khl, D, p.S, p.Hkv, nb, kst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (!st) st = make_tmap(&tvk, pa.vhl, D, p.S, p.Hkv, nb, kst, BLK);
         if (st) return st;
-        auto kernel = split ? attn_bwd_dq_tc_kernel<true> : attn_bwd_dq_tc_kernel<false>;
+        auto kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true> : attn_bwd_dq_tc_kernel<true, false>)
+                            : (masked ? attn_bwd_dq_tc_kernel<false, true> : attn_bwd_dq_tc_kernel<false, false>);
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
         const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B);

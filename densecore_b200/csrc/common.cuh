@@ -44,6 +44,66 @@ __device__ __forceinline__ float mask_value(const AttnProblem &p, int64_t b, int
     return static_cast<const uint8_t *>(p.mask)[off] ? 0.0f : -INFINITY;
 }
 
+// N mask values of (b, h) starting at element (i, j) and stepping `step` elements (the key
+// stride for a run along a row, the query stride for a run along a column), for the entries
+// whose bit is set in `bits` (the others read as 0). Float masks give their value, bool masks 0
+// or -inf. A run with unit step on a 16-byte (float) or 4-byte (bool) boundary loads four
+// values at a time; a zero step loads one value.
+template <int N>
+__device__ __forceinline__ void mask_run(const AttnProblem &p, int64_t b, int64_t h, int64_t i, int64_t j,
+                                         int64_t step, uint32_t bits, float (&out)[N]) {
+    const int64_t off = b * p.ms[0] + h * p.ms[1] + i * p.ms[2] + j * p.ms[3];
+    if (p.mask_kind == MASK_FLOAT) {
+        const float *m = static_cast<const float *>(p.mask) + off;
+        if (step == 0) {
+            const float v = bits ? *m : 0.0f;
+#pragma unroll
+            for (int c = 0; c < N; c++) out[c] = v;
+        } else if (step == 1 && (reinterpret_cast<uintptr_t>(m) & 15u) == 0) {
+#pragma unroll
+            for (int g = 0; g < N / 4; g++) {
+                if (((bits >> (4 * g)) & 15u) == 15u) {
+                    const float4 v = *reinterpret_cast<const float4 *>(m + 4 * g);
+                    out[4 * g] = v.x;
+                    out[4 * g + 1] = v.y;
+                    out[4 * g + 2] = v.z;
+                    out[4 * g + 3] = v.w;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) out[4 * g + e] = ((bits >> (4 * g + e)) & 1u) ? m[4 * g + e] : 0.0f;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < N; c++) out[c] = ((bits >> c) & 1u) ? m[c * step] : 0.0f;
+        }
+    } else {
+        const uint8_t *m = static_cast<const uint8_t *>(p.mask) + off;
+        if (step == 0) {
+            const float v = (bits && !*m) ? -INFINITY : 0.0f;
+#pragma unroll
+            for (int c = 0; c < N; c++) out[c] = v;
+        } else if (step == 1 && (reinterpret_cast<uintptr_t>(m) & 3u) == 0) {
+#pragma unroll
+            for (int g = 0; g < N / 4; g++) {
+                uint32_t w = 0x01010101u;
+                if (((bits >> (4 * g)) & 15u) == 15u) {
+                    w = *reinterpret_cast<const uint32_t *>(m + 4 * g);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        if ((bits >> (4 * g + e)) & 1u) w = (w & ~(0xFFu << (8 * e))) | ((uint32_t)m[4 * g + e] << (8 * e));
+                }
+#pragma unroll
+                for (int e = 0; e < 4; e++) out[4 * g + e] = ((w >> (8 * e)) & 0xFFu) ? 0.0f : -INFINITY;
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < N; c++) out[c] = (((bits >> c) & 1u) && !m[c * step]) ? -INFINITY : 0.0f;
+        }
+    }
+}
+
 // Whether key j is visible to query row i under top-left causal alignment.
 __device__ __forceinline__ bool causal_visible(int causal, int64_t i, int64_t j) {
     return !causal || j <= i;
