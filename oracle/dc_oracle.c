@@ -22,6 +22,9 @@
  *   src/sleef.rs:310-322,499-515    SLEEF xexpf (ldexp2 / pow2i helpers)
  *   src/sleef.rs:1184-1196          libm expf / logf (glibc here, as on any Linux build)
  *   src/sleef.rs:1227-1256          exp_u20 (Arm Optimized Routines vexpq_f32_u20)
+ *   src/torch_random.rs:9-13,43-97  mt19937: seeding, twist, tempering, random, random64
+ *   src/torch_random.rs:106-110     uniform_real_distribution<double> (53 bits)
+ *   src/torch_random.rs:242-254     bernoulli with a scalar p (the dropout keep draw)
  *
  * Rounding rules that matter for parity: build with -ffp-contract=off so that no a*b+c is
  * fused behind our back; fmaf() is used exactly where the Rust code calls mul_add (or a
@@ -665,5 +668,64 @@ DCO_EXPORT void dco_bmm(const float *a, const float *b, int64_t bs, int64_t rows
             sgemm_portable(0, 0, (size_t)cols, (size_t)rows, (size_t)k, 1.0f, m, (size_t)cols, s,
                            (size_t)k, 0.0f, o, (size_t)cols);
         }
+    }
+}
+
+/* ------------------------------------------------ PyTorch's CPU generator (mt19937) -- */
+/* Engine state as DenseCore keeps it (src/torch_random.rs:19-26): 624 state words, then
+ * `left` and `next`. The seed and the cached normal samples are not needed by dropout. */
+enum { MT_N = 624, MT_M = 397 };
+#define MT_MATRIX_A 0x9908b0dfu
+#define MT_UMASK 0x80000000u
+#define MT_LMASK 0x7fffffffu
+
+/* manual_seed (torch_random.rs:43-56): Knuth's multiplier 1812433253, left = 1, next = 0. */
+DCO_EXPORT void dco_mt_seed(uint64_t seed, uint32_t st[MT_N + 2]) {
+    st[0] = (uint32_t)seed;
+    for (uint32_t j = 1; j < MT_N; j++) st[j] = 1812433253u * (st[j - 1] ^ (st[j - 1] >> 30)) + j;
+    st[MT_N] = 1;     /* left */
+    st[MT_N + 1] = 0; /* next */
+}
+
+static inline uint32_t mt_twist(uint32_t u, uint32_t v) {
+    return (((u & MT_UMASK) | (v & MT_LMASK)) >> 1) ^ ((v & 1u) ? MT_MATRIX_A : 0u);
+}
+
+/* next_state (torch_random.rs:66-77), in place. */
+static void mt_next_state(uint32_t *s) {
+    int j;
+    for (j = 0; j < MT_N - MT_M; j++) s[j] = s[j + MT_M] ^ mt_twist(s[j], s[j + 1]);
+    for (; j < MT_N - 1; j++) s[j] = s[j + MT_M - MT_N] ^ mt_twist(s[j], s[j + 1]);
+    s[MT_N - 1] = s[MT_M - 1] ^ mt_twist(s[MT_N - 1], s[0]);
+}
+
+/* random (torch_random.rs:79-91): decrement left, twist when it reaches 0, temper. */
+static uint32_t mt_random(uint32_t *st) {
+    if (--st[MT_N] == 0) {
+        mt_next_state(st);
+        st[MT_N] = MT_N;
+        st[MT_N + 1] = 0;
+    }
+    uint32_t y = st[st[MT_N + 1]++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+}
+
+DCO_EXPORT void dco_mt_random(uint32_t *st, int64_t n, uint32_t *out) {
+    for (int64_t i = 0; i < n; i++) out[i] = mt_random(st);
+}
+
+/* bernoulli(n, p) (torch_random.rs:242-254): each draw is uniform_real_distribution<double>
+ * (:106-110): random64 = (first random << 32) | second, its low 53 bits times 2^-53, then
+ * fma(x, 1 - 0, 0) = x; the element is 1 when that is below p. Written as packed bits:
+ * element e is bit e % 32 of word e / 32 (the caller zeroes the words). */
+DCO_EXPORT void dco_mt_bernoulli_bits(uint32_t *st, int64_t n, double p, uint32_t *bits) {
+    for (int64_t e = 0; e < n; e++) {
+        uint64_t hi = mt_random(st), lo = mt_random(st);
+        double x = (double)(((hi << 32) | lo) & ((1ull << 53) - 1)) * (1.0 / (double)(1ull << 53));
+        if (fma(x, 1.0 - 0.0, 0.0) < p) bits[e >> 5] |= 1u << (e & 31);
     }
 }
