@@ -22,7 +22,8 @@ DC_PREC_3XTF32, DC_PREC_TF32, DC_PREC_FP32 = 0, 1, 2
 # Every entry point include/densecore_sdpa.h declares.
 EXPORTS = ("dc_sdpa_fwd", "dc_sdpa_bwd_workspace_size", "dc_sdpa_bwd", "dc_sdpa_decode_workspace_size",
            "dc_sdpa_decode_default_splits", "dc_sdpa_decode", "dc_sdpa_decode_noalloc", "dc_attn_merge", "dc_attn_probs",
-           "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report", "dc_device_status")
+           "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report", "dc_device_status",
+           "dc_dropout_keep_bits", "dc_rng_skip", "dc_sdpa_fwd_dropout", "dc_sdpa_bwd_dropout", "dc_attn_probs_dropout")
 
 
 class DcTensor(ctypes.Structure):
@@ -68,6 +69,17 @@ def load():
         L.dc_attn_merge.restype = i
         L.dc_attn_probs.argtypes = [_P, _P, _P, _P, i, i, d, i, _P, vp]
         L.dc_attn_probs.restype = i
+        u32p, f = ctypes.POINTER(ctypes.c_uint32), ctypes.c_float
+        L.dc_dropout_keep_bits.argtypes = [vp, vp, i64, d, vp, vp]
+        L.dc_dropout_keep_bits.restype = i
+        L.dc_rng_skip.argtypes = [u32p, ctypes.c_uint64, u32p]
+        L.dc_rng_skip.restype = i
+        L.dc_sdpa_fwd_dropout.argtypes = [_P, _P, _P, _P, i, i, d, i, vp, f, _P, _P, vp]
+        L.dc_sdpa_fwd_dropout.restype = i
+        L.dc_sdpa_bwd_dropout.argtypes = [_P] * 7 + [i, i, d, i, vp, f, _P, _P, _P, vp, sz, vp]
+        L.dc_sdpa_bwd_dropout.restype = i
+        L.dc_attn_probs_dropout.argtypes = [_P, _P, _P, _P, i, i, d, vp, f, i, _P, vp]
+        L.dc_attn_probs_dropout.restype = i
         L.dc_last_error.argtypes = []
         L.dc_last_error.restype = ctypes.c_char_p
         L.dc_abi_version.argtypes = []

@@ -85,6 +85,47 @@ def _flash_attention_backward(grad_out, q, k, v, out, lse, causal, scale=None, m
     return gq, gk, gv
 
 
+def _flash_attention_dropout(q, k, v, causal, scale, mask, keep, keep_scale, precision=None):
+    """Forward with dropout on the weights (dc_sdpa_fwd_dropout): (out, lse). ``keep`` holds
+    the packed keep bits of the (B, H, L, S) weights, ``keep_scale`` = float32(1/(1-p))."""
+    L = _lib.load()
+    dev = _require_cuda(q, k, v, mask, keep)
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("flash attention takes (B, H, L, E) tensors")
+    B, H, Lq = q.shape[:3]
+    out = torch.empty((B, H, Lq, v.shape[3]), device=dev, dtype=torch.float32)
+    lse = torch.empty((B, H, Lq), device=dev, dtype=torch.float32)
+    prec = precision_code() if precision is None else precision
+    has, sc = _scale_args(scale)
+    with torch.cuda.device(dev):
+        vs = [_lib.view(t) for t in (q, k, v, mask, out, lse)]
+        st = L.dc_sdpa_fwd_dropout(*[_lib.ref(x) for x in vs[:4]], int(bool(causal)), has, sc, prec, keep.data_ptr(),
+                                   float(keep_scale), _lib.ref(vs[4]), _lib.ref(vs[5]), _lib.stream_of(q))
+    _lib.check(st, "flash attention forward failed")
+    return out, lse
+
+
+def _flash_attention_dropout_backward(grad_out, q, k, v, out, lse, causal, scale, mask, keep, keep_scale,
+                                      precision=None):
+    """Backward of :func:`_flash_attention_dropout` (dc_sdpa_bwd_dropout): (grad_q, grad_k, grad_v)."""
+    L = _lib.load()
+    dev = _require_cuda(grad_out, q, k, v, out, lse, mask, keep)
+    gq = torch.empty(q.shape, device=dev, dtype=torch.float32)
+    gk = torch.empty(k.shape, device=dev, dtype=torch.float32)
+    gv = torch.empty(v.shape, device=dev, dtype=torch.float32)
+    prec = precision_code() if precision is None else precision
+    has, sc = _scale_args(scale)
+    with torch.cuda.device(dev):
+        nbytes = L.dc_sdpa_bwd_workspace_size(q.shape[0], q.shape[1], q.shape[2])
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        views = [_lib.view(t) for t in (grad_out, q, k, v, out, lse, mask, gq, gk, gv)]
+        st = L.dc_sdpa_bwd_dropout(*[_lib.ref(x) for x in views[:7]], int(bool(causal)), has, sc, prec,
+                                   keep.data_ptr(), float(keep_scale), *[_lib.ref(x) for x in views[7:]],
+                                   ws.data_ptr(), ws.numel(), _lib.stream_of(q))
+    _lib.check(st, "flash attention backward failed")
+    return gq, gk, gv
+
+
 def _decode(q, k, v, scale=None, mask=None, num_splits=0, workspace=None):
     """Split-KV decode for q_len == 1 (dc_sdpa_decode): (out, lse)."""
     L = _lib.load()
@@ -115,10 +156,11 @@ def _attn_merge(out_acc, lse_acc, out_part, lse_part):
     return out_acc, lse_acc
 
 
-def _attn_probs(q, k, lse, causal, scale=None, mask=None, average_heads=True):
-    """softmax(scale q k^T + mask) from the forward's lse; (B,L,S) head mean or (B,H,L,S)."""
+def _attn_probs(q, k, lse, causal, scale=None, mask=None, average_heads=True, keep=None, keep_scale=0.0):
+    """softmax(scale q k^T + mask) from the forward's lse; (B,L,S) head mean or (B,H,L,S).
+    With ``keep`` (packed dropout keep bits) each probability is times its dropout factor."""
     L = _lib.load()
-    dev = _require_cuda(q, k, lse, mask)
+    dev = _require_cuda(q, k, lse, mask, keep)
     B, H, Lq = q.shape[:3]
     S = k.shape[2]
     shape = (B, Lq, S) if average_heads else (B, H, Lq, S)
@@ -126,8 +168,13 @@ def _attn_probs(q, k, lse, causal, scale=None, mask=None, average_heads=True):
     has, sc = _scale_args(scale)
     with torch.cuda.device(dev):
         vs = [_lib.view(t) for t in (q, k, lse, mask, probs)]
-        st = L.dc_attn_probs(*[_lib.ref(x) for x in vs[:4]], int(bool(causal)), has, sc,
-                             int(bool(average_heads)), _lib.ref(vs[4]), _lib.stream_of(q))
+        if keep is None:
+            st = L.dc_attn_probs(*[_lib.ref(x) for x in vs[:4]], int(bool(causal)), has, sc,
+                                 int(bool(average_heads)), _lib.ref(vs[4]), _lib.stream_of(q))
+        else:
+            st = L.dc_attn_probs_dropout(*[_lib.ref(x) for x in vs[:4]], int(bool(causal)), has, sc, keep.data_ptr(),
+                                         float(keep_scale), int(bool(average_heads)), _lib.ref(vs[4]),
+                                         _lib.stream_of(q))
     _lib.check(st, "attention probabilities failed")
     return probs
 

@@ -10,6 +10,10 @@
 //   * backward recomputes P = exp(s - lse) (:363-374), dV += P^T dO, dP = dO V^T,
 //     dS = P (dP - delta) with delta = sum(dO * O) per row (:327-330, :411-416),
 //     dQ += scale dS K, dK += scale dS^T Q (:417-446).
+// With dropout (AttnProblem::keep) the weights that meet V are P * Z, Z = keep_scale or 0 per
+// element, while the softmax normaliser and lse stay those of P -- DenseCore's math path
+// multiplies the softmax output by the noise (python/densecore/functional.py:336-340). The
+// backward then uses dV += (P Z)^T dO and dS = P (Z dP - delta).
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -86,13 +90,14 @@ __global__ void __launch_bounds__(FW_WARPS *WARP) fwd_simt_kernel(AttnProblem p)
         for (int r = 0; r < FW_RPW; r++) {
             const int rr = warp * FW_RPW + r;
             const int64_t i = q0 + rr;
-            float s = -INFINITY;
+            float s = -INFINITY, z = 1.0f;
             if (i < p.L && kj < p.S && causal_visible(p.causal, i, kj)) {
                 const float *qr = sq + rr * E, *kr = sk + lane * KP;
                 float dot = 0.0f;
                 for (int d = 0; d < E; d++) dot = fmaf(qr[d], kr[d], dot);
                 s = dot * p.scale;
                 if (p.mask_kind) s += mask_value(p, b, h, i, kj);
+                z = keep_factor(p, b, h, i, kj);
             }
             const float m_new = fmaxf(m[r], warp_max(s));
             if (m_new == -INFINITY) continue;  // the block adds nothing (warp-uniform)
@@ -100,10 +105,11 @@ __global__ void __launch_bounds__(FW_WARPS *WARP) fwd_simt_kernel(AttnProblem p)
             const float corr = expf(m[r] - m_new);
             l[r] = fmaf(l[r], corr, warp_sum(pj));
             m[r] = m_new;
+            const float pz = pj * z;
 #pragma unroll
             for (int t = 0; t < T; t++) acc[r][t] *= corr;
             for (int j = 0; j < FW_BK; j++) {
-                const float pb = __shfl_sync(0xffffffffu, pj, j);
+                const float pb = __shfl_sync(0xffffffffu, pz, j);
                 if (pb == 0.0f) continue;
                 const float *vr = sv + j * VP;
 #pragma unroll
@@ -216,7 +222,9 @@ __global__ void __launch_bounds__(BK_WARPS *WARP) bwd_dkdv_simt_kernel(AttnProbl
                     const float *dr = sdo + warp * Ev, *vr = sv + lane * VP;
                     float dp = 0.0f;
                     for (int d = 0; d < Ev; d++) dp = fmaf(dr[d], vr[d], dp);
-                    ds = pr * (dp - srow[2 * warp + 1]);
+                    const float z = keep_factor(p, b, h, i, kj);
+                    ds = pr * (dp * z - srow[2 * warp + 1]);
+                    pr *= z;
                 }
                 sP[warp * BK_KEYS + lane] = pr;
                 sDS[warp * BK_KEYS + lane] = ds;
@@ -306,7 +314,7 @@ __global__ void __launch_bounds__(BK_WARPS *WARP) bwd_dq_simt_kernel(AttnProblem
             const float *dr = sdo + warp * Ev, *vr = sv + lane * VP;
             float dp = 0.0f;
             for (int d = 0; d < Ev; d++) dp = fmaf(dr[d], vr[d], dp);
-            ds = pr * (dp - delta_i);
+            ds = pr * (dp * keep_factor(p, b, h, i, kj) - delta_i);
         }
         sDS[warp * BK_KEYS + lane] = ds;
         __syncwarp();
@@ -332,7 +340,8 @@ __global__ void __launch_bounds__(BK_WARPS *WARP) bwd_dq_simt_kernel(AttnProblem
 }
 
 // ------------------------------------------------------------- probabilities ----
-// probs[b, (h,) i, j] = exp(scale q.k + mask - lse); averaged over heads when requested.
+// probs[b, (h,) i, j] = exp(scale q.k + mask - lse) (times the dropout factor); averaged over
+// heads when requested.
 __global__ void probs_kernel(AttnProblem p, float *probs, int64_t ps0, int64_t ps1, int64_t ps2,
                              int64_t ps3, int average) {
     const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -349,7 +358,7 @@ __global__ void probs_kernel(AttnProblem p, float *probs, int64_t ps0, int64_t p
             for (int64_t d = 0; d < p.E; d++) dot = fmaf(qr[d * p.qs[3]], kr[d * p.ks[3]], dot);
             float s = dot * p.scale;
             if (p.mask_kind) s += mask_value(p, b, h, i, j);
-            pr = expf(s - p.lse[b * p.ls[0] + h * p.ls[1] + i * p.ls[2]]);
+            pr = expf(s - p.lse[b * p.ls[0] + h * p.ls[1] + i * p.ls[2]]) * keep_factor(p, b, h, i, j);
         }
         if (average)
             avg += pr;

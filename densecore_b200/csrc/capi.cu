@@ -243,14 +243,27 @@ int dc_sdpa_fwd_path(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor
     return pick_forward_path(p, precision);
 }
 
-int dc_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
-                const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
-                dc_tensor_t *out, dc_tensor_t *lse, void *stream) {
+// Dropout arguments shared by the *_dropout entry points: the keep bits of B*H*L*S elements.
+static int set_keep(AttnProblem &p, const uint32_t *keep_bits, float keep_scale) {
+    if (p.B * p.H * p.L * p.S > 0 && !keep_bits)
+        return fail(DC_ERR_VALUE, "dropout: keep_bits must not be null");
+    if ((reinterpret_cast<uintptr_t>(keep_bits) & 3u) != 0)
+        return fail(DC_ERR_VALUE, "dropout: keep_bits must be 4-byte aligned");
+    p.keep = keep_bits;
+    p.keep_scale = keep_scale;
+    return DC_OK;
+}
+
+static int sdpa_fwd_impl(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                         const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                         const uint32_t *keep_bits, float keep_scale, bool dropout, dc_tensor_t *out,
+                         dc_tensor_t *lse, void *stream) {
     AttnProblem p;
     int st = fill_problem(q, k, v, causal, has_scale, scale, p);
     if (!st) st = fill_mask(mask, p);
     if (!st) st = check_out(out, lse, p);
     if (!st) st = check_precision(precision);
+    if (!st && dropout) st = set_keep(p, keep_bits, keep_scale);
     if (st) return st;
     p.out = static_cast<float *>(out->data);
     p.lse = static_cast<float *>(lse->data);
@@ -259,6 +272,7 @@ int dc_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v
     if (p.B == 0 || p.H == 0 || p.L == 0) return DC_OK;
     if ((st = device_ok())) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dropout) return simt_forward(p, s);
     switch (pick_forward_path(p, precision)) {
         case 2: {
             const int splits = decode_pick_splits(p);
@@ -275,21 +289,38 @@ int dc_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v
     }
 }
 
+int dc_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                dc_tensor_t *out, dc_tensor_t *lse, void *stream) {
+    return sdpa_fwd_impl(q, k, v, mask, causal, has_scale, scale, precision, nullptr, 0.0f, false, out, lse,
+                         stream);
+}
+
+int dc_sdpa_fwd_dropout(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                        const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                        const uint32_t *keep_bits, float keep_scale, dc_tensor_t *out, dc_tensor_t *lse,
+                        void *stream) {
+    return sdpa_fwd_impl(q, k, v, mask, causal, has_scale, scale, precision, keep_bits, keep_scale, true, out,
+                         lse, stream);
+}
+
 size_t dc_sdpa_bwd_workspace_size(int64_t batch, int64_t heads, int64_t q_len) {
     const size_t n = (size_t)(batch > 0 ? batch : 0) * (heads > 0 ? heads : 0) *
                      (q_len > 0 ? q_len : 0);
     return ((n * sizeof(float) + 255) / 256) * 256;
 }
 
-int dc_sdpa_bwd(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tensor_t *k,
-                const dc_tensor_t *v, const dc_tensor_t *out, const dc_tensor_t *lse,
-                const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
-                dc_tensor_t *grad_q, dc_tensor_t *grad_k, dc_tensor_t *grad_v, void *workspace,
-                size_t workspace_bytes, void *stream) {
+static int sdpa_bwd_impl(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tensor_t *k,
+                         const dc_tensor_t *v, const dc_tensor_t *out, const dc_tensor_t *lse,
+                         const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                         const uint32_t *keep_bits, float keep_scale, bool dropout, dc_tensor_t *grad_q,
+                         dc_tensor_t *grad_k, dc_tensor_t *grad_v, void *workspace, size_t workspace_bytes,
+                         void *stream) {
     AttnProblem p;
     int st = fill_problem(q, k, v, causal, has_scale, scale, p);
     if (!st) st = fill_mask(mask, p);
     if (!st) st = check_precision(precision);
+    if (!st && dropout) st = set_keep(p, keep_bits, keep_scale);
     if (st) return st;
     // src/lib.rs:658-662: grad and out shaped like the output, lse (B, H, L).
     if (!is_f32(grad_out, 4) || !sizes_are(grad_out, {p.B, p.H, p.L, p.Ev}) || !is_f32(out, 4) ||
@@ -322,9 +353,40 @@ int dc_sdpa_bwd(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tens
         return st;
     g.delta = static_cast<float *>(ws.ptr);
     // The tensor-core backward computes delta in its own pre-pass.
-    if (precision != DC_PREC_FP32 && tc_backward_supported(p, g)) return tc_backward(p, g, precision, s);
+    if (!dropout && precision != DC_PREC_FP32 && tc_backward_supported(p, g)) return tc_backward(p, g, precision, s);
     if (p.L > 0 && (st = bwd_delta(p, g, s))) return st;
     return simt_backward(p, g, s);
+}
+
+int dc_sdpa_bwd(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tensor_t *k,
+                const dc_tensor_t *v, const dc_tensor_t *out, const dc_tensor_t *lse,
+                const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                dc_tensor_t *grad_q, dc_tensor_t *grad_k, dc_tensor_t *grad_v, void *workspace,
+                size_t workspace_bytes, void *stream) {
+    return sdpa_bwd_impl(grad_out, q, k, v, out, lse, mask, causal, has_scale, scale, precision, nullptr, 0.0f,
+                         false, grad_q, grad_k, grad_v, workspace, workspace_bytes, stream);
+}
+
+int dc_sdpa_bwd_dropout(const dc_tensor_t *grad_out, const dc_tensor_t *q, const dc_tensor_t *k,
+                        const dc_tensor_t *v, const dc_tensor_t *out, const dc_tensor_t *lse,
+                        const dc_tensor_t *mask, int causal, int has_scale, double scale, int precision,
+                        const uint32_t *keep_bits, float keep_scale, dc_tensor_t *grad_q, dc_tensor_t *grad_k,
+                        dc_tensor_t *grad_v, void *workspace, size_t workspace_bytes, void *stream) {
+    return sdpa_bwd_impl(grad_out, q, k, v, out, lse, mask, causal, has_scale, scale, precision, keep_bits,
+                         keep_scale, true, grad_q, grad_k, grad_v, workspace, workspace_bytes, stream);
+}
+
+int dc_dropout_keep_bits(const uint32_t *state_in, uint32_t *state_out, int64_t n, double keep_prob,
+                         uint32_t *bits, void *stream) {
+    if (n > 0) {
+        int st = device_ok();
+        if (st) return st;
+    }
+    return keep_bits(state_in, state_out, n, keep_prob, bits, static_cast<cudaStream_t>(stream));
+}
+
+int dc_rng_skip(const uint32_t *state_in, uint64_t outputs, uint32_t *state_out) {
+    return rng_skip(state_in, outputs, state_out);
 }
 
 size_t dc_sdpa_decode_workspace_size(int64_t batch, int64_t heads, int64_t head_dim_v,
@@ -430,12 +492,14 @@ int dc_attn_merge(dc_tensor_t *out_acc, dc_tensor_t *lse_acc, const dc_tensor_t 
                  static_cast<cudaStream_t>(stream));
 }
 
-int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *lse,
-                  const dc_tensor_t *mask, int causal, int has_scale, double scale,
-                  int average_heads, dc_tensor_t *probs, void *stream) {
+static int attn_probs_impl(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *lse,
+                           const dc_tensor_t *mask, int causal, int has_scale, double scale,
+                           const uint32_t *keep_bits, float keep_scale, bool dropout, int average_heads,
+                           dc_tensor_t *probs, void *stream) {
     AttnProblem p;
     int st = fill_problem(q, k, k, causal, has_scale, scale, p);
     if (!st) st = fill_mask(mask, p);
+    if (!st && dropout) st = set_keep(p, keep_bits, keep_scale);
     if (st) return st;
     if (!is_f32(lse, 3) || !sizes_are(lse, {p.B, p.H, p.L}))
         return fail(DC_ERR_VALUE, "logsumexp must be float32 (B, H, L)");
@@ -459,6 +523,21 @@ int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t 
     if ((st = device_ok())) return st;
     return simt_probs(p, static_cast<float *>(probs->data), ps, average_heads,
                       static_cast<cudaStream_t>(stream));
+}
+
+int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *lse,
+                  const dc_tensor_t *mask, int causal, int has_scale, double scale,
+                  int average_heads, dc_tensor_t *probs, void *stream) {
+    return attn_probs_impl(q, k, lse, mask, causal, has_scale, scale, nullptr, 0.0f, false, average_heads, probs,
+                           stream);
+}
+
+int dc_attn_probs_dropout(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *lse,
+                          const dc_tensor_t *mask, int causal, int has_scale, double scale,
+                          const uint32_t *keep_bits, float keep_scale, int average_heads, dc_tensor_t *probs,
+                          void *stream) {
+    return attn_probs_impl(q, k, lse, mask, causal, has_scale, scale, keep_bits, keep_scale, true, average_heads,
+                           probs, stream);
 }
 
 }  // extern "C"

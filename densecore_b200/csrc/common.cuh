@@ -24,6 +24,11 @@ struct AttnProblem {
     int causal;
     float scale;
     int group;  // H / Hkv
+    // Dropout on the attention weights (null = none): weight (b, h, i, j) is multiplied by
+    // keep_scale when bit e % 32 of keep[e / 32] is set, e = ((b * H + h) * L + i) * S + j,
+    // and by 0 otherwise.
+    const uint32_t *keep;
+    float keep_scale;
 };
 
 // Backward extras: grad_out (B,H,L,Ev), dq (B,H,L,E), dk (B,Hkv,S,E), dv (B,Hkv,S,Ev),
@@ -102,6 +107,13 @@ __device__ __forceinline__ void mask_run(const AttnProblem &p, int64_t b, int64_
             for (int c = 0; c < N; c++) out[c] = (((bits >> c) & 1u) && !m[c * step]) ? -INFINITY : 0.0f;
         }
     }
+}
+
+// The dropout factor of weight (b, h, i, j): keep_scale or 0 (1 without dropout).
+__device__ __forceinline__ float keep_factor(const AttnProblem &p, int64_t b, int64_t h, int64_t i, int64_t j) {
+    if (!p.keep) return 1.0f;
+    const int64_t e = ((b * p.H + h) * p.L + i) * p.S + j;
+    return (__ldg(p.keep + (e >> 5)) >> (e & 31)) & 1u ? p.keep_scale : 0.0f;
 }
 
 // Whether key j is visible to query row i under top-left causal alignment.

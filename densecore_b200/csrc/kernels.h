@@ -39,6 +39,13 @@ int device_error(int reset);
 // Device address of that word (passed to the kernels), or nullptr.
 int *device_error_word();
 
+// Dropout keep masks (rng.cu): n bernoulli(keep_prob) draws of DenseCore's generator stream
+// from the device state st_in (624 words, left, next) as packed bits; the advanced state goes
+// to st_out (which may equal st_in). rng_skip: the same advance on host memory, no device.
+int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_prob, uint32_t *bits,
+              cudaStream_t stream);
+int rng_skip(const uint32_t *st_in, uint64_t outputs, uint32_t *st_out);
+
 // The library's stream-ordered scratch pool (pool.cu): memory for `bytes` on `stream`'s
 // order of the current device, and its release on the same stream.
 int pool_alloc(void **ptr, size_t bytes, cudaStream_t stream);

@@ -13,7 +13,7 @@ namespace sm100 {
 // an error code and unwinds instead of spinning forever.
 constexpr uint64_t WAIT_TIMEOUT_NS = 1000000000ull;  // 1 s
 
-enum DeviceError : int { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1 };
+enum DeviceError : int { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_GENERATOR_STATE = 2 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

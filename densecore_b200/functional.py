@@ -15,6 +15,7 @@ import numpy as np
 import torch
 
 from . import _native
+from . import random as _random
 
 
 def _as_mask(attn_mask, device):
@@ -73,6 +74,49 @@ class _FlashAttention(torch.autograd.Function):
         return gq, gk, gv, None, None, None
 
 
+def _dropout_probability(p):
+    """functional.py:219-226: a real number in [0, 1] (bools are refused)."""
+    if isinstance(p, (bool, np.bool_)) or not isinstance(p, numbers.Real):
+        raise TypeError("dropout probability must be real")
+    p = float(p)
+    if not 0.0 <= p <= 1.0:
+        raise ValueError("dropout probability must be in [0, 1]")
+    return p
+
+
+def _keep_mask(n, p, device, generator=None):
+    """The dropout keep bits of n weights and the survivors' factor, as ``_dropout_noise``
+    (functional.py:638-641) draws them: bernoulli(1 - p) from the generator, survivors times
+    float32(1) / float32(1 - p). p == 1 draws nothing and zeroes every weight (``dropout``
+    multiplies by 0 there, functional.py:242-243)."""
+    if p == 1.0:
+        return torch.zeros(max((n + 31) // 32, 1), dtype=torch.int32, device=device), 0.0
+    keep = _random.dropout_keep_bits(n, 1.0 - p, device, generator)
+    return keep, float(np.float32(1.0) / np.float32(1.0 - p))
+
+
+class _FlashAttentionDropout(torch.autograd.Function):
+    """The fused kernels with dropout on the weights; saves q, k, v, out, lse and the keep bits."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale, mask, p):
+        _native._require_cuda(q, k, v, mask)  # before the draw, so a refused call consumes nothing
+        n = q.shape[0] * q.shape[1] * q.shape[2] * k.shape[2]
+        keep, keep_scale = _keep_mask(n, p, q.device)
+        out, lse = _native._flash_attention_dropout(q, k, v, causal, scale, mask, keep, keep_scale)
+        ctx.save_for_backward(q, k, v, out, lse, keep)
+        ctx.causal, ctx.scale, ctx.mask, ctx.keep_scale = causal, scale, mask, keep_scale
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        q, k, v, out, lse, keep = ctx.saved_tensors
+        gq, gk, gv = _native._flash_attention_dropout_backward(
+            grad.contiguous() if grad.stride(-1) != 1 else grad, q, k, v, out, lse, ctx.causal, ctx.scale, ctx.mask,
+            keep, ctx.keep_scale)
+        return gq, gk, gv, None, None, None, None
+
+
 def flash_attention(q, k, v, causal=False, scale=None, mask=None):
     """(out, lse) of the fused kernel on (B,H,L,E) / (B,Hkv,S,E) / (B,Hkv,S,Ev) CUDA tensors,
     differentiable in q, k and v."""
@@ -117,8 +161,7 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.
         scale = 1.0 / math.sqrt(embed) if embed else 1.0
     elif isinstance(scale, (bool, np.bool_)) or not isinstance(scale, numbers.Real):
         raise TypeError("scale must be real")
-    if dropout_p:
-        raise NotImplementedError("dropout_p > 0 is not supported by the CUDA attention kernels")
+    p = _dropout_probability(dropout_p) if dropout_p else 0.0
     for t in (query, key, value):
         if t.dtype != torch.float32:
             raise TypeError(f"attention tensors must be float32, got {t.dtype}")
@@ -127,7 +170,10 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.
         q, k, v = query.unsqueeze(1), key.unsqueeze(1), value.unsqueeze(1)
     else:
         q, k, v = query, key, value
-    out, _lse = flash_attention(q, k, v, is_causal, float(scale), mask)
+    if p:
+        out = _FlashAttentionDropout.apply(q, k, v, is_causal, float(scale), mask, p)
+    else:
+        out, _lse = flash_attention(q, k, v, is_causal, float(scale), mask)
     return out.squeeze(1) if rank == 3 else out
 
 
@@ -153,7 +199,9 @@ def multi_head_attention_forward(query, key, value, embed_dim_to_check, num_head
     fused kernel with strided (N, H, L, D) views of the projections -- no transposed copies.
     As in the reference, a query row whose keys are all masked yields NaN (output and
     gradients); ``need_weights`` returns the softmax probabilities (head-averaged by default),
-    which are not differentiable here. dropout_p > 0 in training raises NotImplementedError.
+    which are not differentiable here. In training, dropout_p > 0 drops the probabilities with
+    DenseCore's masks (functional.py:450-451); the returned weights are the dropped ones, as
+    there.
     """
     F = torch.nn.functional
     if is_causal and attn_mask is None:
@@ -166,8 +214,7 @@ def multi_head_attention_forward(query, key, value, embed_dim_to_check, num_head
     tgt_len, bsz, embed_dim = query.shape
     if embed_dim != embed_dim_to_check:
         raise ValueError(f"was expecting embedding dimension of {embed_dim_to_check}, but got {embed_dim}")
-    if training and dropout_p > 0:
-        raise NotImplementedError("MHA dropout is not supported by the CUDA attention kernels")
+    p = _dropout_probability(dropout_p) if training and dropout_p > 0 else 0.0
     head_dim = embed_dim // num_heads
     biases = (None, None, None) if in_proj_bias is None else in_proj_bias.chunk(3)
     weights = (q_proj_weight, k_proj_weight, v_proj_weight) if use_separate_proj_weight else in_proj_weight.chunk(3)
@@ -215,7 +262,11 @@ def multi_head_attention_forward(query, key, value, embed_dim_to_check, num_head
         dead = ~allowed.expand(bsz, num_heads, tgt_len, S).any(-1)
         if not bool(dead.any()):
             dead = None
-    out, lse = _MHACore.apply(qh, kh, vh, float(math.sqrt(1.0 / head_dim)), mask, dead)
+    keep, keep_scale = (None, 0.0)
+    if p:
+        _native._require_cuda(qh, kh, vh, mask)
+        keep, keep_scale = _keep_mask(bsz * num_heads * tgt_len * S, p, qh.device)
+    out, lse = _MHACore.apply(qh, kh, vh, float(math.sqrt(1.0 / head_dim)), mask, dead, keep, keep_scale)
     out = out.permute(2, 0, 1, 3).reshape(tgt_len * bsz, embed_dim)
     out = F.linear(out, out_proj_weight, out_proj_bias).reshape(tgt_len, bsz, -1)
     if not batched:
@@ -224,7 +275,7 @@ def multi_head_attention_forward(query, key, value, embed_dim_to_check, num_head
         return out, None
     with torch.no_grad():
         probs = _native._attn_probs(qh, kh, lse, False, float(math.sqrt(1.0 / head_dim)), mask,
-                                    average_heads=average_attn_weights)
+                                    average_heads=average_attn_weights, keep=keep, keep_scale=keep_scale)
         if dead is not None:
             d = dead.any(1) if average_attn_weights else dead
             probs = probs.masked_fill(d.unsqueeze(-1), float("nan"))
@@ -237,10 +288,13 @@ class _MHACore(torch.autograd.Function):
     the key/value gradients of its (batch, head)."""
 
     @staticmethod
-    def forward(ctx, qh, kh, vh, scale, mask, dead):
-        out, lse = _native._flash_attention(qh, kh, vh, False, scale, mask)
+    def forward(ctx, qh, kh, vh, scale, mask, dead, keep, keep_scale):
+        if keep is None:
+            out, lse = _native._flash_attention(qh, kh, vh, False, scale, mask)
+        else:
+            out, lse = _native._flash_attention_dropout(qh, kh, vh, False, scale, mask, keep, keep_scale)
         ctx.save_for_backward(qh, kh, vh, out, lse)
-        ctx.scale, ctx.mask, ctx.dead = scale, mask, dead
+        ctx.scale, ctx.mask, ctx.dead, ctx.keep, ctx.keep_scale = scale, mask, dead, keep, keep_scale
         ctx.mark_non_differentiable(lse)
         if dead is not None:
             out = out.masked_fill(dead.unsqueeze(-1), float("nan"))
@@ -252,11 +306,15 @@ class _MHACore(torch.autograd.Function):
         grad = grad.contiguous()
         if ctx.dead is not None:
             grad = grad.masked_fill(ctx.dead.unsqueeze(-1), 0.0)
-        gq, gk, gv = _native._flash_attention_backward(grad, qh, kh, vh, out, lse, False, ctx.scale, ctx.mask)
+        if ctx.keep is None:
+            gq, gk, gv = _native._flash_attention_backward(grad, qh, kh, vh, out, lse, False, ctx.scale, ctx.mask)
+        else:
+            gq, gk, gv = _native._flash_attention_dropout_backward(grad, qh, kh, vh, out, lse, False, ctx.scale,
+                                                                   ctx.mask, ctx.keep, ctx.keep_scale)
         if ctx.dead is not None:
             nan = float("nan")
             gq = gq.masked_fill(ctx.dead.unsqueeze(-1), nan)
             bh = ctx.dead.any(-1)[..., None, None]
             gk = gk.masked_fill(bh, nan)
             gv = gv.masked_fill(bh, nan)
-        return gq, gk, gv, None, None, None
+        return gq, gk, gv, None, None, None, None, None

@@ -13,6 +13,11 @@
  *   dc_attn_merge    logsumexp merge of partial results (ring attention; no CPU counterpart)
  *   dc_attn_probs    softmax(scale*QK^T + mask) averaged over heads: the need_weights output of
  *                    multi_head_attention_forward (python/densecore/functional.py:456-461)
+ *   dc_dropout_keep_bits  the bernoulli draw of _dropout_noise (functional.py:638-641,
+ *                    src/torch_random.rs:242-254) as a device bit mask
+ *   dc_sdpa_fwd_dropout / dc_sdpa_bwd_dropout / dc_attn_probs_dropout  SDPA and MHA with
+ *                    dropout_p > 0 (functional.py:312-340, :450-451), fused
+ *   dc_rng_skip      host-side skip-ahead of the generator state (no reference counterpart)
  *   dc_last_error    the message of the last failure on this thread (PyErr text in lib.rs)
  *
  * Conventions
@@ -152,6 +157,60 @@ DC_API int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_te
                   const dc_tensor_t *mask, int causal, int has_scale, double scale,
                   int average_heads, dc_tensor_t *probs, void *stream);
 
+/* ---- Dropout (python/densecore/functional.py:229-244, :312-340, :450-451, :638-641) ----
+ * DenseCore runs SDPA with dropout_p > 0 on its math path: the softmax weights are multiplied
+ * by noise = bernoulli(1 - p) / float32(1 - p), drawn in row-major (B, H, L, S) order from the
+ * CPU generator that manual_seed seeds (PyTorch's mt19937 as src/torch_random.rs ports it).
+ * Here the generator's engine state lives in device memory as 626 uint32 words -- the 624
+ * state words, then `left` and `next` (src/torch_random.rs:19-26) -- the keep mask is drawn
+ * on the device, and the attention kernels apply it. */
+
+/* n bernoulli(keep_prob) draws as packed bits -- element e is bit e % 32 of bits[e / 32],
+ * ceil(n / 32) words, 4-byte aligned -- bit-identical to DenseCore's Generator::bernoulli
+ * (src/torch_random.rs:242-254) continuing from the device state state_in: each draw takes
+ * two 32-bit outputs, x = (random64 & (2^53 - 1)) * 2^-53, keep when x < keep_prob. The
+ * state after the 2n outputs is written to state_out (which may equal state_in). A state
+ * whose `left` is not in 1..624 sets dc_device_status() to 2 and writes nothing.
+ * The first call in a process computes the generator's jump tables on the host (a fraction
+ * of a second), and the first call on each device copies them there with synchronous copies:
+ * make that call before any stream capture. */
+DC_API int dc_dropout_keep_bits(const uint32_t *state_in, uint32_t *state_out, int64_t n,
+                                double keep_prob, uint32_t *bits, void *stream);
+
+/* Host memory only, no device: state_out = the engine state (626 words, as above) after
+ * `outputs` 32-bit outputs from state_in, outputs <= 2^36. state_out may equal state_in.
+ * No counterpart in the reference (it draws sequentially). */
+DC_API int dc_rng_skip(const uint32_t *state_in, uint64_t outputs, uint32_t *state_out);
+
+/* dc_sdpa_fwd with dropout on the attention weights: weight (b, h, i, j) is multiplied by
+ * keep_scale when bit ((b*H + h)*L + i)*S + j of keep_bits is set and by 0 otherwise (the
+ * mask of dc_dropout_keep_bits over B*H*L*S elements; keep_scale = float32(1) /
+ * float32(1 - p), as _dropout_noise divides). lse is the logsumexp of the undropped scores.
+ * Runs the CUDA-core fp32 kernels whatever the precision (which is still validated).
+ * Replaces the math path of scaled_dot_product_attention with dropout (functional.py:318-340). */
+DC_API int dc_sdpa_fwd_dropout(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                               const dc_tensor_t *mask, int causal, int has_scale, double scale,
+                               int precision, const uint32_t *keep_bits, float keep_scale,
+                               dc_tensor_t *out, dc_tensor_t *lse, void *stream);
+
+/* The backward of dc_sdpa_fwd_dropout (same keep_bits and keep_scale; out and lse from it):
+ * dV = (P Z)^T dO, dS = P (Z (dO V^T) - rowsum(dO * out)) with Z the dropout factors. */
+DC_API int dc_sdpa_bwd_dropout(const dc_tensor_t *grad_out, const dc_tensor_t *q,
+                               const dc_tensor_t *k, const dc_tensor_t *v, const dc_tensor_t *out,
+                               const dc_tensor_t *lse, const dc_tensor_t *mask, int causal,
+                               int has_scale, double scale, int precision,
+                               const uint32_t *keep_bits, float keep_scale, dc_tensor_t *grad_q,
+                               dc_tensor_t *grad_k, dc_tensor_t *grad_v, void *workspace,
+                               size_t workspace_bytes, void *stream);
+
+/* dc_attn_probs with each probability times its dropout factor: the weights
+ * multi_head_attention_forward returns when it trains with dropout (functional.py:450-461). */
+DC_API int dc_attn_probs_dropout(const dc_tensor_t *q, const dc_tensor_t *k,
+                                 const dc_tensor_t *lse, const dc_tensor_t *mask, int causal,
+                                 int has_scale, double scale, const uint32_t *keep_bits,
+                                 float keep_scale, int average_heads, dc_tensor_t *probs,
+                                 void *stream);
+
 /* Kernel tracing. While enabled, every kernel the library launches is bracketed by two
  * CUDA events on its launch stream. dc_kernel_timing_report() waits for the recorded events
  * and writes {"<kernel>": [launches, total_ms], ...} as JSON into buf (truncated to len);
@@ -160,9 +219,11 @@ DC_API int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_te
 DC_API int dc_kernel_timing(int enable);
 DC_API int dc_kernel_timing_report(char *buf, size_t len, int reset);
 
-/* Device-side status of the tensor-core kernels: 0, or 1 when a kernel gave up on a wait
- * that did not complete within its bound (1 s); that CTA then unwound without writing its
- * outputs. Synchronises with the device. reset != 0 clears the status. -1 on a CUDA error. */
+/* Device-side status of the library's kernels: 0; 1 when a tensor-core kernel gave up on a
+ * wait that did not complete within its bound (1 s) -- that CTA then unwound without writing
+ * its outputs; 2 when dc_dropout_keep_bits read a generator state whose `left` word is not in
+ * 1..624 -- it then wrote neither mask nor state. Synchronises with the device. reset != 0
+ * clears the status. -1 on a CUDA error. */
 DC_API int dc_device_status(int reset);
 
 /* Message of the last failing call on this host thread ("" if none). */

@@ -718,6 +718,11 @@ DCO_EXPORT void dco_mt_random(uint32_t *st, int64_t n, uint32_t *out) {
     for (int64_t i = 0; i < n; i++) out[i] = mt_random(st);
 }
 
+/* n outputs drawn and discarded (advances the engine exactly as n random() calls). */
+DCO_EXPORT void dco_mt_discard(uint32_t *st, int64_t n) {
+    for (int64_t i = 0; i < n; i++) (void)mt_random(st);
+}
+
 /* bernoulli(n, p) (torch_random.rs:242-254): each draw is uniform_real_distribution<double>
  * (:106-110): random64 = (first random << 32) | second, its low 53 bits times 2^-53, then
  * fma(x, 1 - 0, 0) = x; the element is 1 when that is below p. Written as packed bits:

@@ -28,8 +28,17 @@ def test_rejections_match_reference():
         sdpa(q, k, v, scale="x")
     with pytest.raises(TypeError):
         sdpa(q.numpy(), k, v)
-    with pytest.raises(NotImplementedError):
+    # functional.py:219-226 (dropout's own checks), then the device check before any draw.
+    with pytest.raises(ValueError, match=r"\[0, 1\]"):
+        sdpa(q, k, v, dropout_p=1.5)
+    with pytest.raises(TypeError, match="real"):
+        sdpa(q, k, v, dropout_p=True)
+    with pytest.raises(TypeError, match="real"):
+        sdpa(q, k, v, dropout_p="x")
+    state = dc.get_rng_state()
+    with pytest.raises(RuntimeError, match="CUDA"):
         sdpa(q, k, v, dropout_p=0.1)
+    assert torch.equal(dc.get_rng_state(), state)  # the refused call drew nothing
     with pytest.raises(TypeError):
         sdpa(q.double(), k, v)
 
