@@ -49,6 +49,9 @@ WORKLOADS = {
                             bwd=False, cfg=4),
     "decode_splitkv": dict(q=(64, 32, 1, 128), kv=(64, 32, 8192, 128), causal=False, mask=None, amp=1.0,
                            bwd=False, cfg=5),
+    # Config 3 with attention dropout (GPT-2's 0.1): the keep mask is drawn every step.
+    "gpt2_dropout_fwd_bwd": dict(q=(8, 12, 1024, 64), kv=(8, 12, 1024, 64), causal=True, mask=None, amp=1.0,
+                                 bwd=True, cfg=3, dropout=0.1),
 }
 
 
@@ -223,6 +226,25 @@ def cpu_baseline(w, name, budget_s=12.0, threads=None):
         return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                 "sample": f"causal prefix of {R} rows x {heads} heads of [1,16,32768,128], fwd, "
                           f"{dt:.1f} s"}
+    if w.get("dropout"):
+        # DenseCore runs dropout on its math path (functional.py:318-340): bmm through the
+        # portable sgemm, one thread (torch_blas.rs:404-445), softmax, the sequential bernoulli
+        # draw. Whole heads, one after another, including each head's draw.
+        p = w["dropout"]
+        gen = oracle.MtGenerator(1)
+        done, dt = 0, 0.0
+        while dt < budget_s and done < B * H:
+            q, k, v, g = (rng.normal(size=(1, 1, L, D)).astype(np.float32) * w["amp"] for _ in range(4))
+            t0 = time.perf_counter()
+            keep = oracle.unpack_bits(gen.keep_bits(L * S, 1 - p), L * S)
+            out, saved = oracle.sdpa_math_forward(q, k, v, causal=w["causal"], noise=oracle.dropout_noise(keep, p))
+            oracle.sdpa_math_backward(g, v, saved)
+            dt += time.perf_counter() - t0
+            done += 1
+        amount, unit = work(w)
+        return {"value": amount / (B * H) * done / dt / 1e12, "unit": unit, "cores": 1, "kind": "port",
+                "sample": f"{done} of {B * H} heads of {name} through the dropout math path "
+                          f"(fwd+bwd, mask draw included), {dt:.1f} s"}
     # Whole (batch, head) tasks; tasks are independent, so a sample's rate is the full run's.
     nb = min(B, max(1, math.ceil(threads / H)))
     q = rng.normal(size=(nb, H, L, D)).astype(np.float32) * w["amp"]
@@ -273,7 +295,8 @@ def run_reference(args, w, name, rank, world):
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": name, "shape_q": list(w["q"]), "shape_kv": list(w["kv"]),
-                       "causal": w["causal"], "mask": w["mask"], "baseline_cfg": w["cfg"]},
+                       "causal": w["causal"], "mask": w["mask"], "dropout_p": w.get("dropout", 0.0),
+                       "baseline_cfg": w["cfg"]},
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -339,6 +362,15 @@ def main():
 
         def step():
             _native._decode(q, k, v, None, None, splits, ws)
+    elif w.get("dropout"):
+        from densecore_b200.functional import _keep_mask
+        n_weights = q.shape[0] * q.shape[1] * q.shape[2] * k.shape[2]
+        dc.manual_seed(1234 + rank)
+
+        def step():
+            keep, ks = _keep_mask(n_weights, w["dropout"], device)
+            out, lse = _native._flash_attention_dropout(q, k, v, causal, None, mask, keep, ks)
+            _native._flash_attention_dropout_backward(g, q, k, v, out, lse, causal, None, mask, keep, ks)
     elif w["bwd"]:
         def step():
             out, lse = _native._flash_attention(q, k, v, causal, None, mask)
@@ -430,6 +462,7 @@ def main():
                 "data": "synthetic (seeded N(0,1) of the config's shape)",
                 "config": {"workload": name, "baseline_cfg": w["cfg"], "shape_q": list(w["q"]),
                            "shape_kv": list(w["kv"]), "causal": causal, "mask": w["mask"],
+                           "dropout_p": w.get("dropout", 0.0),
                            "per_rank": ("zig-zag sequence shard (ring attention, NCCL send/recv)"
                                         if ring is not None else "full workload (weak scaling)"),
                            "parallelism": f"ring{world}" if ring is not None else f"dp{world}",
@@ -444,12 +477,15 @@ def main():
 
 
 def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
+    """The metric through the public API with host buffers: every step copies its inputs from
+    pinned host memory and its outputs (out and, with a backward, the three gradients) back.
+    Steps are pipelined the way a training or serving loop would run them: step i+1's inputs go
+    up on one stream while step i computes on a second and step i-1's results come down on a
+    third (two buffer slots, events guarding their reuse)."""
     import densecore_b200 as dc
     ins = [q, k, v] + ([g] if g is not None else [])
     if w["cfg"] == 5:
         ins = [q]  # the KV cache is device-resident state; a decode step brings its query
-    host_in = [t.detach().cpu().pin_memory() for t in ins]
-    dev_in = [torch.empty_like(t) for t in ins]
     if ring is not None:
         outs_shape = [tuple(q.shape)]
     elif w["cfg"] == 5:
@@ -458,38 +494,69 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
         outs_shape = [tuple(w["q"]), tuple(w["q"]), tuple(w["kv"]), tuple(w["kv"])]
     else:
         outs_shape = [tuple(w["q"])]
-    host_out = [torch.empty(s, dtype=torch.float32).pin_memory() for s in outs_shape]
+    nslot = 2
+    host_in = [[t.detach().cpu().pin_memory() for t in ins] for _ in range(nslot)]
+    dev_in = [[torch.empty_like(t) for t in ins] for _ in range(nslot)]
+    host_out = [[torch.empty(s_, dtype=torch.float32).pin_memory() for s_ in outs_shape] for _ in range(nslot)]
+    s_h2d, s_comp, s_d2h = (torch.cuda.Stream(device) for _ in range(3))
+    ev_in = [torch.cuda.Event() for _ in range(nslot)]    # the slot's inputs landed
+    ev_used = [torch.cuda.Event() for _ in range(nslot)]  # the slot's compute finished
+    ev_out = [torch.cuda.Event() for _ in range(nslot)]   # the slot's results are on the host
+    used = [False] * nslot
 
-    def step():
-        for h, d in zip(host_in, dev_in):
-            d.copy_(h, non_blocking=True)
+    def compute(d):
         if ring is not None:
-            res = [ring(*dev_in)[0]]
-        elif w["cfg"] == 5:
-            res = [dc.scaled_dot_product_attention(dev_in[0], k, v)]
-        elif w["bwd"]:
-            tq, tk, tv = (t.requires_grad_(True) for t in dev_in[:3])
-            y = dc.scaled_dot_product_attention(tq, tk, tv, attn_mask=mask, is_causal=w["causal"])
-            y.backward(dev_in[3])
+            return [ring(*d)[0]]
+        if w["cfg"] == 5:
+            return [dc.scaled_dot_product_attention(d[0], k, v)]
+        if w["bwd"]:
+            tq, tk, tv = (t.requires_grad_(True) for t in d[:3])
+            y = dc.scaled_dot_product_attention(tq, tk, tv, attn_mask=mask, is_causal=w["causal"],
+                                                dropout_p=w.get("dropout", 0.0))
+            y.backward(d[3])
             res = [y.detach(), tq.grad, tk.grad, tv.grad]
             for t in (tq, tk, tv):
                 t.grad = None
                 t.requires_grad_(False)
-        else:
-            res = [dc.scaled_dot_product_attention(*dev_in[:3], attn_mask=mask, is_causal=w["causal"])]
-        for h, r in zip(host_out, res):
-            h.copy_(r, non_blocking=True)
+            return res
+        return [dc.scaled_dot_product_attention(*d[:3], attn_mask=mask, is_causal=w["causal"])]
 
-    for _ in range(args.warmup):
-        step()
+    def step(i):
+        sl = i % nslot
+        with torch.cuda.stream(s_h2d):
+            if used[sl]:
+                s_h2d.wait_event(ev_used[sl])  # the slot's previous compute read its inputs
+            for h, d in zip(host_in[sl], dev_in[sl]):
+                d.copy_(h, non_blocking=True)
+            ev_in[sl].record(s_h2d)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_in[sl])
+            res = compute(dev_in[sl])
+            ev_used[sl].record(s_comp)
+        with torch.cuda.stream(s_d2h):
+            if used[sl]:
+                s_d2h.wait_event(ev_out[sl])
+            s_d2h.wait_event(ev_used[sl])
+            for h, r in zip(host_out[sl], res):
+                r.record_stream(s_d2h)  # the allocator keeps r until the copy is done
+                h.copy_(r, non_blocking=True)
+            ev_out[sl].record(s_d2h)
+        used[sl] = True
+
+    for i in range(args.warmup):
+        step(i)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
+    cur = torch.cuda.current_stream(device)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        step()
-    e.record()
+    s.record(cur)
+    s_h2d.wait_event(s)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    for sl in range(nslot):
+        cur.wait_event(ev_out[sl])
+    e.record(cur)
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
     world = 1
@@ -501,8 +568,8 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
     if ring is not None:
         world = 1  # the ranks share one sequence
     return {"value": world * amount / (ms / 1e3) / scale, "unit": "GB/s" if scale == 1e9 else "TFLOP/s",
-            "ms_per_step": ms, "h2d_bytes_per_step": sum(t.numel() * 4 for t in host_in),
-            "d2h_bytes_per_step": sum(t.numel() * 4 for t in host_out)}
+            "ms_per_step": ms, "h2d_bytes_per_step": sum(t.numel() * 4 for t in host_in[0]),
+            "d2h_bytes_per_step": sum(t.numel() * 4 for t in host_out[0]), "pipelined": True}
 
 
 if __name__ == "__main__":

@@ -20,10 +20,11 @@
 //   * pos = 625 - left is the next output; a seeded or fully used block (left == 1) is
 //     twisted first, so the canonical block starts at B0 = 0 or 624 and pos >= B0;
 //   * G = B0 + 624; chunk c >= 1 covers words [G + cJ, G + (c+1)J), chunk 0 covers
-//     [pos, G + J) -- J = 624 * 1680 words, so every chunk start is a block start;
+//     [pos, G + J) -- J = 624 * 840 words, so every chunk start is a block start;
 //   * a CTA owns the 32-element mask words whose first word lies in its chunk. CTA c >= 1
-//     reaches its chunk start by at most two jumps (c = c1 * 32 + c0, tables x^(c0 J) and
-//     x^(c1 32 J)), then generates 192 words per step in a 1024-word shared ring;
+//     reaches its chunk start by one jump with x^(c J) mod phi (a table computed on the host
+//     as needed, 2048 entries at most), then generates 224 words per phase in a mirrored
+//     2048-word shared ring while other warps turn earlier words into keep bits;
 //   * the CTA whose chunk holds the block of the last consumed word writes the new state in
 //     DenseCore's form (that block, left = 625 - next, next = words of it consumed).
 #include <cuda_runtime.h>
@@ -38,6 +39,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
+#include "trace.h"
 
 namespace dc {
 namespace {
@@ -46,12 +48,15 @@ constexpr int MT_N = 624, MT_M = 397;
 constexpr uint32_t MATRIX_A = 0x9908b0dfu, UMASK = 0x80000000u, LMASK = 0x7fffffffu;
 constexpr int DEG = 19937;                  // degree of phi
 constexpr int PW = (DEG + 63) / 64;         // 64-bit words of a reduced polynomial (312)
-constexpr int64_t CHUNK = 624LL * 1680;     // words per chunk (1,048,320)
-constexpr int LEVEL = 32;                   // chunk c = c1 * LEVEL + c0
-constexpr int MAX_CHUNKS = LEVEL * LEVEL;
-constexpr int RING = 1024;                  // shared ring of state words (power of two)
-constexpr int STEP = 192;                   // words generated per step (6 warps; < 227)
-constexpr int THREADS = 640;                // 624 jump accumulators, rounded up to warps
+constexpr int64_t CHUNK = 624LL * 840;      // words per chunk (524,160)
+constexpr int MAX_CHUNKS = 2048;            // jump table entries x^(c J), c < MAX_CHUNKS
+constexpr int RING = 2048;                  // shared ring of state words (power of two)
+constexpr int GEN_WARPS = 7;                // warps generating the stream
+constexpr int STEP = GEN_WARPS * 32;        // words generated per phase (224 <= 624 - 397)
+constexpr int CONV_WARPS = 4;               // warps turning words into keep bits
+constexpr int THREADS = (GEN_WARPS + CONV_WARPS) * 32;
+constexpr int JW = 4;                       // window words per thread in a jump (156 threads)
+static_assert(MT_N + 2 * STEP <= RING, "a jump phase must not overwrite words still being read");
 
 __host__ __device__ __forceinline__ int64_t imin(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ uint32_t twist(uint32_t u, uint32_t v) {
@@ -119,33 +124,81 @@ int berlekamp_massey(const std::vector<uint8_t> &s, Poly &C) {
     return (int)L;
 }
 
-struct Field {
-    Poly phi;                // DEG + 1 bits
-    std::vector<Poly> phs;   // phi << s, s = 0..63 (PW + 2 words each)
+// dst ^= src << sh (bits), over dst's words.
+void xor_shifted(Poly &dst, const Poly &src, int64_t sh) {
+    const int64_t ws = sh >> 6, bs = sh & 63;
+    for (int64_t k = 0; k < (int64_t)src.size(); k++) {
+        if (ws + k < (int64_t)dst.size()) dst[ws + k] ^= src[k] << bs;
+        if (bs && ws + k + 1 < (int64_t)dst.size()) dst[ws + k + 1] ^= src[k] >> (64 - bs);
+    }
+}
 
-    // p (up to 2 DEG - 1 bits, any length) reduced mod phi into PW words.
+uint32_t byte_at(const Poly &p, int64_t pos) {
+    const int64_t w = pos >> 6, b = pos & 63;
+    uint64_t v = p[w] >> b;
+    if (b > 56 && w + 1 < (int64_t)p.size()) v |= p[w + 1] << (64 - b);
+    return (uint32_t)(v & 0xffu);
+}
+
+// Arithmetic in GF(2)[x] / phi, eight coefficients at a time.
+struct Field {
+    Poly phi;                   // DEG + 1 bits
+    // red[(o * 256 + t) * (PW + 1)]: the multiple q * phi (deg q < 8) whose coefficients
+    // DEG .. DEG + 7 are the byte t, shifted left by 8 o bits. XORed in at word s / 8 it clears
+    // coefficients DEG + 8 s .. DEG + 8 s + 7 of a product (o = s % 8).
+    std::vector<uint64_t> red;
+
+    void init(const Poly &phi_) {
+        phi = phi_;
+        red.assign((size_t)8 * 256 * (PW + 1), 0);
+        for (int q = 0; q < 256; q++) {
+            Poly m(PW + 2, 0);
+            for (int i = 0; i < 8; i++)
+                if ((q >> i) & 1) xor_shifted(m, phi, i);
+            const uint32_t t = byte_at(m, DEG);  // a bijection of q (phi is monic)
+            for (int o = 0; o < 8; o++) {
+                Poly sh(PW + 2, 0);
+                xor_shifted(sh, m, 8 * o);
+                memcpy(&red[((size_t)o * 256 + t) * (PW + 1)], sh.data(), (PW + 1) * 8);
+            }
+        }
+    }
+    // p (2 PW + 2 words, degree <= 2 DEG - 2) reduced mod phi into PW words.
     Poly reduce(Poly p) const {
-        const int64_t top = (int64_t)p.size() * 64 - 1;
-        for (int64_t k = top; k >= DEG; k--) {
-            if (!bit(p.data(), k)) continue;
-            const int64_t sft = k - DEG, w = sft >> 6;
-            const Poly &q = phs[sft & 63];
-            for (int j = 0; j < PW + 2 && w + j < (int64_t)p.size(); j++) p[w + j] ^= q[j];
+        p.resize(2 * PW + 2, 0);
+        for (int64_t s = (DEG - 2) / 8; s >= 0; s--) {
+            const uint32_t t = byte_at(p, DEG + 8 * s);
+            if (!t) continue;
+            const uint64_t *m = &red[((size_t)(s & 7) * 256 + t) * (PW + 1)];
+            uint64_t *d = p.data() + (s >> 3);
+            for (int j = 0; j <= PW; j++) d[j] ^= m[j];
         }
         p.resize(PW);
         return p;
     }
     Poly mul(const Poly &a, const Poly &b) const {
-        std::vector<Poly> bs(64, Poly(PW + 1, 0));
-        for (int s = 0; s < 64; s++)
-            for (int k = 0; k <= PW; k++)
-                bs[s][k] = (k < PW ? b[k] << s : 0) | (s && k > 0 ? b[k - 1] >> (64 - s) : 0);
         Poly prod(2 * PW + 2, 0);
-        for (int64_t i = 0; i < DEG; i++) {
-            if (!bit(a.data(), i)) continue;
-            const int64_t w = i >> 6;
-            const Poly &q = bs[i & 63];
-            for (int k = 0; k <= PW; k++) prod[w + k] ^= q[k];
+        std::vector<uint64_t> tab((size_t)256 * (PW + 1));
+        for (int o = 0; o < 8; o++) {
+            // tab[v] = (b * v) << 8 o for every byte v
+            std::fill(tab.begin(), tab.begin() + (PW + 1), 0ull);
+            for (int i = 0; i < 8; i++) {
+                Poly sh(PW + 1, 0);
+                xor_shifted(sh, b, 8 * o + i);
+                memcpy(&tab[((size_t)1 << i) * (PW + 1)], sh.data(), (PW + 1) * 8);
+            }
+            for (int v = 3; v < 256; v++) {
+                if (!(v & (v - 1))) continue;
+                const uint64_t *x = &tab[(size_t)(v & (v - 1)) * (PW + 1)], *y = &tab[(size_t)(v & -v) * (PW + 1)];
+                uint64_t *z = &tab[(size_t)v * (PW + 1)];
+                for (int j = 0; j <= PW; j++) z[j] = x[j] ^ y[j];
+            }
+            for (int w = 0; w < PW; w++) {
+                const uint32_t v = (uint32_t)(a[w] >> (8 * o)) & 0xffu;
+                if (!v) continue;
+                const uint64_t *m = &tab[(size_t)v * (PW + 1)];
+                for (int j = 0; j <= PW; j++) prod[w + j] ^= m[j];
+            }
         }
         return reduce(std::move(prod));
     }
@@ -173,21 +226,24 @@ struct Field {
     }
 };
 
+// x^(c J) mod phi for c = 0 .. count - 1, PW words each, grown on demand. Storage for all
+// MAX_CHUNKS entries is reserved up front, so entries never move once written.
 struct JumpTables {
     bool ok = false;
     std::string error;
     Field f;
-    std::vector<uint64_t> t0, t1;  // LEVEL polynomials of PW words: x^(c0 J), x^(c1 LEVEL J)
+    std::mutex mu;
+    std::vector<uint64_t> t;
+    int count = 0;
 };
 
-// The state words of a seeded generator (torch_random.rs:43-56), then enough outputs of its
-// stream for Berlekamp-Massey.
+// The state words of a seeded generator (torch_random.rs:43-56).
 void seed_block(uint64_t seed, uint32_t *st) {
     st[0] = (uint32_t)seed;
     for (uint32_t j = 1; j < MT_N; j++) st[j] = 1812433253u * (st[j - 1] ^ (st[j - 1] >> 30)) + j;
 }
 
-const JumpTables &tables() {
+JumpTables &tables() {
     static JumpTables T;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -213,31 +269,27 @@ const JumpTables &tables() {
             T.error = "generator jump tables: characteristic polynomial has no constant term";
             return;
         }
-        T.f.phi = phi;
-        T.f.phs.assign(64, Poly(PW + 2, 0));
-        for (int sft = 0; sft < 64; sft++)
-            for (int k = 0; k < PW + 2; k++) {
-                uint64_t v = (k <= PW ? phi[k] << sft : 0);
-                if (sft && k > 0 && k - 1 <= PW) v |= phi[k - 1] >> (64 - sft);
-                T.f.phs[sft][k] = v;
-            }
-        T.t0.assign((size_t)LEVEL * PW, 0);
-        T.t1.assign((size_t)LEVEL * PW, 0);
-        Poly one(PW, 0);
-        one[0] = 1;
-        std::vector<Poly> a(LEVEL), b(LEVEL);
-        a[0] = b[0] = one;
-        a[1] = T.f.powx((uint64_t)CHUNK);
-        for (int c = 2; c < LEVEL; c++) a[c] = T.f.mul(a[c - 1], a[1]);
-        b[1] = T.f.mul(a[LEVEL - 1], a[1]);
-        for (int c = 2; c < LEVEL; c++) b[c] = T.f.mul(b[c - 1], b[1]);
-        for (int c = 0; c < LEVEL; c++) {
-            memcpy(&T.t0[(size_t)c * PW], a[c].data(), PW * 8);
-            memcpy(&T.t1[(size_t)c * PW], b[c].data(), PW * 8);
-        }
+        T.f.init(phi);
+        T.t.assign((size_t)MAX_CHUNKS * PW, 0);
+        T.t[0] = 1;  // x^0
+        T.count = 1;
         T.ok = true;
     });
     return T;
+}
+
+// Makes entries 0 .. need - 1 (need <= MAX_CHUNKS) available; returns the table.
+const uint64_t *table_upto(JumpTables &T, int need) {
+    std::lock_guard<std::mutex> lock(T.mu);
+    while (T.count < need) {
+        const int c = T.count;
+        Poly r = c == 1 ? T.f.powx((uint64_t)CHUNK)
+                        : T.f.mul(Poly(T.t.begin() + (size_t)(c - 1) * PW, T.t.begin() + (size_t)c * PW),
+                                  Poly(T.t.begin() + PW, T.t.begin() + 2 * PW));
+        memcpy(&T.t[(size_t)c * PW], r.data(), PW * 8);
+        T.count = c + 1;
+    }
+    return T.t.data();
 }
 
 // ------------------------------------------------------------ host: the same walk ----
@@ -275,55 +327,80 @@ namespace {
 struct KeepArgs {
     const uint32_t *st_in;
     uint32_t *st_out;
-    const uint64_t *t0, *t1;
-    uint16_t *bits16;   // mask words as 16-bit halves (little-endian)
-    int64_t n;          // elements
-    int64_t nmask;      // 32-element mask words
-    uint64_t thresh;    // keep when (random64 & (2^53 - 1)) < thresh
-    int *err;           // the library's device error word
+    const uint32_t *tab;  // x^(c J) mod phi, 2 PW 32-bit words per c
+    uint32_t *bits;       // mask words
+    int64_t n;            // elements
+    int64_t nmask;        // 32-element mask words
+    uint64_t thresh;      // keep when (random64 & (2^53 - 1)) < thresh
+    int *err;             // the library's device error word
 };
 
-// Generates X[P, P + cnt) into the ring (cnt <= STEP), threads 0..cnt-1.
-__device__ __forceinline__ void gen_step(uint32_t *ring, int64_t P, int cnt) {
+// Generates X[P, P + cnt) (cnt <= STEP) into both copies of the ring, threads 0..cnt-1. Ring
+// slot k % RING and its mirror RING + k % RING hold X[k], so a run of up to RING words read
+// from any slot below RING needs no wrap-around. Slot arithmetic is 32-bit (RING divides 2^32).
+__device__ __forceinline__ void gen_step(uint32_t *ring, uint32_t P, int cnt) {
     const int t = threadIdx.x;
     if (t < cnt) {
-        const int64_t k = P + t;
-        ring[k & (RING - 1)] =
-            ring[(k - MT_N + MT_M) & (RING - 1)] ^ twist(ring[(k - MT_N) & (RING - 1)], ring[(k - MT_N + 1) & (RING - 1)]);
+        const uint32_t k = P + t;
+        const uint32_t v = ring[(k - MT_N + MT_M) & (RING - 1)] ^
+                           twist(ring[(k - MT_N) & (RING - 1)], ring[(k - MT_N + 1) & (RING - 1)]);
+        ring[k & (RING - 1)] = v;
+        ring[(k & (RING - 1)) + RING] = v;
     }
 }
 
-// Jumps the window X[b, b + 624) in the ring (P == b + 624 on entry) by the polynomial g:
-// on return the ring holds X[b + dist, b + dist + 624) and P == b + dist + 624.
-__device__ void jump_window(uint32_t *ring, const uint64_t *__restrict__ g, int64_t &b, int64_t &P, int64_t dist) {
-    const int w = threadIdx.x;
-    uint32_t acc = 0;
+// Jumps the window X[b, b + 624) in the ring (P == b + 624 on entry) by the polynomial g
+// (DEG bits in 2 PW 32-bit words): on return the ring holds X[b + dist, b + dist + 624) and
+// P == b + dist + 624. Thread t < 156 accumulates window words t + 156 d, d < 4 (a warp reads
+// consecutive words: no bank conflicts), two set bits of g per loop turn.
+__device__ void jump_window(uint32_t *ring, const uint32_t *__restrict__ g, int64_t &b, int64_t &P, int64_t dist) {
+    const int tid = threadIdx.x;
+    constexpr int NT = MT_N / JW;
+    uint32_t acc[JW] = {0u, 0u, 0u, 0u};
+    const uint32_t b32 = (uint32_t)b;
     for (int j = 0; j * STEP < DEG; j++) {
-        gen_step(ring, P, STEP);
+        gen_step(ring, (uint32_t)P, STEP);
         P += STEP;
         __syncthreads();
-        if (w < MT_N) {
-            const int64_t i0 = b + (int64_t)j * STEP + w;
+        if (tid < NT) {
+            // X[b + STEP j + i + w], i < STEP, w < 624: all below P and held (624 + 2 STEP <= RING).
+            const uint32_t *p = ring + ((b32 + (uint32_t)(j * STEP)) & (RING - 1)) + tid;
 #pragma unroll
-            for (int u = 0; u < STEP / 64; u++) {
-                uint64_t gw = __ldg(g + (j * STEP) / 64 + u);
+            for (int u = 0; u < STEP / 32; u++) {
+                const int gi = j * (STEP / 32) + u;
+                uint32_t gw = gi < 2 * PW ? __ldg(g + gi) : 0u;
                 while (gw) {
-                    const int t = __ffsll((long long)gw) - 1;
+                    const int t1 = __ffs(gw) - 1;
                     gw &= gw - 1;
-                    acc ^= ring[(i0 + 64 * u + t) & (RING - 1)];
+                    const int t2 = gw ? __ffs(gw) - 1 : t1;
+                    const uint32_t m2 = gw ? ~0u : 0u;
+                    gw &= gw - 1;
+                    const uint32_t *r1 = p + 32 * u + t1, *r2 = p + 32 * u + t2;
+#pragma unroll
+                    for (int d = 0; d < JW; d++) acc[d] ^= r1[NT * d] ^ (r2[NT * d] & m2);
                 }
             }
         }
     }
     __syncthreads();
     b += dist;
-    if (w < MT_N) ring[(b + w) & (RING - 1)] = acc;
+    if (tid < NT) {
+#pragma unroll
+        for (int d = 0; d < JW; d++) {
+            const uint32_t k = ((uint32_t)b + tid + NT * d) & (RING - 1);
+            ring[k] = acc[d];
+            ring[k + RING] = acc[d];
+        }
+    }
     P = b + MT_N;
     __syncthreads();
 }
 
+// Warps 0..6 generate the stream, STEP words per phase; warps 7..10 turn words produced in
+// earlier phases into keep bits (one element per lane, one 32-bit mask word per warp) and
+// copy out the end state, so conversion overlaps generation.
 __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
-    __shared__ uint32_t ring[RING];
+    __shared__ uint32_t ring[2 * RING];
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int c = blockIdx.x;
 
@@ -346,65 +423,68 @@ __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
     const bool owns_end = (E < G ? 0 : (E - G) / CHUNK) == c;
     if (q >= q_end && !owns_end) return;  // uniform across the CTA
 
-    for (int i = tid; i < MT_N; i += THREADS) ring[i] = a.st_in[i];
+    for (int i = tid; i < MT_N; i += THREADS) ring[i] = ring[i + RING] = a.st_in[i];
     __syncthreads();
     int64_t b = 0, P = MT_N;  // window X[b, b + 624), produced up to P
     if (c > 0) {
         while (P < G + MT_N) {  // the base window at G
             const int cnt = (int)imin(STEP, G + MT_N - P);
-            gen_step(ring, P, cnt);
+            gen_step(ring, (uint32_t)P, cnt);
             P += cnt;
             __syncthreads();
         }
         b = G;
-        const int c0 = c % LEVEL, c1 = c / LEVEL;
-        if (c0) jump_window(ring, a.t0 + (size_t)c0 * PW, b, P, c0 * CHUNK);
-        if (c1) jump_window(ring, a.t1 + (size_t)c1 * PW, b, P, (int64_t)c1 * LEVEL * CHUNK);
+        jump_window(ring, a.tab + (size_t)c * 2 * PW, b, P, c * CHUNK);
     }
+    // Every phase: words below P are visible; generation writes X[P, P + STEP) over the slots
+    // of X[P - RING, P - RING + STEP), while conversion reads at or above pos + 64 q >= P - 624
+    // and the end-state copy at or above E > P - 624 - STEP.
     bool captured = !owns_end;
     while (q < q_end || !captured) {
-        gen_step(ring, P, STEP);
-        P += STEP;
-        __syncthreads();
-        // Up to three mask words whose 64 words are produced.
-        int64_t ready = (P - (pos + 64 * q)) / 64;
-        int cnt = (int)imin(imin(3, q_end - q), ready);
+        const int64_t ready = (P - (pos + 64 * q)) / 64;  // mask words whose words are all below P
+        int cnt = (int)imin(imin(CONV_WARPS, q_end - q), ready);
         if (cnt < 0) cnt = 0;
-        if (warp < 2 * cnt) {
-            const int64_t qq = q + warp / 2, half = warp & 1;
-            const uint32_t y = temper(ring[(pos + 64 * qq + 32 * half + lane) & (RING - 1)]);
-            const uint32_t nxt = __shfl_down_sync(0xffffffffu, y, 1);
-            const int64_t e = 32 * qq + 16 * half + lane / 2;
-            const uint64_t m = ((uint64_t)(y & 0x1fffffu) << 32) | nxt;
-            const bool keep = !(lane & 1) && e < a.n && m < a.thresh;
-            uint32_t x = __ballot_sync(0xffffffffu, keep) & 0x55555555u;
-            x = (x | (x >> 1)) & 0x33333333u;
-            x = (x | (x >> 2)) & 0x0f0f0f0fu;
-            x = (x | (x >> 4)) & 0x00ff00ffu;
-            x = (x | (x >> 8)) & 0x0000ffffu;
-            if (lane == 0) a.bits16[2 * qq + half] = (uint16_t)x;
-        }
-        q += cnt;
-        if (!captured && P >= E + MT_N) {
-            for (int i = tid; i < MT_N; i += THREADS) a.st_out[i] = ring[(E + i) & (RING - 1)];
-            if (tid == 0) {
-                const uint32_t next = (uint32_t)(last - E + 1);
-                a.st_out[MT_N] = 625u - next;
-                a.st_out[MT_N + 1] = next;
+        const bool capture = !captured && P >= E + MT_N;
+        if (warp < GEN_WARPS) {
+            gen_step(ring, (uint32_t)P, STEP);
+        } else {
+            const int cw = warp - GEN_WARPS;
+            if (cw < cnt) {
+                const int64_t e = 32 * (q + cw) + lane;
+                const uint32_t k = (uint32_t)(pos + 2 * e) & (RING - 1);
+                const uint32_t hi32 = temper(ring[k]), lo32 = temper(ring[k + 1]);  // k + 1 < 2 RING
+                const uint64_t m = ((uint64_t)(hi32 & 0x1fffffu) << 32) | lo32;
+                const uint32_t word = __ballot_sync(0xffffffffu, e < a.n && m < a.thresh);
+                if (lane == 0) a.bits[q + cw] = word;
             }
-            captured = true;
+            if (capture) {
+                const int ct = tid - GEN_WARPS * 32;
+                for (int i = ct; i < MT_N; i += THREADS - GEN_WARPS * 32)
+                    a.st_out[i] = ring[((uint32_t)E + i) & (RING - 1)];
+                if (ct == 0) {
+                    const uint32_t next = (uint32_t)(last - E + 1);
+                    a.st_out[MT_N] = 625u - next;
+                    a.st_out[MT_N + 1] = next;
+                }
+            }
         }
+        __syncthreads();
+        P += STEP;
+        q += cnt;
+        captured = captured || capture;
     }
 }
 
-// Per-device copies of the jump tables.
+// Per-device copies of the jump table (MAX_CHUNKS entries reserved, filled on demand).
 constexpr int kTableDevices = 64;
 std::mutex g_tab_mu;
 uint64_t *g_tab_dev[kTableDevices];
+int g_tab_count[kTableDevices];
 
-int device_tables(const uint64_t **t0, const uint64_t **t1) {
-    const JumpTables &T = tables();
+int device_table(int need, const uint32_t **tab) {
+    JumpTables &T = tables();
     if (!T.ok) return fail(DC_ERR_RUNTIME, T.error);
+    const uint64_t *host = table_upto(T, need);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "dropout: current device");
@@ -413,26 +493,26 @@ int device_tables(const uint64_t **t0, const uint64_t **t1) {
     std::lock_guard<std::mutex> lock(g_tab_mu);
     if (!g_tab_dev[dev]) {
         uint64_t *p = nullptr;
-        const size_t bytes = 2 * (size_t)LEVEL * PW * 8;
-        e = cudaMalloc(&p, bytes);
-        if (e != cudaSuccess) return cuda_fail(e, "dropout: jump tables");
-        e = cudaMemcpy(p, T.t0.data(), bytes / 2, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(p + (size_t)LEVEL * PW, T.t1.data(), bytes / 2, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
-            cudaFree(p);
-            return cuda_fail(e, "dropout: jump tables upload");
-        }
+        e = cudaMalloc(&p, (size_t)MAX_CHUNKS * PW * 8);
+        if (e != cudaSuccess) return cuda_fail(e, "dropout: jump table");
         g_tab_dev[dev] = p;
     }
-    *t0 = g_tab_dev[dev];
-    *t1 = g_tab_dev[dev] + (size_t)LEVEL * PW;
+    if (g_tab_count[dev] < need) {
+        // Entries below the old count may be in use by launches in flight; only new ones are
+        // written.
+        const size_t from = (size_t)g_tab_count[dev] * PW;
+        e = cudaMemcpy(g_tab_dev[dev] + from, host + from, ((size_t)need * PW - from) * 8, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, "dropout: jump table upload");
+        g_tab_count[dev] = need;
+    }
+    *tab = reinterpret_cast<const uint32_t *>(g_tab_dev[dev]);
     return DC_OK;
 }
 
 }  // namespace
 
-// Elements per launch: 1022 chunks of words (the two-level table reaches 1024 chunks; one
-// chunk is lost to the head and one to the tail), rounded down to whole mask words.
+// Elements per launch: MAX_CHUNKS - 2 chunks of words (one chunk may be taken by the head and
+// one by the tail), rounded down to whole mask words.
 constexpr int64_t kMaxElemsPerLaunch = ((MAX_CHUNKS - 2) * CHUNK / 2) / 32 * 32;
 
 int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_prob, uint32_t *bits,
@@ -448,14 +528,15 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
         cudaError_t e = cudaMemcpyAsync(st_out, st_in, (MT_N + 2) * 4, cudaMemcpyDeviceToDevice, stream);
         return e == cudaSuccess ? DC_OK : cuda_fail(e, "dropout: state copy");
     }
-    const uint64_t *t0 = nullptr, *t1 = nullptr;
-    int st = device_tables(&t0, &t1);
+    const int64_t launches = (n + kMaxElemsPerLaunch - 1) / kMaxElemsPerLaunch;
+    const int64_t first = imin(kMaxElemsPerLaunch, n);
+    const uint32_t *tab = nullptr;
+    int st = device_table((int)(2 + (2 * first - 1) / CHUNK), &tab);
     if (st) return st;
     int *err = device_error_word();
     if (!err) return fail(DC_ERR_CUDA, "device error word is unavailable");
     // keep iff m * 2^-53 < keep_prob  <=>  m < ceil(keep_prob * 2^53) (the scaling is exact)
     const uint64_t thresh = (uint64_t)ceil(keep_prob * 9007199254740992.0);
-    const int64_t launches = (n + kMaxElemsPerLaunch - 1) / kMaxElemsPerLaunch;
     uint32_t *tmp = nullptr;
     if (launches > 1 || st_out == st_in) {
         st = pool_alloc(reinterpret_cast<void **>(&tmp), 2 * (MT_N + 2) * 4, stream);
@@ -465,9 +546,12 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
     for (int64_t l = 0; l < launches; l++) {
         const int64_t e0 = l * kMaxElemsPerLaunch, ne = imin(kMaxElemsPerLaunch, n - e0);
         uint32_t *dst = l == launches - 1 && st_out != st_in ? st_out : tmp + (l & 1) * (MT_N + 2);
-        KeepArgs a{src, dst, t0, t1, reinterpret_cast<uint16_t *>(bits + e0 / 32), ne, (ne + 31) / 32, thresh, err};
+        KeepArgs a{src, dst, tab, bits + e0 / 32, ne, (ne + 31) / 32, thresh, err};
         const int64_t grid = 2 + (2 * ne - 1) / CHUNK;
-        keep_bits_kernel<<<(unsigned)grid, THREADS, 0, stream>>>(a);
+        {
+            KernelTrace tr("dropout_keep_bits", stream);
+            keep_bits_kernel<<<(unsigned)grid, THREADS, 0, stream>>>(a);
+        }
         st = check_launch("dropout keep bits");
         if (st) {
             pool_free(tmp, stream);
@@ -497,7 +581,7 @@ int rng_skip(const uint32_t *st_in, uint64_t outputs, uint32_t *st_out) {
         return DC_OK;
     }
     if (outputs > (1ull << 36)) return fail(DC_ERR_VALUE, "generator skip: more than 2^36 outputs");
-    const JumpTables &T = tables();
+    JumpTables &T = tables();
     if (!T.ok) return fail(DC_ERR_RUNTIME, T.error);
     const int64_t pos = 625 - (int64_t)left;
     const int64_t B0 = pos == MT_N ? MT_N : 0, G = B0 + MT_N;
@@ -512,11 +596,10 @@ int rng_skip(const uint32_t *st_in, uint64_t outputs, uint32_t *st_out) {
         s.x.resize(MT_N);
         s.base = G;
         int64_t cc = c;
-        while (cc > 0) {  // chunks beyond one table reach walk in steps of the largest jump
-            const int64_t step = cc >= (int64_t)MAX_CHUNKS ? (int64_t)(LEVEL - 1) * LEVEL : cc;
-            const int64_t c0 = step % LEVEL, c1 = step / LEVEL;
-            if (c0) s.jump(&T.t0[(size_t)c0 * PW], c0 * CHUNK);
-            if (c1) s.jump(&T.t1[(size_t)c1 * PW], c1 * LEVEL * CHUNK);
+        while (cc > 0) {  // beyond the table, chain its largest jump
+            const int step = (int)imin(cc, MAX_CHUNKS - 1);
+            const uint64_t *tab = table_upto(T, step + 1);
+            s.jump(tab + (size_t)step * PW, step * CHUNK);
             cc -= step;
         }
     }

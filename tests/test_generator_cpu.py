@@ -12,7 +12,7 @@ import oracle
 from densecore_b200 import _lib
 
 _U32P = ctypes.POINTER(ctypes.c_uint32)
-CHUNK = 624 * 1680  # words per chunk of the library's parallel walk
+CHUNK = 624 * 840  # words per chunk of the library's parallel walk
 
 
 def _skip(state, outputs):

@@ -125,6 +125,33 @@ def test_config_shapes_against_oracle(name, precision):
     _assert_close("lse", glse, lse, TOL[precision])
 
 
+PERSISTENT_CASES = {
+    # More tiles than a B200 has SMs, so the persistent backward kernels loop over several tiles
+    # per CTA: ragged lengths with grouped-query heads (dQ 5 x 80 = 400 tiles, dK/dV 6 x 40 =
+    # 240), keys past the last query under causal masking (dK/dV tiles without query rows), and
+    # a per-batch bool mask.
+    "many_tiles_ragged_gqa": ((4, 20, 640, 64), (4, 10, 700, 64), True, None),
+    "keys_past_queries": ((4, 8, 256, 64), (4, 8, 1024, 64), True, None),
+    "many_tiles_bool_mask": ((2, 24, 512, 64), (2, 24, 512, 64), False, "bool"),
+}
+
+
+@pytest.mark.parametrize("name", sorted(PERSISTENT_CASES))
+def test_many_tiles_per_cta_against_oracle(name, precision):
+    qs, ks, causal, mkind = PERSISTENT_CASES[name]
+    q, k, v, g = _inputs(sum(name.encode()), qs, ks)
+    mask = None
+    if mkind == "bool":
+        mask = np.random.default_rng(3).random((qs[0], 1, qs[2], ks[2])) > 0.2
+    got = _run(q, k, v, g, mask, causal, enable_gqa=qs[1] != ks[1])
+    fm = oracle.flash_mask(mask, q.shape, ks[2])
+    out, lse = oracle.flash_forward(q, k, v, fm, causal)
+    ref = [out, *oracle.flash_backward(g, q, k, v, out, lse, fm, causal)]
+    for nm, a, r in zip(("out", "dq", "dk", "dv"), got, ref):
+        _assert_close(nm, a, r, TOL[precision])
+    assert dc._lib.load().dc_device_status(0) == 0
+
+
 def test_mha_core_key_padding_against_oracle(precision):
     # cfg2's core: (B*H, L, D) with a per-batch key-padding length in [16, 128].
     B, H, L, D = 4, 8, 128, 64
