@@ -13,9 +13,9 @@
 //               the S MMAs read only K from shared memory); each landed K / V tile x is split
 //               in place into hi = tf32(x) and lo = tf32(x - hi) (3xTF32: a*b ~ ah*bh + ah*bl
 //               + al*bh keeps fp32-class accuracy on the TF32 tensor cores).
-//   warps 9, 14 MMA issuers (one thread each, descriptors precomputed): warp 9 issues
+//   warps 9, 14 MMA issuers (whole warps, one elected lane issuing; descriptors precomputed): warp 9 issues
 //               S_j = Q K_j^T into one of two TMEM buffers, warp 14 O_blk = P_j V_j with P read
-//               from TMEM. With two issuers one thread's barrier waits overlap the other's
+//               from TMEM. With two issuers one warp's barrier waits overlap the other's
 //               MMAs, and S_{j+1} runs on the tensor core while the softmax warps work on
 //               block j.
 //   warps 0-7   softmax, two threads per query row (TMEM lane), each owning half of the
@@ -265,17 +265,18 @@ __global__ void __maxnreg__(128)
         }
     } else if (warp == C::W_MMA) {
         // -------------------------------------------------------- MMA issuer: S = Q K^T ----
-        if (lane == 0) {
+        // The whole warp runs the loop converged; one elected lane issues each MMA.
+        {
             // Descriptor of K stage 0; stage and k-step offsets go into the address field.
             const uint64_t kdesc0 = sdesc_sw128(sb + C::OFF_K, 16, 1024);
             const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO;
-            bool ok = mbar_wait(bar(C::Q_READY), 0, abort, err);
+            bool ok = mbar_wait_warp(bar(C::Q_READY), 0, abort, err);
             tc_fence_after();
             for (int j = 0; ok && j < nblk; j++) {
                 const int bb = j & 1, ks = j % C::KST;
                 // S buffer bb held P_{j-2}, read by PV_{j-2}.
-                if (j >= 2 && !mbar_wait(bar(C::PV_DONE_B + bb), ((j - 2) >> 1) & 1, abort, err)) break;
-                if (!mbar_wait(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
+                if (j >= 2 && !mbar_wait_warp(bar(C::PV_DONE_B + bb), ((j - 2) >> 1) & 1, abort, err)) break;
+                if (!mbar_wait_warp(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
                 tc_fence_after();
                 const uint64_t kd = kdesc0 + ((ks * C::KV_STAGE) >> 4);
                 const uint32_t d_s = tmem + C::col_s(bb);
@@ -283,33 +284,33 @@ __global__ void __maxnreg__(128)
 #pragma unroll
                     for (int kk = 0; kk < C::D / 8; kk++) {
                         const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
-                        mma_tf32_ts(d_s, q_hi + kk * 8, kd + ((C::KV_BYTES >> 4) + off), C::IDESC_S, kk > 0 ? 1u : 0u);
-                        mma_tf32_ts(d_s, q_lo + kk * 8, kd + off, C::IDESC_S, 1u);
+                        mma_tf32_ts_w(d_s, q_hi + kk * 8, kd + ((C::KV_BYTES >> 4) + off), C::IDESC_S, kk > 0 ? 1u : 0u);
+                        mma_tf32_ts_w(d_s, q_lo + kk * 8, kd + off, C::IDESC_S, 1u);
                     }
                 }
 #pragma unroll
                 for (int kk = 0; kk < C::D / 8; kk++) {
                     const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
-                    mma_tf32_ts(d_s, q_hi + kk * 8, kd + off, C::IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+                    mma_tf32_ts_w(d_s, q_hi + kk * 8, kd + off, C::IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
                 }
-                tc_commit(bar(C::S_FULL + bb));
-                tc_commit(bar(C::K_EMPTY + ks));
+                tc_commit_w(bar(C::S_FULL + bb));
+                tc_commit_w(bar(C::K_EMPTY + ks));
             }
-            // Every MMA this thread issued completes before TMEM is released.
-            tc_commit(bar(C::DRAIN));
+            // Every MMA this warp issued completes before TMEM is released.
+            tc_commit_w(bar(C::DRAIN));
             volatile int never = 0;
-            mbar_wait(bar(C::DRAIN), 0, &never, nullptr);
+            mbar_wait_warp(bar(C::DRAIN), 0, &never, nullptr);
         }
     } else if (warp == C::W_PV) {
         // ----------------------------------------------------- MMA issuer: O_blk = P V ----
-        if (lane == 0) {
+        {
             const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
             for (int i = 0; i < nblk; i++) {
                 const int bi = i & 1, vs = i % C::VST;
-                if (!mbar_wait(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) break;
-                if (!mbar_wait(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) break;
+                if (!mbar_wait_warp(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) break;
+                if (!mbar_wait_warp(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) break;
                 // O_blk buffer i % NOB held block i - NOB until the softmax threads folded it.
-                if (i >= C::NOB && !mbar_wait(bar(C::OB_FREE + i % C::NOB), ((i / C::NOB) - 1) & 1, abort, err))
+                if (i >= C::NOB && !mbar_wait_warp(bar(C::OB_FREE + i % C::NOB), ((i / C::NOB) - 1) & 1, abort, err))
                     break;
                 const uint32_t d_ob = tmem + C::col_ob(i);
                 tc_fence_after();
@@ -318,20 +319,20 @@ __global__ void __maxnreg__(128)
                 if (SPLIT) {  // the small cross terms first, then the main products
 #pragma unroll
                     for (int kk = 0; kk < C::BN / 8; kk++) {
-                        mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
-                                    kk > 0 ? 1u : 0u);
-                        mma_tf32_ts(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
+                        mma_tf32_ts_w(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
+                                      kk > 0 ? 1u : 0u);
+                        mma_tf32_ts_w(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
                     }
                 }
 #pragma unroll
                 for (int kk = 0; kk < C::BN / 8; kk++)
-                    mma_tf32_ts(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
-                tc_commit(bar(C::PV_DONE_B + bi));
-                tc_commit(bar(C::V_EMPTY + vs));
+                    mma_tf32_ts_w(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
+                tc_commit_w(bar(C::PV_DONE_B + bi));
+                tc_commit_w(bar(C::V_EMPTY + vs));
             }
-            tc_commit(bar(C::DRAIN_PV));
+            tc_commit_w(bar(C::DRAIN_PV));
             volatile int never = 0;
-            mbar_wait(bar(C::DRAIN_PV), 0, &never, nullptr);
+            mbar_wait_warp(bar(C::DRAIN_PV), 0, &never, nullptr);
         }
     } else if (warp >= C::W_CVT && warp < C::W_PV) {
         // --------------------------------------------------------------- converters ----

@@ -30,7 +30,7 @@
 //         the 64 dQ columns).
 //
 // Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer of S
-// and dP (one thread; it also owns TMEM), warp 10 a second TMA producer (the MN-major ring, so
+// and dP (the whole warp, converged, with one elected lane issuing; it also owns TMEM), warp 10 a second TMA producer (the MN-major ring, so
 // that the K-major ring can run ahead of it), warp 11 MMA issuer of the gradients (so that
 // either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout
 // records an error and unwinds. The softmax loops stay branch-free per column (validity as a
@@ -91,13 +91,13 @@ __device__ __forceinline__ void mma_s(uint32_t d, uint32_t a_hi, uint64_t a_lo, 
     if (SPLIT) {
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++) {
-            mma_tf32_ts(d, a_hi + kk * 8, b_hi + (BLO + koff<BLK_CHUNK>(kk)), IDESC_S, kk > 0 ? 1u : 0u);
-            mma_tf32_ss(d, a_lo + koff<RES_CHUNK>(kk), b_hi + koff<BLK_CHUNK>(kk), IDESC_S, 1u);
+            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<BLK_CHUNK>(kk)), IDESC_S, kk > 0 ? 1u : 0u);
+            mma_tf32_ss_w(d, a_lo + koff<RES_CHUNK>(kk), b_hi + koff<BLK_CHUNK>(kk), IDESC_S, 1u);
         }
     }
 #pragma unroll
     for (int kk = 0; kk < D / 8; kk++)
-        mma_tf32_ts(d, a_hi + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
 }
 
 // Gradient-type product over BLK (3 passes with SPLIT): d (+)= A B with A hi / lo in TMEM and
@@ -108,13 +108,13 @@ __device__ __forceinline__ void mma_g(uint32_t d, uint32_t a_hi, uint32_t a_lo, 
     if (SPLIT) {
 #pragma unroll
         for (int kk = 0; kk < BLK / 8; kk++) {
-            mma_tf32_ts(d, a_hi + kk * 8, b_hi + (BLO + mnoff(kk)), IDESC_G, (accumulate || kk > 0) ? 1u : 0u);
-            mma_tf32_ts(d, a_lo + kk * 8, b_hi + mnoff(kk), IDESC_G, 1u);
+            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + mnoff(kk)), IDESC_G, (accumulate || kk > 0) ? 1u : 0u);
+            mma_tf32_ts_w(d, a_lo + kk * 8, b_hi + mnoff(kk), IDESC_G, 1u);
         }
     }
 #pragma unroll
     for (int kk = 0; kk < BLK / 8; kk++)
-        mma_tf32_ts(d, a_hi + kk * 8, b_hi + mnoff(kk), IDESC_G, (accumulate || SPLIT || kk > 0) ? 1u : 0u);
+        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + mnoff(kk), IDESC_G, (accumulate || SPLIT || kk > 0) ? 1u : 0u);
 }
 
 // Row `row` of a 128-byte-swizzled TILE-row tile in shared memory into TMEM columns
@@ -420,48 +420,48 @@ __global__ void __maxnreg__(168)
         }
     } else if (warp == W_MMA) {
         // ------------------------------------------------------- MMA: S^T and dP^T ------
-        if (lane == 0) {
+        {  // the whole warp, converged; one elected lane issues
             const uint64_t klo = sdesc_sw128(sb + OFF_KLO, 16, 1024), vlo = sdesc_sw128(sb + OFF_VLO, 16, 1024);
-            bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
+            bool ok = warp_wait(bar(KV_READY), 0, abort, err);
             tc_fence_after();
             for (int i = 0; ok && i < nblk; i++) {
                 const int ss = i % NSS, bb = i & 1;
                 const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
                 // Buffer bb holds P^T / dS^T of block i-2 until its gradient MMAs finish.
-                if (i >= 2 && !mbar_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
-                if (!mbar_wait(bar(SS_FULL + ss), (i / NSS) & 1, abort, err)) break;
+                if (i >= 2 && !warp_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(SS_FULL + ss), (i / NSS) & 1, abort, err)) break;
                 tc_fence_after();
                 mma_s<SPLIT>(tmem + c_s(bb), tmem + C_KHI, klo, sdesc_sw128(sst + SS_QK, 16, 1024));
                 mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_VHI, vlo, sdesc_sw128(sst + SS_DOK, 16, 1024));
-                tc_commit(bar(S_FULL + bb));
-                tc_commit(bar(SS_EMPTY + ss));
+                tc_commit_w(bar(S_FULL + bb));
+                tc_commit_w(bar(SS_EMPTY + ss));
             }
-            tc_commit(bar(DRAIN));
+            tc_commit_w(bar(DRAIN));
             volatile int never = 0;
-            mbar_wait(bar(DRAIN), 0, &never, nullptr);
+            warp_wait(bar(DRAIN), 0, &never, nullptr);
         }
     } else if (warp == W_GMMA) {
         // ------------------------------------------------ MMA: dV_blk and dK_blk ------
-        if (lane == 0) {
+        {  // the whole warp, converged; one elected lane issues
             for (int i = 0; i < nblk; i++) {
                 const int sgi = i % NSG, bb = i & 1;
                 const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
-                if (!mbar_wait(bar(P_FULL + bb), (i >> 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(P_FULL + bb), (i >> 1) & 1, abort, err)) break;
                 const bool first = (i % FOLD) == 0;
-                if (first && i >= FOLD && !mbar_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, err)) break;
-                if (!mbar_wait(bar(SG_FULL + sgi), (i / NSG) & 1, abort, err)) break;
+                if (first && i >= FOLD && !warp_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(SG_FULL + sgi), (i / NSG) & 1, abort, err)) break;
                 tc_fence_after();
                 mma_g<SPLIT>(tmem + C_DV, tmem + c_s(bb), tmem + c_plo(bb),
                              sdesc_mn_sw128_32b(gst + SG_DOMN, BLK_CHUNK, 512), !first);
                 mma_g<SPLIT>(tmem + C_DK, tmem + c_dp(bb), tmem + c_dslo(bb),
                              sdesc_mn_sw128_32b(gst + SG_QMN, BLK_CHUNK, 512), !first);
-                tc_commit(bar(G_DONE + bb));
-                if ((i % FOLD) == FOLD - 1 || i == nblk - 1) tc_commit(bar(CHAIN_DONE));
-                tc_commit(bar(SG_EMPTY + sgi));
+                tc_commit_w(bar(G_DONE + bb));
+                if ((i % FOLD) == FOLD - 1 || i == nblk - 1) tc_commit_w(bar(CHAIN_DONE));
+                tc_commit_w(bar(SG_EMPTY + sgi));
             }
-            tc_commit(bar(DRAIN_G));
+            tc_commit_w(bar(DRAIN_G));
             volatile int never = 0;
-            mbar_wait(bar(DRAIN_G), 0, &never, nullptr);
+            warp_wait(bar(DRAIN_G), 0, &never, nullptr);
         }
     } else if (warp < W_PROD) {
         // ---------------------------------- P^T and dS^T, then the fp32 dV / dK folds ----
@@ -728,46 +728,46 @@ __global__ void __maxnreg__(168)
         }
     } else if (warp == W_MMA) {
         // ------------------------------------------------------------ MMA: S and dP ------
-        if (lane == 0) {
+        {  // the whole warp, converged; one elected lane issues
             const uint64_t qlo = sdesc_sw128(sb + OFF_QLO, 16, 1024), dolo = sdesc_sw128(sb + OFF_DOLO, 16, 1024);
-            bool ok = mbar_wait(bar(QD_READY), 0, abort, err);
+            bool ok = warp_wait(bar(QD_READY), 0, abort, err);
             tc_fence_after();
             for (int j = 0; ok && j < nblk; j++) {
                 const int ss = j % NSS, bb = j & 1;
                 const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
                 // Buffer bb holds dS of block j-2 until its gradient MMAs finish.
-                if (j >= 2 && !mbar_wait(bar(G_DONE + bb), ((j - 2) >> 1) & 1, abort, err)) break;
-                if (!mbar_wait(bar(SS_FULL + ss), (j / NSS) & 1, abort, err)) break;
+                if (j >= 2 && !warp_wait(bar(G_DONE + bb), ((j - 2) >> 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(SS_FULL + ss), (j / NSS) & 1, abort, err)) break;
                 tc_fence_after();
                 mma_s<SPLIT>(tmem + c_s(bb), tmem + C_QHI, qlo, sdesc_sw128(sst + SS_KK, 16, 1024));
                 mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_DOHI, dolo, sdesc_sw128(sst + SS_VK, 16, 1024));
-                tc_commit(bar(S_FULL + bb));
-                tc_commit(bar(SS_EMPTY + ss));
+                tc_commit_w(bar(S_FULL + bb));
+                tc_commit_w(bar(SS_EMPTY + ss));
             }
-            tc_commit(bar(DRAIN));
+            tc_commit_w(bar(DRAIN));
             volatile int never = 0;
-            mbar_wait(bar(DRAIN), 0, &never, nullptr);
+            warp_wait(bar(DRAIN), 0, &never, nullptr);
         }
     } else if (warp == W_GMMA) {
         // ---------------------------------------------------------------- MMA: dQ_blk ----
-        if (lane == 0) {
+        {  // the whole warp, converged; one elected lane issues
             for (int j = 0; j < nblk; j++) {
                 const int sgi = j % NSG, bb = j & 1;
                 const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
-                if (!mbar_wait(bar(DS_FULL + bb), (j >> 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(DS_FULL + bb), (j >> 1) & 1, abort, err)) break;
                 const bool first = (j % FOLD) == 0;
-                if (first && j >= FOLD && !mbar_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, err)) break;
-                if (!mbar_wait(bar(SG_FULL + sgi), (j / NSG) & 1, abort, err)) break;
+                if (first && j >= FOLD && !warp_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(SG_FULL + sgi), (j / NSG) & 1, abort, err)) break;
                 tc_fence_after();
                 mma_g<SPLIT>(tmem + C_DQB, tmem + c_dp(bb), tmem + c_dslo(bb),
                              sdesc_mn_sw128_32b(gst + SG_KMN, BLK_CHUNK, 512), !first);
-                tc_commit(bar(G_DONE + bb));
-                if ((j % FOLD) == FOLD - 1 || j == nblk - 1) tc_commit(bar(CHAIN_DONE));
-                tc_commit(bar(SG_EMPTY + sgi));
+                tc_commit_w(bar(G_DONE + bb));
+                if ((j % FOLD) == FOLD - 1 || j == nblk - 1) tc_commit_w(bar(CHAIN_DONE));
+                tc_commit_w(bar(SG_EMPTY + sgi));
             }
-            tc_commit(bar(DRAIN_G));
+            tc_commit_w(bar(DRAIN_G));
             volatile int never = 0;
-            mbar_wait(bar(DRAIN_G), 0, &never, nullptr);
+            warp_wait(bar(DRAIN_G), 0, &never, nullptr);
         }
     } else if (warp < W_PROD) {
         // ----------------------------------------------------- dS, then the fp32 dQ fold --

@@ -72,6 +72,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// mbar_wait by a whole converged warp with one outcome for every lane, so that the
+// warp-collective instructions after it (tcgen05.ld / st, elect.sync issue) run converged.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int *abort, int *err_flag) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, err_flag));
+}
+
 // ---------------------------------------------------------------------- TMA -------
 // 4-D tiled load of a box into shared memory, completing on `bar` (transaction bytes).
 __device__ __forceinline__ void tma_load_4d(const CUtensorMap *map, uint32_t dst, uint32_t bar,
@@ -136,6 +142,39 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      bar)
                  : "memory");
+}
+
+// Warp-issued forms: all 32 lanes of a converged warp call these with the same arguments and
+// one lane (elect.sync) issues. Measured on B200 (one CTA per SM, kind::tf32, M = 128): a
+// converged warp issues back-to-back MMAs at the tensor core's own rate (about 18 cycles at
+// N = 32, 33 at N = 64, N/2 beyond), while a single lane inside a divergent branch
+// (`if (lane == 0)`) needs about 46 cycles per MMA whatever N.
+__device__ __forceinline__ void mma_tf32_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit_w(uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+        : "memory");
 }
 
 #define DC_TMEM_REGS32(r)                                                                       \

@@ -130,8 +130,10 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.
     As DenseCore's: a boolean mask is True where attention is allowed, a float mask is added to
     the scores; is_causal applies a top-left lower-triangular mask and cannot be combined with
     attn_mask; scale defaults to 1/sqrt(E). Fully masked rows give 0 (and zero gradients).
-    Differences: dropout_p > 0 raises NotImplementedError (DenseCore leaves the fused path
-    for it); grouped-query heads run natively instead of widening K/V.
+    dropout_p > 0 draws the keep bits from the default generator's stream, exactly as
+    DenseCore's math path draws them (functional.py:318-340, :638-641).
+    Differences: dropout runs in the fused kernels instead of the math path; grouped-query
+    heads run natively instead of widening K/V.
     """
     for name, t in (("query", query), ("key", key), ("value", value)):
         if not isinstance(t, torch.Tensor):
