@@ -117,7 +117,7 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) 
     else tmem_st16(taddr, r);
 }
 
-// hi = tf32(x) in place and, with SPLIT, lo = tf32(x - hi) `lo_off` bytes further.
+// hi = tf32(x) in place and, with SPLIT, lo = x - hi (tf32_lo) `lo_off` bytes further.
 // Single-pass TF32 rounds to nearest here rather than letting the tensor core drop the low
 // mantissa bits (which would bias every operand toward zero).
 template <bool SPLIT>
@@ -133,10 +133,10 @@ __device__ __forceinline__ void split_tile(uint8_t *hi, uint32_t lo_off, uint32_
         *ph = hv;
         if (SPLIT) {
             float4 lv;
-            lv.x = __uint_as_float(tf32_rna(x.x - hv.x));
-            lv.y = __uint_as_float(tf32_rna(x.y - hv.y));
-            lv.z = __uint_as_float(tf32_rna(x.z - hv.z));
-            lv.w = __uint_as_float(tf32_rna(x.w - hv.w));
+            lv.x = __uint_as_float(tf32_lo(x.x, __float_as_uint(hv.x)));
+            lv.y = __uint_as_float(tf32_lo(x.y, __float_as_uint(hv.y)));
+            lv.z = __uint_as_float(tf32_lo(x.z, __float_as_uint(hv.z)));
+            lv.w = __uint_as_float(tf32_lo(x.w, __float_as_uint(hv.w)));
             *(reinterpret_cast<float4 *>(hi + lo_off) + i) = lv;
         }
     }
@@ -441,7 +441,7 @@ __global__ void __maxnreg__(128)
                     const float pc = dead ? 0.0f : ex2_approx(s[r0 + c] - m);
                     rs += pc;
                     phi[c] = tf32_rna(pc);
-                    if (SPLIT) plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
+                    if (SPLIT) plo[c] = tf32_lo(pc, phi[c]);
                 }
                 tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
                 if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);

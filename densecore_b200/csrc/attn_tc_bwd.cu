@@ -23,8 +23,8 @@
 //         tensor core while the softmax warps work on block i. The same warps add the block
 //         accumulators into fp32 registers every FOLD blocks (the tensor core's accumulation is
 //         coarser than fp32 over long chains): the first four keep dV, the other four dK.
-//   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi in
-//         TMEM, lo in shared memory); 32-key blocks of K and V (K-major, 4 stages) and of K
+//   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi and
+//         lo in TMEM, so that no pass reads A from shared memory); 32-key blocks of K and V (K-major, 4 stages) and of K
 //         (MN-major, 2 stages) stream through two rings. Per block: S = Q K^T and dP = dO V^T,
 //         dS in TMEM, dQ_blk += dS K, folded into fp32 registers (each softmax warp keeps 32 of
 //         the 64 dQ columns).
@@ -93,6 +93,24 @@ __device__ __forceinline__ void mma_s(uint32_t d, uint32_t a_hi, uint64_t a_lo, 
         for (int kk = 0; kk < D / 8; kk++) {
             mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<BLK_CHUNK>(kk)), IDESC_S, kk > 0 ? 1u : 0u);
             mma_tf32_ss_w(d, a_lo + koff<RES_CHUNK>(kk), b_hi + koff<BLK_CHUNK>(kk), IDESC_S, 1u);
+        }
+    }
+#pragma unroll
+    for (int kk = 0; kk < D / 8; kk++)
+        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+}
+
+// mma_s with A_lo in TMEM too (columns a_lo + 8 kk): every pass reads A from TMEM and only
+// the streamed B tile from shared memory. An A operand in shared memory costs the tensor core
+// 4 KB of shared-memory reads per k-step, more than the whole N = 32 product.
+template <bool SPLIT>
+__device__ __forceinline__ void mma_s_t(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t b_hi) {
+    constexpr uint32_t BLO = BLK_BYTES >> 4;
+    if (SPLIT) {
+#pragma unroll
+        for (int kk = 0; kk < D / 8; kk++) {
+            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<BLK_CHUNK>(kk)), IDESC_S, kk > 0 ? 1u : 0u);
+            mma_tf32_ts_w(d, a_lo + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, 1u);
         }
     }
 #pragma unroll
@@ -541,8 +559,8 @@ __global__ void __maxnreg__(168)
                 phi[c] = tf32_rna(pc);
                 sr[c] = tf32_rna(ds);
                 if (SPLIT) {
-                    plo[c] = tf32_rna(pc - __uint_as_float(phi[c]));
-                    dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
+                    plo[c] = tf32_lo(pc, phi[c]);
+                    dr[c] = tf32_lo(ds, sr[c]);
                 }
             }
             tmem_st16(tl + c_s(bb) + cb, phi);
@@ -596,8 +614,8 @@ enum { QD_FULL, QD_READY, SS_FULL, SS_EMPTY = SS_FULL + NSS, SG_FULL = SS_EMPTY 
        DRAIN, DRAIN_G, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
-// TMEM: Q hi | dO hi | 2 x (S, dP / dS hi, dS lo) | dQ_blk
-constexpr uint32_t C_QHI = 0, C_DOHI = 64, C_DQB = 320, TCOLS = 512;
+// TMEM: Q hi | dO hi | 2 x (S, dP / dS hi, dS lo) | dQ_blk | Q lo | dO lo
+constexpr uint32_t C_QHI = 0, C_DOHI = 64, C_DQB = 320, C_QLO = 384, C_DOLO = 448, TCOLS = 512;
 __device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 96; }
 __device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 160 + b * 96; }
 __device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 192 + b * 96; }
@@ -729,7 +747,6 @@ __global__ void __maxnreg__(168)
     } else if (warp == W_MMA) {
         // ------------------------------------------------------------ MMA: S and dP ------
         {  // the whole warp, converged; one elected lane issues
-            const uint64_t qlo = sdesc_sw128(sb + OFF_QLO, 16, 1024), dolo = sdesc_sw128(sb + OFF_DOLO, 16, 1024);
             bool ok = warp_wait(bar(QD_READY), 0, abort, err);
             tc_fence_after();
             for (int j = 0; ok && j < nblk; j++) {
@@ -739,8 +756,8 @@ __global__ void __maxnreg__(168)
                 if (j >= 2 && !warp_wait(bar(G_DONE + bb), ((j - 2) >> 1) & 1, abort, err)) break;
                 if (!warp_wait(bar(SS_FULL + ss), (j / NSS) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_QHI, qlo, sdesc_sw128(sst + SS_KK, 16, 1024));
-                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_DOHI, dolo, sdesc_sw128(sst + SS_VK, 16, 1024));
+                mma_s_t<SPLIT>(tmem + c_s(bb), tmem + C_QHI, tmem + C_QLO, sdesc_sw128(sst + SS_KK, 16, 1024));
+                mma_s_t<SPLIT>(tmem + c_dp(bb), tmem + C_DOHI, tmem + C_DOLO, sdesc_sw128(sst + SS_VK, 16, 1024));
                 tc_commit_w(bar(S_FULL + bb));
                 tc_commit_w(bar(SS_EMPTY + ss));
             }
@@ -781,8 +798,9 @@ __global__ void __maxnreg__(168)
 #pragma unroll
         for (int x = 0; x < D / 2; x++) acc[x] = 0.0f;
         bool ok = warp_wait(bar(QD_FULL), 0, abort, err);
-        if (ok) {  // Q (half 0) or dO (half 1) hi rows into TMEM
+        if (ok) {  // Q (half 0) or dO (half 1) hi and lo rows into TMEM
             row_to_tmem(sg + half * RES_BYTES, row, tl, half ? C_DOHI : C_QHI);
+            if (SPLIT) row_to_tmem(sg + (half ? OFF_DOLO : OFF_QLO), row, tl, half ? C_DOLO : C_QLO);
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
@@ -834,7 +852,7 @@ __global__ void __maxnreg__(168)
                 const float pc = ((vbits >> c) & 1u) ? ex2_approx(__uint_as_float(sr[c]) - lse2) : 0.0f;
                 const float ds = pc * (__uint_as_float(dr[c]) - del);
                 sr[c] = tf32_rna(ds);
-                if (SPLIT) dr[c] = tf32_rna(ds - __uint_as_float(sr[c]));
+                if (SPLIT) dr[c] = tf32_lo(ds, sr[c]);
             }
             tmem_st16(tl + c_dp(bb) + cb, sr);
             if (SPLIT) tmem_st16(tl + c_dslo(bb) + cb, dr);

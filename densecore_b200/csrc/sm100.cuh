@@ -281,5 +281,14 @@ __device__ __forceinline__ uint32_t tf32_rna(float x) {
     return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 
+// The low part of a 3xTF32 split, lo = x - hi with hi = tf32_rna(x): exact in fp32 (at most
+// 13 significant bits) and handed to the tensor core unrounded, which reads only its top 11
+// significant bits. That truncation errs by less than 2^-10 of lo, below 2^-22 of x; as lo
+// takes either sign (hi rounds to nearest), the errors do not accumulate in one direction.
+// One FADD instead of a further round to nearest on the softmax warps' critical path.
+__device__ __forceinline__ uint32_t tf32_lo(float x, uint32_t hi) {
+    return __float_as_uint(x - __uint_as_float(hi));
+}
+
 }  // namespace sm100
 }  // namespace dc
