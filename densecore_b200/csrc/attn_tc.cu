@@ -142,6 +142,19 @@ __device__ __forceinline__ void split_tile(uint8_t *hi, uint32_t lo_off, uint32_
     }
 }
 
+// max over N values as a balanced tree (a dependency chain of log2 N instead of N).
+template <int N>
+__device__ __forceinline__ float max_tree(const float (&v)[N]) {
+    float t[N / 2];
+#pragma unroll
+    for (int i = 0; i < N / 2; i++) t[i] = fmaxf(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+    for (int w = N / 4; w >= 1; w /= 2)
+#pragma unroll
+        for (int i = 0; i < w; i++) t[i] = fmaxf(t[2 * i], t[2 * i + 1]);
+    return t[0];
+}
+
 // Row `row` of a raw 128-byte-swizzled tile (rows of 128-byte chunks, chunk stride
 // `chunk_bytes`) into TMEM: tf32 hi at col_hi and, with SPLIT, lo at col_lo.
 template <int CHUNKS, bool SPLIT>
@@ -399,22 +412,18 @@ __global__ void __maxnreg__(128)
 #pragma unroll
                 for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(r[x]);
             }
-            float bmax = -INFINITY;
             if (!edge) {
 #pragma unroll
-                for (int c = 0; c < C::HB; c++) {
-                    s[c] *= a.scale_log2;
-                    bmax = fmaxf(bmax, s[c]);
-                }
+                for (int c = 0; c < C::HB; c++) s[c] *= a.scale_log2;
             } else {
 #pragma unroll
                 for (int c = 0; c < C::HB; c++) {
                     float x = s[c] * a.scale_log2;
                     if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
                     s[c] = ((vbits >> c) & 1u) ? x : -INFINITY;
-                    bmax = fmaxf(bmax, s[c]);
                 }
             }
+            float bmax = max_tree<C::HB>(s);
             // The block's row max, shared with the partner thread (the other half) through
             // shared memory and an mbarrier (a bounded wait, unlike bar.sync).
             xmax[(bb * 2 + half) * C::BM + row] = bmax;
@@ -432,20 +441,21 @@ __global__ void __maxnreg__(128)
                 m = m_new;
             }
             const bool dead = (m == -INFINITY);
-            float rs = 0.0f;
+            float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four partial row sums: shorter chains
 #pragma unroll
             for (int r0 = 0; r0 < C::HB; r0 += 16) {  // P in 16-column pieces
                 uint32_t phi[16], plo[16];
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
                     const float pc = dead ? 0.0f : ex2_approx(s[r0 + c] - m);
-                    rs += pc;
+                    part[c & 3] += pc;
                     phi[c] = tf32_rna(pc);
                     if (SPLIT) plo[c] = tf32_lo(pc, phi[c]);
                 }
                 tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
                 if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);
             }
+            const float rs = (part[0] + part[1]) + (part[2] + part[3]);
             l = fmaf(l, corr, rs);
             tmem_wait_st();
             tc_fence_before();
@@ -460,13 +470,19 @@ __global__ void __maxnreg__(128)
                     break;
                 }
                 tc_fence_after();
+                const bool scaled = __any_sync(0xffffffffu, corr != 1.0f);
 #pragma unroll
                 for (int c = 0; c < C::HD / 16; c++) {
                     uint32_t r[16];
                     tmem_ld16(tl + C::col_ob(j - 1) + half * C::HD + 16 * c, r);
                     tmem_wait_ld();
+                    if (scaled) {
 #pragma unroll
-                    for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(r[x])) * corr;
+                        for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(r[x])) * corr;
+                    } else {
+#pragma unroll
+                        for (int x = 0; x < 16; x++) o[16 * c + x] += __uint_as_float(r[x]);
+                    }
                 }
                 tc_fence_before();
                 mbar_arrive(bar(C::OB_FREE + (j - 1) % C::NOB));

@@ -24,20 +24,22 @@
 //         accumulators into fp32 registers every FOLD blocks (the tensor core's accumulation is
 //         coarser than fp32 over long chains): the first four keep dV, the other four dK.
 //   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi and
-//         lo in TMEM, so that no pass reads A from shared memory); 32-key blocks of K and V (K-major, 4 stages) and of K
-//         (MN-major, 2 stages) stream through two rings. Per block: S = Q K^T and dP = dO V^T,
-//         dS in TMEM, dQ_blk += dS K, folded into fp32 registers (each softmax warp keeps 32 of
-//         the 64 dQ columns).
+//         lo in TMEM, so that no pass reads A from shared memory); 64-key blocks of K and V
+//         (K-major) and of K (MN-major) stream through three two-stage rings. Per
+//         block: S = Q K^T and dP = dO V^T (N = 64), dS in TMEM, dQ_blk = dS K, folded into
+//         fp32 registers (each softmax warp keeps 32 of the 64 dQ columns). The S, dP and dQ
+//         columns are single; the order in which one warp issues the MMAs keeps the tensor
+//         core busy (see the kernel).
 //
-// Roles (both kernels): warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer of S
-// and dP (the whole warp, converged, with one elected lane issuing; it also owns TMEM), warp 10 a second TMA producer (the MN-major ring, so
-// that the K-major ring can run ahead of it), warp 11 MMA issuer of the gradients (so that
-// either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout
-// records an error and unwinds. The softmax loops stay branch-free per column (validity as a
-// bit mask; a user mask in a separate pass) to keep the hot code small: twelve warps running
-// different loops already crowd the instruction cache. Grids are 1-D: groups of GROUP_HEADS (batch, head) pairs, and within a group the
-// tiles with the most causal work first. The group keeps the streamed operands of its heads
-// in L2; the order within it keeps the last wave short.
+// Roles: warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer (the whole warp,
+// converged, with one elected lane issuing; it also owns TMEM), warp 10 a second TMA producer
+// (the MN-major ring, so that the K-major ring can run ahead of it), warp 11 the gradient MMAs
+// (so that either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout records an error and unwinds. The softmax loops stay
+// branch-free per column (validity as a bit mask; a user mask in a separate pass) to keep the
+// hot code small: twelve warps running different loops already crowd the instruction cache.
+// Grids are 1-D: groups of GROUP_HEADS (batch, head) pairs, and within a group the tiles with
+// the most causal work first. The group keeps the streamed operands of its heads in L2; the
+// order within it keeps the last wave short.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -100,38 +102,40 @@ __device__ __forceinline__ void mma_s(uint32_t d, uint32_t a_hi, uint64_t a_lo, 
         mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
 }
 
-// mma_s with A_lo in TMEM too (columns a_lo + 8 kk): every pass reads A from TMEM and only
-// the streamed B tile from shared memory. An A operand in shared memory costs the tensor core
-// 4 KB of shared-memory reads per k-step, more than the whole N = 32 product.
-template <bool SPLIT>
+// mma_s with A_lo in TMEM too (columns a_lo + 8 kk) and an NB-row streamed B tile (N = NB):
+// every pass reads A from TMEM and only the streamed B tile from shared memory. An A operand in
+// shared memory costs the tensor core 4 KB of shared-memory reads per k-step, more than the
+// whole N = 32 product.
+template <bool SPLIT, int NB = BLK>
 __device__ __forceinline__ void mma_s_t(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t b_hi) {
-    constexpr uint32_t BLO = BLK_BYTES >> 4;
+    constexpr uint32_t BLO = (uint32_t)(NB * D * 4) >> 4, CH = NB * 128;
+    constexpr uint32_t ID = idesc_tf32(128, NB, 0, 0);
     if (SPLIT) {
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++) {
-            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<BLK_CHUNK>(kk)), IDESC_S, kk > 0 ? 1u : 0u);
-            mma_tf32_ts_w(d, a_lo + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, 1u);
+            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<CH>(kk)), ID, kk > 0 ? 1u : 0u);
+            mma_tf32_ts_w(d, a_lo + kk * 8, b_hi + koff<CH>(kk), ID, 1u);
         }
     }
 #pragma unroll
     for (int kk = 0; kk < D / 8; kk++)
-        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<CH>(kk), ID, (SPLIT || kk > 0) ? 1u : 0u);
 }
 
-// Gradient-type product over BLK (3 passes with SPLIT): d (+)= A B with A hi / lo in TMEM and
-// B hi / lo MN-major in shared memory (descriptor b_hi, lo BLK_BYTES further).
-template <bool SPLIT>
+// Gradient-type product over NB rows (3 passes with SPLIT): d (+)= A B with A hi / lo in TMEM
+// and B hi / lo MN-major in shared memory (descriptor b_hi, lo NB * D * 4 bytes further).
+template <bool SPLIT, int NB = BLK>
 __device__ __forceinline__ void mma_g(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t b_hi, bool accumulate) {
-    constexpr uint32_t BLO = BLK_BYTES >> 4;
+    constexpr uint32_t BLO = (uint32_t)(NB * D * 4) >> 4;
     if (SPLIT) {
 #pragma unroll
-        for (int kk = 0; kk < BLK / 8; kk++) {
+        for (int kk = 0; kk < NB / 8; kk++) {
             mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + mnoff(kk)), IDESC_G, (accumulate || kk > 0) ? 1u : 0u);
             mma_tf32_ts_w(d, a_lo + kk * 8, b_hi + mnoff(kk), IDESC_G, 1u);
         }
     }
 #pragma unroll
-    for (int kk = 0; kk < BLK / 8; kk++)
+    for (int kk = 0; kk < NB / 8; kk++)
         mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + mnoff(kk), IDESC_G, (accumulate || SPLIT || kk > 0) ? 1u : 0u);
 }
 
@@ -164,6 +168,13 @@ __device__ __forceinline__ uint32_t col_bits(int64_t lo, int64_t hi) {
     lo = lo < 0 ? 0 : lo;
     hi = hi > 16 ? 16 : hi;
     return hi > lo ? ((0xFFFFu >> (16 - (int)(hi - lo))) << (int)lo) : 0u;
+}
+
+// Bit c set for the columns c of [lo, hi) within 0..31.
+__device__ __forceinline__ uint32_t col_bits32(int64_t lo, int64_t hi) {
+    lo = lo < 0 ? 0 : lo;
+    hi = hi > 32 ? 32 : hi;
+    return hi > lo ? ((0xFFFFFFFFu >> (32 - (int)(hi - lo))) << (int)lo) : 0u;
 }
 
 // Adds 16 TMEM columns of this lane into acc[0..15].
@@ -600,31 +611,42 @@ __global__ void __maxnreg__(168)
 
 // ========================================================================= dQ ========
 namespace qq {
-// Two rings as in dkdv: K-major K and V tiles (S / dP MMAs; 4 stages) and MN-major K tiles
-// (the dQ MMA; 2 stages).
-constexpr int NSS = 4, NSG = 2;
-// S stage: K_K hi, lo | V_K hi, lo; G stage: K_MN hi, lo (8 KB tiles)
-constexpr uint32_t SS_KK = 0, SS_VK = 2 * BLK_BYTES, SG_KMN = 0;
-constexpr uint32_t SSTAGE = 4 * BLK_BYTES, GSTAGE = 2 * BLK_BYTES;  // 32 KB, 16 KB
-constexpr uint32_t OFF_SRING = 0, OFF_GRING = NSS * SSTAGE;
-constexpr uint32_t OFF_QLO = OFF_GRING + NSG * GSTAGE, OFF_DOLO = OFF_QLO + RES_BYTES;
-constexpr uint32_t OFF_BAR = OFF_DOLO + RES_BYTES;
-enum { QD_FULL, QD_READY, SS_FULL, SS_EMPTY = SS_FULL + NSS, SG_FULL = SS_EMPTY + NSS, SG_EMPTY = SG_FULL + NSG,
-       S_FULL = SG_EMPTY + NSG, DS_FULL = S_FULL + 2, G_DONE = DS_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE,
-       DRAIN, DRAIN_G, NBAR };
+// 64-key blocks: the S / dP products run at N = 64, where a tensor-core MMA does twice the work
+// of an N = 32 one for a little more time.
+constexpr int NB = 64;
+constexpr uint32_t NB_BYTES = NB * D * 4;  // one streamed fp32 tile (16 KB)
+constexpr uint32_t NB_CHUNK = NB * 128;    // 8 KB per 32-column chunk
+// Three rings of two stages, each stage a tile's hi and lo copies (32 KB), each freed by its
+// own reader: K (K-major) by the S MMAs, V (K-major) by the dP MMAs, K (MN-major) by the dQ
+// MMAs. Separate rings give every load about two blocks of lead time.
+constexpr int NST = 2;
+constexpr uint32_t STAGE = 2 * NB_BYTES;
+constexpr uint32_t OFF_KK = 0, OFF_VK = NST * STAGE, OFF_KMN = 2 * NST * STAGE;
+// Until they are in TMEM, Q hi / dO hi wait in the K ring and Q lo / dO lo in the V ring.
+constexpr uint32_t OFF_QHI = OFF_KK, OFF_DOHI = OFF_KK + RES_BYTES, OFF_QLO = OFF_VK, OFF_DOLO = OFF_VK + RES_BYTES;
+constexpr uint32_t OFF_BAR = 3 * NST * STAGE;
+// Per block j: S (S_FULL) read out by the softmax warps (S_READ: S_{j+1} may overwrite it);
+// dP (DP_FULL) turned into dS hi / lo (DS_READY); dQ_blk = dS K (DQ_DONE: dS read, dP_{j+1}
+// may overwrite it) folded into registers (DQ_FREE: the accumulator may restart).
+enum { QD_FULL, QD_READY, KK_FULL, KK_EMPTY = KK_FULL + NST, VK_FULL = KK_EMPTY + NST, VK_EMPTY = VK_FULL + NST,
+       SG_FULL = VK_EMPTY + NST, SG_EMPTY = SG_FULL + NST, S_FULL = SG_EMPTY + NST, S_READ, DP_FULL, DS_READY,
+       DQ_DONE, DQ_FREE, DRAIN, DRAIN_G, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
-// TMEM: Q hi | dO hi | 2 x (S, dP / dS hi, dS lo) | dQ_blk | Q lo | dO lo
-constexpr uint32_t C_QHI = 0, C_DOHI = 64, C_DQB = 320, C_QLO = 384, C_DOLO = 448, TCOLS = 512;
-__device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 96; }
-__device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 160 + b * 96; }
-__device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 192 + b * 96; }
-static_assert(2 * RES_BYTES <= 2 * SSTAGE, "Q / dO hi are staged in S stages 0-1");
+// TMEM: Q hi | Q lo | dO hi | dO lo | S | dP / dS hi | dS lo | dQ_blk
+constexpr uint32_t C_QHI = 0, C_QLO = 64, C_DOHI = 128, C_DOLO = 192, C_S = 256, C_DP = 320, C_DSLO = 384,
+                   C_DQB = 448, TCOLS = 512;
+static_assert(2 * RES_BYTES <= NST * STAGE, "Q / dO tiles are staged in the K and V rings");
 static_assert(SMEM <= 232448, "smem");
 }  // namespace qq
 
 // tm_q / tm_do: (64, L, H, S2*B), box 128 rows; tm_kk / tm_kmn / tm_vk: (64, S, Hkv, S2*B),
-// box 32 rows.
+// box 64 rows.
+//
+// One MMA warp issues S_0, dP_0, then per block j: S_{j+1} (once the softmax warps have read
+// S_j) and dP_{j+1} (once dQ_j has read dS_j); a second issues dQ_j once dS_j is in TMEM. The
+// tensor core thus runs ... dQ_j, dP_{j+1}, S_{j+2}, dQ_{j+1} ... while the softmax warps
+// compute dS_{j+1} under S_{j+2} and P_{j+2} under dQ_{j+1}.
 template <bool SPLIT, bool MASKED>
 __global__ void __maxnreg__(168)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -646,7 +668,7 @@ __global__ void __maxnreg__(168)
     const int lo_b = (int)(p.B + b);
     const int64_t q0 = qt * TILE;
     const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
-    const int nblk = (int)((kv_end + BLK - 1) / BLK);
+    const int nblk = (int)((kv_end + NB - 1) / NB);
     auto bar = [&](int i) { return sb + OFF_BAR + 8u * (uint32_t)i; };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + OFF_MISC);
     volatile int *abort = reinterpret_cast<volatile int *>(sg + OFF_MISC + 4);
@@ -655,21 +677,20 @@ __global__ void __maxnreg__(168)
     if (threadIdx.x == 0) {
         mbar_init(bar(QD_FULL), 1);
         mbar_init(bar(QD_READY), 256);
-        for (int s = 0; s < NSS; s++) {
-            mbar_init(bar(SS_FULL + s), 1);
-            mbar_init(bar(SS_EMPTY + s), 1);
-        }
-        for (int s = 0; s < NSG; s++) {
+        for (int s = 0; s < NST; s++) {
+            mbar_init(bar(KK_FULL + s), 1);
+            mbar_init(bar(KK_EMPTY + s), 1);
+            mbar_init(bar(VK_FULL + s), 1);
+            mbar_init(bar(VK_EMPTY + s), 1);
             mbar_init(bar(SG_FULL + s), 1);
             mbar_init(bar(SG_EMPTY + s), 1);
         }
-        for (int s = 0; s < 2; s++) {
-            mbar_init(bar(S_FULL + s), 1);
-            mbar_init(bar(DS_FULL + s), 256);
-            mbar_init(bar(G_DONE + s), 1);
-        }
-        mbar_init(bar(CHAIN_DONE), 1);
-        mbar_init(bar(BLK_FREE), 256);
+        mbar_init(bar(S_FULL), 1);
+        mbar_init(bar(S_READ), 256);
+        mbar_init(bar(DP_FULL), 1);
+        mbar_init(bar(DS_READY), 256);
+        mbar_init(bar(DQ_DONE), 1);
+        mbar_init(bar(DQ_FREE), 256);
         mbar_init(bar(DRAIN), 1);
         mbar_init(bar(DRAIN_G), 1);
         *abort = 0;
@@ -690,35 +711,41 @@ __global__ void __maxnreg__(168)
             int issued = -1;
             mbar_expect_tx(bar(QD_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
             for (int c = 0; c < CHUNKS; c++) {
-                tma_load_4d(&tm_q, sb + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
-                tma_load_4d(&tm_do, sb + RES_BYTES + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                tma_load_4d(&tm_q, sb + OFF_QHI + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                tma_load_4d(&tm_do, sb + OFF_DOHI + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 if (SPLIT) {
                     tma_load_4d(&tm_q, sb + OFF_QLO + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
                     tma_load_4d(&tm_do, sb + OFF_DOLO + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
                 }
             }
             bool ok = mbar_wait(bar(QD_READY), 0, abort, err);
+            int k_issued = -1, v_issued = -1;
             for (int j = 0; ok && j < nblk; j++) {
-                const int ss = j % NSS;
-                if (j >= NSS && !mbar_wait(bar(SS_EMPTY + ss), ((j / NSS) - 1) & 1, abort, err)) break;
-                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE, fs = bar(SS_FULL + ss);
-                mbar_expect_tx(fs, (SPLIT ? 4 : 2) * BLK_BYTES);
+                const int st = j % NST;
+                if (j >= NST && !mbar_wait(bar(KK_EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(KK_FULL + st), (SPLIT ? 2 : 1) * NB_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = c * BLK_CHUNK;
-                    tma_load_4d(&tm_kk, sst + SS_KK + o, fs, 32 * c, j * BLK, (int)hk, (int)b);
-                    tma_load_4d(&tm_vk, sst + SS_VK + o, fs, 32 * c, j * BLK, (int)hk, (int)b);
-                    if (SPLIT) {
-                        tma_load_4d(&tm_kk, sst + SS_KK + BLK_BYTES + o, fs, 32 * c, j * BLK, (int)hk, lo_b);
-                        tma_load_4d(&tm_vk, sst + SS_VK + BLK_BYTES + o, fs, 32 * c, j * BLK, (int)hk, lo_b);
-                    }
+                    const uint32_t o = OFF_KK + st * STAGE + c * NB_CHUNK;
+                    tma_load_4d(&tm_kk, sb + o, bar(KK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_kk, sb + o + NB_BYTES, bar(KK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
                 }
-                issued = j;
+                k_issued = j;
+                if (j >= NST && !mbar_wait(bar(VK_EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(VK_FULL + st), (SPLIT ? 2 : 1) * NB_BYTES);
+                for (int c = 0; c < CHUNKS; c++) {
+                    const uint32_t o = OFF_VK + st * STAGE + c * NB_CHUNK;
+                    tma_load_4d(&tm_vk, sb + o, bar(VK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_vk, sb + o + NB_BYTES, bar(VK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
+                }
+                v_issued = j;
             }
             if (*abort) {
                 volatile int never = 0;
                 mbar_wait(bar(QD_FULL), 0, &never, nullptr);
-                for (int j = max(0, issued - NSS + 1); j <= issued; j++)
-                    mbar_wait(bar(SS_FULL + j % NSS), (j / NSS) & 1, &never, nullptr);
+                for (int j = max(0, k_issued - NST + 1); j <= k_issued; j++)
+                    mbar_wait(bar(KK_FULL + j % NST), (j / NST) & 1, &never, nullptr);
+                for (int j = max(0, v_issued - NST + 1); j <= v_issued; j++)
+                    mbar_wait(bar(VK_FULL + j % NST), (j / NST) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_PROD2) {
@@ -726,60 +753,82 @@ __global__ void __maxnreg__(168)
         if (lane == 0) {
             int issued = -1;
             for (int j = 0; j < nblk; j++) {
-                const int sgi = j % NSG;
-                if (j >= NSG && !mbar_wait(bar(SG_EMPTY + sgi), ((j / NSG) - 1) & 1, abort, err)) break;
-                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE, fg = bar(SG_FULL + sgi);
-                mbar_expect_tx(fg, (SPLIT ? 2 : 1) * BLK_BYTES);
+                const int st = j % NST;
+                if (j >= NST && !mbar_wait(bar(SG_EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(SG_FULL + st), (SPLIT ? 2 : 1) * NB_BYTES);
                 for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = c * BLK_CHUNK;
-                    tma_load_4d(&tm_kmn, gst + SG_KMN + o, fg, 32 * c, j * BLK, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_kmn, gst + SG_KMN + BLK_BYTES + o, fg, 32 * c, j * BLK, (int)hk, lo_b);
+                    const uint32_t o = OFF_KMN + st * STAGE + c * NB_CHUNK;
+                    tma_load_4d(&tm_kmn, sb + o, bar(SG_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_kmn, sb + o + NB_BYTES, bar(SG_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
                 }
                 issued = j;
                 if (*abort) break;
             }
             if (*abort) {
                 volatile int never = 0;
-                for (int j = max(0, issued - NSG + 1); j <= issued; j++)
-                    mbar_wait(bar(SG_FULL + j % NSG), (j / NSG) & 1, &never, nullptr);
+                for (int j = max(0, issued - NST + 1); j <= issued; j++)
+                    mbar_wait(bar(SG_FULL + j % NST), (j / NST) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
-        // ------------------------------------------------------------ MMA: S and dP ------
-        {  // the whole warp, converged; one elected lane issues
+        // ------------------------------------------------------ MMA: S and dP, one warp ----
+        // A tensor-core MMA issue blocks once a few hundred cycles of work are queued, so any
+        // wait of the issuing warp idles the tensor core: S / dP and dQ have a warp each, and
+        // one warp's waits overlap the other's MMAs.
+        {
+            auto s_mma = [&](int j) {
+                const uint32_t st = OFF_KK + (j % NST) * STAGE;
+                mma_s_t<SPLIT, NB>(tmem + C_S, tmem + C_QHI, tmem + C_QLO, sdesc_sw128(sb + st, 16, 1024));
+                tc_commit_w(bar(S_FULL));
+                tc_commit_w(bar(KK_EMPTY + j % NST));
+            };
+            auto dp_mma = [&](int j) {
+                const uint32_t st = OFF_VK + (j % NST) * STAGE;
+                mma_s_t<SPLIT, NB>(tmem + C_DP, tmem + C_DOHI, tmem + C_DOLO, sdesc_sw128(sb + st, 16, 1024));
+                tc_commit_w(bar(DP_FULL));
+                tc_commit_w(bar(VK_EMPTY + j % NST));
+            };
             bool ok = warp_wait(bar(QD_READY), 0, abort, err);
             tc_fence_after();
-            for (int j = 0; ok && j < nblk; j++) {
-                const int ss = j % NSS, bb = j & 1;
-                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
-                // Buffer bb holds dS of block j-2 until its gradient MMAs finish.
-                if (j >= 2 && !warp_wait(bar(G_DONE + bb), ((j - 2) >> 1) & 1, abort, err)) break;
-                if (!warp_wait(bar(SS_FULL + ss), (j / NSS) & 1, abort, err)) break;
+            if (ok && nblk > 0) {
+                ok = warp_wait(bar(KK_FULL), 0, abort, err) && warp_wait(bar(VK_FULL), 0, abort, err);
                 tc_fence_after();
-                mma_s_t<SPLIT>(tmem + c_s(bb), tmem + C_QHI, tmem + C_QLO, sdesc_sw128(sst + SS_KK, 16, 1024));
-                mma_s_t<SPLIT>(tmem + c_dp(bb), tmem + C_DOHI, tmem + C_DOLO, sdesc_sw128(sst + SS_VK, 16, 1024));
-                tc_commit_w(bar(S_FULL + bb));
-                tc_commit_w(bar(SS_EMPTY + ss));
+                if (ok) {
+                    s_mma(0);
+                    dp_mma(0);
+                }
             }
+            for (int j = 0; ok && j + 1 < nblk; j++) {
+                const int nx = j + 1;
+                // S of block j+1 overwrites S_j once the softmax warps hold it in registers.
+                if (!warp_wait(bar(S_READ), j & 1, abort, err)) break;
+                if (!warp_wait(bar(KK_FULL + nx % NST), (nx / NST) & 1, abort, err)) break;
+                tc_fence_after();
+                s_mma(nx);
+                // dP of block j+1 overwrites dS_j once dQ_j has read it.
+                if (!warp_wait(bar(DQ_DONE), j & 1, abort, err)) break;
+                if (!warp_wait(bar(VK_FULL + nx % NST), (nx / NST) & 1, abort, err)) break;
+                tc_fence_after();
+                dp_mma(nx);
+            }
+            // Every MMA this warp issued completes before TMEM is released.
             tc_commit_w(bar(DRAIN));
             volatile int never = 0;
             warp_wait(bar(DRAIN), 0, &never, nullptr);
         }
     } else if (warp == W_GMMA) {
-        // ---------------------------------------------------------------- MMA: dQ_blk ----
-        {  // the whole warp, converged; one elected lane issues
-            for (int j = 0; j < nblk; j++) {
-                const int sgi = j % NSG, bb = j & 1;
-                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
-                if (!warp_wait(bar(DS_FULL + bb), (j >> 1) & 1, abort, err)) break;
-                const bool first = (j % FOLD) == 0;
-                if (first && j >= FOLD && !warp_wait(bar(BLK_FREE), ((j / FOLD) - 1) & 1, abort, err)) break;
-                if (!warp_wait(bar(SG_FULL + sgi), (j / NSG) & 1, abort, err)) break;
+        // ------------------------------------------------------------- MMA: dQ_blk = dS K ----
+        {
+            bool ok = true;
+            for (int j = 0; ok && j < nblk; j++) {
+                const int sgi = j % NST;
+                if (!warp_wait(bar(DS_READY), j & 1, abort, err)) break;
+                if (!warp_wait(bar(SG_FULL + sgi), (j / NST) & 1, abort, err)) break;
+                if (j >= 1 && !warp_wait(bar(DQ_FREE), (j - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_g<SPLIT>(tmem + C_DQB, tmem + c_dp(bb), tmem + c_dslo(bb),
-                             sdesc_mn_sw128_32b(gst + SG_KMN, BLK_CHUNK, 512), !first);
-                tc_commit_w(bar(G_DONE + bb));
-                if ((j % FOLD) == FOLD - 1 || j == nblk - 1) tc_commit_w(bar(CHAIN_DONE));
+                mma_g<SPLIT, NB>(tmem + C_DQB, tmem + C_DP, tmem + C_DSLO,
+                                 sdesc_mn_sw128_32b(sb + OFF_KMN + sgi * STAGE, NB_CHUNK, 512), false);
+                tc_commit_w(bar(DQ_DONE));
                 tc_commit_w(bar(SG_EMPTY + sgi));
             }
             tc_commit_w(bar(DRAIN_G));
@@ -793,13 +842,13 @@ __global__ void __maxnreg__(168)
         const int64_t q = q0 + row;
         const bool row_ok = q < p.L;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        const int cb = half * 16;  // this thread's key columns of a block
+        const int cb = half * 32;  // this thread's key columns of a block
         float acc[D / 2];          // dQ columns [32 half, 32 half + 32)
 #pragma unroll
         for (int x = 0; x < D / 2; x++) acc[x] = 0.0f;
         bool ok = warp_wait(bar(QD_FULL), 0, abort, err);
-        if (ok) {  // Q (half 0) or dO (half 1) hi and lo rows into TMEM
-            row_to_tmem(sg + half * RES_BYTES, row, tl, half ? C_DOHI : C_QHI);
+        if (ok) {  // Q (half 0) or dO (half 1), hi and lo rows, into TMEM
+            row_to_tmem(sg + (half ? OFF_DOHI : OFF_QHI), row, tl, half ? C_DOHI : C_QHI);
             if (SPLIT) row_to_tmem(sg + (half ? OFF_DOLO : OFF_QLO), row, tl, half ? C_DOLO : C_QLO);
             tmem_wait_st();
             fence_proxy_async_smem();
@@ -809,60 +858,71 @@ __global__ void __maxnreg__(168)
         const int64_t ridx = (b * p.H + h) * p.L + q;
         const float lse2 = row_ok ? a.lse2[ridx] : 0.0f;
         const float del = row_ok ? a.g.delta[ridx] : 0.0f;
-        const int nchain = (nblk + FOLD - 1) / FOLD;
-        int folded = 0;
-        auto fold = [&]() -> bool {
-            if (!warp_wait(bar(CHAIN_DONE), folded & 1, abort, err)) return false;
+        float pv[32];  // P of the block in flight, this thread's 32 columns
+        // Reads S_j, releases its columns, and leaves P_j in pv.
+        auto load_p = [&](int j) -> bool {
+            const int64_t base = (int64_t)j * NB + cb;
+            // Column c is key base + c: valid below S and, under causal masking, up to q.
+            const bool edge = MASKED || !row_ok || (int64_t)(j + 1) * NB > p.S || (p.causal && (int64_t)(j + 1) * NB - 1 > q0);
+            uint32_t vbits = 0xFFFFFFFFu;
+            if (edge) vbits = row_ok ? col_bits32(0, (p.causal ? min(p.S, q + 1) : p.S) - base) : 0u;
+            // The user mask along this query's row, loaded before the wait for S.
+            float mk[MASKED ? 32 : 1];
+            if constexpr (MASKED) mask_run<32>(p, b, h, q, base, p.ms[3], vbits, mk);
+            if (!warp_wait(bar(S_FULL), j & 1, abort, err)) return false;
             tc_fence_after();
-            fold16(tl + C_DQB + 32 * half, acc);
-            fold16(tl + C_DQB + 32 * half + 16, acc + 16);
+            uint32_t sr[32];
+            tmem_ld32(tl + C_S + cb, sr);
+            tmem_wait_ld();
             tc_fence_before();
-            mbar_arrive(bar(BLK_FREE));
-            folded++;
+            mbar_arrive(bar(S_READ));
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                float x = __uint_as_float(sr[c]) * a.scale_log2;
+                if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                pv[c] = ((vbits >> c) & 1u) ? ex2_approx(x - lse2) : 0.0f;
+            }
             return true;
         };
+        if (ok && nblk > 0) ok = load_p(0);
         for (int j = 0; ok && j < nblk; j++) {
-            const int bb = j & 1;
-            const int64_t kb0 = (int64_t)j * BLK;
-            // Column c is key base + c: valid below S and, under causal masking, up to q.
-            const int64_t base = kb0 + cb;
-            const bool edge = MASKED || !row_ok || kb0 + BLK > p.S || (p.causal && kb0 + BLK - 1 > q0);
-            uint32_t vbits = 0xFFFFu;
-            if (edge) vbits = row_ok ? col_bits(0, (p.causal ? min(p.S, q + 1) : p.S) - base) : 0u;
-            // The user mask along this query's row, loaded before the wait for S.
-            float mk[MASKED ? 16 : 1];
-            if constexpr (MASKED) mask_run<16>(p, b, h, q, base, p.ms[3], vbits, mk);
-            if (!warp_wait(bar(S_FULL + bb), (j >> 1) & 1, abort, err)) {
+            if (!warp_wait(bar(DP_FULL), j & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t sr[16], dr[16];
-            tmem_ld16(tl + c_s(bb) + cb, sr);
-            tmem_ld16(tl + c_dp(bb) + cb, dr);
-            tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                float x = __uint_as_float(sr[c]) * a.scale_log2;
-                if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
-                sr[c] = __float_as_uint(x);
-            }
+            for (int r0 = 0; r0 < 32; r0 += 16) {  // dS in 16-column pieces
+                uint32_t dr[16], xh[16], xl[16];
+                tmem_ld16(tl + C_DP + cb + r0, dr);
+                tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                const float pc = ((vbits >> c) & 1u) ? ex2_approx(__uint_as_float(sr[c]) - lse2) : 0.0f;
-                const float ds = pc * (__uint_as_float(dr[c]) - del);
-                sr[c] = tf32_rna(ds);
-                if (SPLIT) dr[c] = tf32_lo(ds, sr[c]);
+                for (int c = 0; c < 16; c++) {
+                    const float ds = pv[r0 + c] * (__uint_as_float(dr[c]) - del);
+                    xh[c] = tf32_rna(ds);
+                    if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
+                }
+                tmem_st16(tl + C_DP + cb + r0, xh);
+                if (SPLIT) tmem_st16(tl + C_DSLO + cb + r0, xl);
             }
-            tmem_st16(tl + c_dp(bb) + cb, sr);
-            if (SPLIT) tmem_st16(tl + c_dslo(bb) + cb, dr);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(DS_FULL + bb));
-            if (j >= 1 && ((j - 1) % FOLD) == FOLD - 1 && !fold()) ok = false;
+            mbar_arrive(bar(DS_READY));
+            // P of the next block while the tensor core runs dQ_j.
+            if (j + 1 < nblk && !load_p(j + 1)) {
+                ok = false;
+                break;
+            }
+            if (!warp_wait(bar(DQ_DONE), j & 1, abort, err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            fold16(tl + C_DQB + 32 * half, acc);
+            fold16(tl + C_DQB + 32 * half + 16, acc + 16);
+            tc_fence_before();
+            mbar_arrive(bar(DQ_FREE));
         }
-        while (ok && folded < nchain)
-            if (!fold()) ok = false;
         const bool aborted = __any_sync(FULL, *abort != 0);
         if (ok && !aborted && row_ok) {
             float *dqr = a.g.dq + b * a.g.dqs[0] + h * a.g.dqs[1] + q * a.g.dqs[2] + (int64_t)(32 * half) * a.g.dqs[3];
@@ -959,9 +1019,9 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         CUtensorMap tq, tdo, tkk, tkmn, tvk;
         st = make_tmap(&tq, pa.qhl, D, p.L, p.H, nb, qst, TILE);
         if (!st) st = make_tmap(&tdo, pa.dohl, D, p.L, p.H, nb, qst, TILE);
-        if (!st) st = make_tmap(&tkk, pa.khl, D, p.S, p.Hkv, nb, kst, BLK);
-        if (!st) st = make_tmap(&tkmn, pa.khl, D, p.S, p.Hkv, nb, kst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-        if (!st) st = make_tmap(&tvk, pa.vhl, D, p.S, p.Hkv, nb, kst, BLK);
+        if (!st) st = make_tmap(&tkk, pa.khl, D, p.S, p.Hkv, nb, kst, qq::NB);
+        if (!st) st = make_tmap(&tkmn, pa.khl, D, p.S, p.Hkv, nb, kst, qq::NB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        if (!st) st = make_tmap(&tvk, pa.vhl, D, p.S, p.Hkv, nb, kst, qq::NB);
         if (st) return st;
         auto kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true> : attn_bwd_dq_tc_kernel<true, false>)
                             : (masked ? attn_bwd_dq_tc_kernel<false, true> : attn_bwd_dq_tc_kernel<false, false>);
