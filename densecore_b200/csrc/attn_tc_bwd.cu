@@ -44,6 +44,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -949,6 +951,42 @@ struct PoolScratch {
     ~PoolScratch() { pool_free(ptr, stream); }
 };
 
+// The dQ kernel does not depend on the dK / dV kernel: it runs on a second stream of the
+// library's (one per device, created on first use), forked from the caller's stream after the
+// pre-pass and joined back before the call returns, so that the two kernels share the GPU (the
+// CTAs of one fill the SMs that the other's last, shorter tiles leave idle). Both events are
+// created per call, so concurrent calls from several host threads do not share them.
+constexpr int kSideDevices = 64;
+std::mutex g_side_mu;
+cudaStream_t g_side[kSideDevices];
+
+int side_stream(cudaStream_t *out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "backward: current device");
+    if (dev < 0 || dev >= kSideDevices) return fail(DC_ERR_UNSUPPORTED, "backward: device ordinal above 63");
+    std::lock_guard<std::mutex> lock(g_side_mu);
+    if (!g_side[dev]) {
+        e = cudaStreamCreateWithFlags(&g_side[dev], cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            g_side[dev] = nullptr;
+            return cuda_fail(e, "backward: create the dQ stream");
+        }
+    }
+    *out = g_side[dev];
+    return DC_OK;
+}
+
+// Records an event on `from` and makes `to` wait for it.
+int stream_edge(cudaStream_t from, cudaStream_t to) {
+    cudaEvent_t ev = nullptr;
+    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ev, from);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(to, ev, 0);
+    if (ev) cudaEventDestroy(ev);  // released once the recorded work completes
+    return e == cudaSuccess ? DC_OK : cuda_fail(e, "backward: stream fork / join");
+}
+
 }  // namespace
 
 bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g) {
@@ -997,6 +1035,15 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     const int64_t qst[3] = {p.H * p.L * D, p.L * D, D}, kst[3] = {p.Hkv * p.S * D, p.S * D, D};
     const int64_t nb = S2 * p.B;
     const bool masked = p.mask_kind != MASK_NONE;
+    // The two tensor-core kernels run concurrently; with tracing on, this record spans both
+    // (from before the fork to after the join, on the caller's stream).
+    KernelTrace pair("bwd_tc", stream);
+    // Fork the dQ stream here, after the pre-pass and before the dK / dV launch.
+    cudaStream_t side = nullptr;
+    if (p.L > 0) {
+        if ((st = side_stream(&side))) return st;
+        if ((st = stream_edge(stream, side))) return st;
+    }
     if (p.S > 0) {
         CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
         st = make_tmap(&tk, pa.khl, D, p.S, p.Hkv, nb, kst, TILE);
@@ -1028,9 +1075,13 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
         const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B);
-        KernelTrace tr("bwd_dq_tc", stream);
-        kernel<<<grid, THREADS, qq::SMEM, stream>>>(tq, tdo, tkk, tkmn, tvk, a);
-        if ((st = check_launch("attn_bwd_dq_tc"))) return st;
+        {
+            KernelTrace tr("bwd_dq_tc", side);
+            kernel<<<grid, THREADS, qq::SMEM, side>>>(tq, tdo, tkk, tkmn, tvk, a);
+        }
+        const int launched = check_launch("attn_bwd_dq_tc");
+        if ((st = stream_edge(side, stream))) return st;
+        if (launched) return launched;
     }
     return DC_OK;
 }
