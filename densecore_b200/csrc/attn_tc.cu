@@ -179,7 +179,7 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_b
     }
 }
 
-template <class C, bool SPLIT, bool MASKED>
+template <class C, bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(128)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                        const __grid_constant__ CUtensorMap tmv, const TcFwdArgs a) {
@@ -399,6 +399,10 @@ __global__ void __maxnreg__(128)
             // the wait hides their latency.
             float mk[MASKED ? C::HB : 1];
             if constexpr (MASKED) mask_run<C::HB>(p, b, h, qrow, k0, p.ms[3], vbits, mk);
+            // Dropout: this row's keep bits for these columns (the weights that meet V are
+            // P * keep_scale where kept, 0 where dropped; the row sum and lse stay undropped).
+            uint32_t kbits = 0;
+            if constexpr (DROP) kbits = row_ok ? keep_run32(p, b, h, qrow, k0) : 0u;
             if (!mbar_wait(bar(C::S_FULL + bb), (j >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
@@ -449,8 +453,10 @@ __global__ void __maxnreg__(128)
                 for (int c = 0; c < 16; c++) {
                     const float pc = dead ? 0.0f : ex2_approx(s[r0 + c] - m);
                     part[c & 3] += pc;
-                    phi[c] = tf32_rna(pc);
-                    if (SPLIT) plo[c] = tf32_lo(pc, phi[c]);
+                    float pw = pc;
+                    if constexpr (DROP) pw = ((kbits >> (r0 + c)) & 1u) ? pc * p.keep_scale : 0.0f;
+                    phi[c] = tf32_rna(pw);
+                    if (SPLIT) plo[c] = tf32_lo(pw, phi[c]);
                 }
                 tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
                 if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);
@@ -550,8 +556,14 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     a.err = device_error_word();
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
     const bool masked = p.mask_kind != MASK_NONE;
-    auto kernel = split ? (masked ? attn_fwd_tc_kernel<C, true, true> : attn_fwd_tc_kernel<C, true, false>)
-                        : (masked ? attn_fwd_tc_kernel<C, false, true> : attn_fwd_tc_kernel<C, false, false>);
+    const bool drop = p.keep != nullptr;
+    decltype(&attn_fwd_tc_kernel<C, true, true, true>) kernel;
+    if (drop)
+        kernel = split ? (masked ? attn_fwd_tc_kernel<C, true, true, true> : attn_fwd_tc_kernel<C, true, false, true>)
+                       : (masked ? attn_fwd_tc_kernel<C, false, true, true> : attn_fwd_tc_kernel<C, false, false, true>);
+    else
+        kernel = split ? (masked ? attn_fwd_tc_kernel<C, true, true, false> : attn_fwd_tc_kernel<C, true, false, false>)
+                       : (masked ? attn_fwd_tc_kernel<C, false, true, false> : attn_fwd_tc_kernel<C, false, false, false>);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
     dim3 grid((unsigned)a.num_q_tiles, (unsigned)p.H, (unsigned)p.B);

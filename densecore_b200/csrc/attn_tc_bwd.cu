@@ -316,7 +316,7 @@ static_assert(SMEM <= 232448, "smem");
 // tm_k / tm_v: (64, S, Hkv, S2*B) over the hi / lo copies (lo at batch B + b), box 128 rows;
 // tm_q* / tm_do*: (64, L, H, S2*B), box 32 rows, K-major (128-byte swizzle) or MN-major
 // (32-byte-atom swizzle).
-template <bool SPLIT, bool MASKED>
+template <bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(168)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_qmn,
@@ -549,6 +549,10 @@ __global__ void __maxnreg__(168)
             // The user mask down this key's column, loaded before the wait for S.
             float mk[MASKED ? 16 : 1];
             if constexpr (MASKED) mask_run<16>(p, b, h, base, key, p.ms[2], vbits, mk);
+            // Dropout: the keep bits of (query base + c, this key). The weights that meet dO are
+            // P * Z; dS = P (Z dP - delta), Z = keep_scale where kept, 0 where dropped.
+            uint32_t zb = 0;
+            if constexpr (DROP) zb = key_ok ? keep_col16(p, b, h, base, key) : 0u;
             if (!warp_wait(bar(S_FULL + bb), (i >> 1) & 1, abort, err)) {
                 ok = false;
                 break;
@@ -568,11 +572,17 @@ __global__ void __maxnreg__(168)
             for (int c = 0; c < 16; c++) {
                 const float lse2 = __shfl_sync(FULL, cur, c), del = __shfl_sync(FULL, cur, 16 + c);
                 const float pc = ((vbits >> c) & 1u) ? ex2_approx(__uint_as_float(sr[c]) - lse2) : 0.0f;
-                const float ds = pc * (__uint_as_float(dr[c]) - del);
-                phi[c] = tf32_rna(pc);
+                float pw = pc, dpv = __uint_as_float(dr[c]);
+                if constexpr (DROP) {
+                    const bool kept = (zb >> c) & 1u;
+                    pw = kept ? pc * p.keep_scale : 0.0f;
+                    dpv = kept ? dpv * p.keep_scale : 0.0f;
+                }
+                const float ds = pc * (dpv - del);
+                phi[c] = tf32_rna(pw);
                 sr[c] = tf32_rna(ds);
                 if (SPLIT) {
-                    plo[c] = tf32_lo(pc, phi[c]);
+                    plo[c] = tf32_lo(pw, phi[c]);
                     dr[c] = tf32_lo(ds, sr[c]);
                 }
             }
@@ -649,7 +659,7 @@ static_assert(SMEM <= 232448, "smem");
 // S_j) and dP_{j+1} (once dQ_j has read dS_j); a second issues dQ_j once dS_j is in TMEM. The
 // tensor core thus runs ... dQ_j, dP_{j+1}, S_{j+2}, dQ_{j+1} ... while the softmax warps
 // compute dS_{j+1} under S_{j+2} and P_{j+2} under dQ_{j+1}.
-template <bool SPLIT, bool MASKED>
+template <bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(168)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_kk, const __grid_constant__ CUtensorMap tm_kmn,
@@ -860,7 +870,8 @@ __global__ void __maxnreg__(168)
         const int64_t ridx = (b * p.H + h) * p.L + q;
         const float lse2 = row_ok ? a.lse2[ridx] : 0.0f;
         const float del = row_ok ? a.g.delta[ridx] : 0.0f;
-        float pv[32];  // P of the block in flight, this thread's 32 columns
+        float pv[32];      // P of the block in flight, this thread's 32 columns
+        uint32_t zcur = 0;  // its dropout keep bits
         // Reads S_j, releases its columns, and leaves P_j in pv.
         auto load_p = [&](int j) -> bool {
             const int64_t base = (int64_t)j * NB + cb;
@@ -871,6 +882,7 @@ __global__ void __maxnreg__(168)
             // The user mask along this query's row, loaded before the wait for S.
             float mk[MASKED ? 32 : 1];
             if constexpr (MASKED) mask_run<32>(p, b, h, q, base, p.ms[3], vbits, mk);
+            if constexpr (DROP) zcur = row_ok ? keep_run32(p, b, h, q, base) : 0u;
             if (!warp_wait(bar(S_FULL), j & 1, abort, err)) return false;
             tc_fence_after();
             uint32_t sr[32];
@@ -900,7 +912,10 @@ __global__ void __maxnreg__(168)
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
-                    const float ds = pv[r0 + c] * (__uint_as_float(dr[c]) - del);
+                    // dS = P (Z dP - delta), Z = keep_scale where kept, 0 where dropped.
+                    float dpv = __uint_as_float(dr[c]);
+                    if constexpr (DROP) dpv = ((zcur >> (r0 + c)) & 1u) ? dpv * p.keep_scale : 0.0f;
+                    const float ds = pv[r0 + c] * (dpv - del);
                     xh[c] = tf32_rna(ds);
                     if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
                 }
@@ -1035,6 +1050,7 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     const int64_t qst[3] = {p.H * p.L * D, p.L * D, D}, kst[3] = {p.Hkv * p.S * D, p.S * D, D};
     const int64_t nb = S2 * p.B;
     const bool masked = p.mask_kind != MASK_NONE;
+    const bool drop = p.keep != nullptr;
     // The two tensor-core kernels run concurrently; with tracing on, this record spans both
     // (from before the fork to after the join, on the caller's stream).
     KernelTrace pair("bwd_tc", stream);
@@ -1053,8 +1069,13 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         if (!st) st = make_tmap(&tdok, pa.dohl, D, p.L, p.H, nb, qst, BLK);
         if (!st) st = make_tmap(&tdomn, pa.dohl, D, p.L, p.H, nb, qst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (st) return st;
-        auto kernel = split ? (masked ? attn_bwd_dkdv_tc_kernel<true, true> : attn_bwd_dkdv_tc_kernel<true, false>)
-                            : (masked ? attn_bwd_dkdv_tc_kernel<false, true> : attn_bwd_dkdv_tc_kernel<false, false>);
+        decltype(&attn_bwd_dkdv_tc_kernel<true, true, true>) kernel;
+        if (drop)
+            kernel = split ? (masked ? attn_bwd_dkdv_tc_kernel<true, true, true> : attn_bwd_dkdv_tc_kernel<true, false, true>)
+                           : (masked ? attn_bwd_dkdv_tc_kernel<false, true, true> : attn_bwd_dkdv_tc_kernel<false, false, true>);
+        else
+            kernel = split ? (masked ? attn_bwd_dkdv_tc_kernel<true, true, false> : attn_bwd_dkdv_tc_kernel<true, false, false>)
+                           : (masked ? attn_bwd_dkdv_tc_kernel<false, true, false> : attn_bwd_dkdv_tc_kernel<false, false, false>);
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
         const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B);
@@ -1070,8 +1091,13 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         if (!st) st = make_tmap(&tkmn, pa.khl, D, p.S, p.Hkv, nb, kst, qq::NB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (!st) st = make_tmap(&tvk, pa.vhl, D, p.S, p.Hkv, nb, kst, qq::NB);
         if (st) return st;
-        auto kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true> : attn_bwd_dq_tc_kernel<true, false>)
-                            : (masked ? attn_bwd_dq_tc_kernel<false, true> : attn_bwd_dq_tc_kernel<false, false>);
+        decltype(&attn_bwd_dq_tc_kernel<true, true, true>) kernel;
+        if (drop)
+            kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true, true> : attn_bwd_dq_tc_kernel<true, false, true>)
+                           : (masked ? attn_bwd_dq_tc_kernel<false, true, true> : attn_bwd_dq_tc_kernel<false, false, true>);
+        else
+            kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true, false> : attn_bwd_dq_tc_kernel<true, false, false>)
+                           : (masked ? attn_bwd_dq_tc_kernel<false, true, false> : attn_bwd_dq_tc_kernel<false, false, false>);
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
         const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B);

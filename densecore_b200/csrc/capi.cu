@@ -272,8 +272,11 @@ static int sdpa_fwd_impl(const dc_tensor_t *q, const dc_tensor_t *k, const dc_te
     if (p.B == 0 || p.H == 0 || p.L == 0) return DC_OK;
     if ((st = device_ok())) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dropout) return simt_forward(p, s);
-    switch (pick_forward_path(p, precision)) {
+    const int path = pick_forward_path(p, precision);
+    // With dropout the tensor-core kernels apply the keep bits; the decode and CUDA-core
+    // shapes take the CUDA-core kernel, which applies them too.
+    if (dropout && path != 1) return simt_forward(p, s);
+    switch (path) {
         case 2: {
             const int splits = decode_pick_splits(p);
             ScopedWorkspace ws;
@@ -353,7 +356,7 @@ static int sdpa_bwd_impl(const dc_tensor_t *grad_out, const dc_tensor_t *q, cons
         return st;
     g.delta = static_cast<float *>(ws.ptr);
     // The tensor-core backward computes delta in its own pre-pass.
-    if (!dropout && precision != DC_PREC_FP32 && tc_backward_supported(p, g)) return tc_backward(p, g, precision, s);
+    if (precision != DC_PREC_FP32 && tc_backward_supported(p, g)) return tc_backward(p, g, precision, s);
     if (p.L > 0 && (st = bwd_delta(p, g, s))) return st;
     return simt_backward(p, g, s);
 }

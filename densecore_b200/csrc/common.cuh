@@ -116,6 +116,33 @@ __device__ __forceinline__ float keep_factor(const AttnProblem &p, int64_t b, in
     return (__ldg(p.keep + (e >> 5)) >> (e & 31)) & 1u ? p.keep_scale : 0.0f;
 }
 
+// Dropout keep bits of the weights (b, h, i, j0 + c), c = 0..31, as one word (bit c). Words
+// past the end of the bit array read as 0; the caller's validity bits cover those columns.
+__device__ __forceinline__ uint32_t keep_run32(const AttnProblem &p, int64_t b, int64_t h, int64_t i, int64_t j0) {
+    const int64_t e = ((b * p.H + h) * p.L + i) * p.S + j0;
+    const int64_t nw = (p.B * p.H * p.L * p.S + 31) >> 5;
+    const int64_t w = e >> 5;
+    const uint32_t lo = w < nw ? __ldg(p.keep + w) : 0u;
+    const uint32_t hi = w + 1 < nw ? __ldg(p.keep + w + 1) : 0u;
+    return __funnelshift_r(lo, hi, (uint32_t)(e & 31));
+}
+
+// Dropout keep bits of the weights (b, h, i0 + c, j), c = 0..15 (down one key's column), bit c.
+__device__ __forceinline__ uint32_t keep_col16(const AttnProblem &p, int64_t b, int64_t h, int64_t i0, int64_t j) {
+    const int64_t nw = (p.B * p.H * p.L * p.S + 31) >> 5;
+    const int64_t e0 = ((b * p.H + h) * p.L + i0) * p.S + j;
+    uint32_t words[16];
+#pragma unroll
+    for (int c = 0; c < 16; c++) {
+        const int64_t w = (e0 + c * p.S) >> 5;
+        words[c] = w < nw ? __ldg(p.keep + w) : 0u;
+    }
+    uint32_t bits = 0;
+#pragma unroll
+    for (int c = 0; c < 16; c++) bits |= ((words[c] >> ((e0 + c * p.S) & 31)) & 1u) << c;
+    return bits;
+}
+
 // Whether key j is visible to query row i under top-left causal alignment.
 __device__ __forceinline__ bool causal_visible(int causal, int64_t i, int64_t j) {
     return !causal || j <= i;

@@ -135,7 +135,11 @@ def _oracle_case(q, k, v, mask, causal, scale, p, seed):
 @pytest.mark.parametrize("shape,kind,causal,scale", [
     ((2, 3, 40, 24, 16, 16), "bool", False, None), ((1, 2, 33, 70, 8, 8), "float", False, 0.7),
     ((2, 2, 64, 64, 32, 32), None, True, None), ((1, 4, 19, 27, 12, 20), "bool4", False, -0.4),
-    ((1, 2, 1024, 1024, 64, 64), None, True, None)])
+    ((1, 2, 1024, 1024, 64, 64), None, True, None),
+    # head dims the tensor-core kernels take: keep bits at unaligned offsets (S not a multiple
+    # of 32), masks, and the D = 128 forward
+    ((2, 3, 200, 173, 64, 64), "bool", False, None), ((2, 2, 130, 257, 64, 64), "float", False, 0.2),
+    ((1, 2, 300, 300, 128, 128), None, True, 0.3), ((1, 2, 97, 200, 64, 64), None, True, None)])
 def test_sdpa_dropout_matches_oracle(shape, kind, causal, scale):
     B, H, L, S, E, Ev = shape
     rng = np.random.default_rng(L + S)
@@ -179,6 +183,25 @@ def test_sdpa_dropout_rank3_and_grouped_heads():
     y = dc.functional.scaled_dot_product_attention(*(torch.tensor(a, device="cuda") for a in (q, k, v)),
                                                    dropout_p=0.4, enable_gqa=True)
     assert rel_err(y.cpu().numpy(), ref) <= 1e-5
+
+
+def test_sdpa_dropout_grouped_heads_tensor_cores():
+    # Head dim 64: the tensor-core kernels, with four query heads over two kv heads.
+    rng = np.random.default_rng(8)
+    q, g = (rng.normal(size=(2, 4, 150, 64)).astype(np.float32) for _ in range(2))
+    k, v = (rng.normal(size=(2, 2, 150, 64)).astype(np.float32) for _ in range(2))
+    wide = lambda a: np.repeat(a, 2, axis=1)
+    ref, saved = _oracle_case(q, wide(k), wide(v), None, True, None, 0.2, 9)
+    dq, dk, dv = oracle.sdpa_math_backward(g, wide(v), saved)
+    dk = dk.reshape(2, 2, 2, 150, 64).sum(axis=2)
+    dv = dv.reshape(2, 2, 2, 150, 64).sum(axis=2)
+    dc.manual_seed(9)
+    t = [torch.tensor(a, device="cuda", requires_grad=True) for a in (q, k, v)]
+    y = dc.functional.scaled_dot_product_attention(*t, dropout_p=0.2, is_causal=True, enable_gqa=True)
+    y.backward(torch.tensor(g, device="cuda"))
+    assert rel_err(y.detach().cpu().numpy(), ref) <= 1e-5
+    for tt, r in zip(t, (dq, dk, dv)):
+        assert rel_err(tt.grad.cpu().numpy(), r) <= 1e-5
 
 
 def test_dropout_one_draws_nothing_and_zeroes():
