@@ -87,21 +87,23 @@ __device__ __forceinline__ constexpr uint32_t mnoff(int kk) { return (uint32_t)(
 
 // S-type product over D (3 passes with SPLIT, cross terms first):
 //   d = A_hi B_lo + A_lo B_hi + A_hi B_hi,
-// A_hi in TMEM (columns a_hi + 8 kk), A_lo in shared memory (K-major, descriptor a_lo),
-// B hi / lo K-major in shared memory (descriptor b_hi, lo BLK_BYTES further).
-template <bool SPLIT>
+// A_hi in TMEM (columns a_hi + 8 kk), A_lo in shared memory (K-major, TILE rows, descriptor
+// a_lo), B hi / lo K-major NB-row tiles in shared memory (descriptor b_hi, lo NB * D * 4 bytes
+// further); N = NB.
+template <bool SPLIT, int NB = BLK>
 __device__ __forceinline__ void mma_s(uint32_t d, uint32_t a_hi, uint64_t a_lo, uint64_t b_hi) {
-    constexpr uint32_t BLO = BLK_BYTES >> 4;
+    constexpr uint32_t BLO = (uint32_t)(NB * D * 4) >> 4, CH = NB * 128;
+    constexpr uint32_t ID = idesc_tf32(128, NB, 0, 0);
     if (SPLIT) {
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++) {
-            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<BLK_CHUNK>(kk)), IDESC_S, kk > 0 ? 1u : 0u);
-            mma_tf32_ss_w(d, a_lo + koff<RES_CHUNK>(kk), b_hi + koff<BLK_CHUNK>(kk), IDESC_S, 1u);
+            mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<CH>(kk)), ID, kk > 0 ? 1u : 0u);
+            mma_tf32_ss_w(d, a_lo + koff<RES_CHUNK>(kk), b_hi + koff<CH>(kk), ID, 1u);
         }
     }
 #pragma unroll
     for (int kk = 0; kk < D / 8; kk++)
-        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<BLK_CHUNK>(kk), IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+        mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<CH>(kk), ID, (SPLIT || kk > 0) ? 1u : 0u);
 }
 
 // mma_s with A_lo in TMEM too (columns a_lo + 8 kk) and an NB-row streamed B tile (N = NB):
@@ -286,36 +288,39 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
 
 // ==================================================================== dK / dV ========
 namespace kv {
-// Two rings: the K-major tiles (read by the S / dP MMAs only) free their stage as soon as those
-// MMAs finish, so they get three stages; the MN-major tiles (read by the gradient MMAs) two.
-constexpr int NSS = 3, NSG = 2;
-// S stage: Q_K hi, lo | dO_K hi, lo; G stage: Q_MN hi, lo | dO_MN hi, lo (8 KB tiles)
-constexpr uint32_t SS_QK = 0, SS_DOK = 2 * BLK_BYTES, SG_QMN = 0, SG_DOMN = 2 * BLK_BYTES;
-constexpr uint32_t SSTAGE = 4 * BLK_BYTES, GSTAGE = 4 * BLK_BYTES;  // 32 KB, 1024-byte aligned
-constexpr uint32_t OFF_SRING = 0, OFF_GRING = NSS * SSTAGE;
-constexpr uint32_t OFF_KLO = OFF_GRING + NSG * GSTAGE, OFF_VLO = OFF_KLO + RES_BYTES;
+// 64-query blocks: S^T and dP^T run at N = 64, where an MMA does twice the work of an N = 32
+// one for a little more time. Tensor memory then holds one block's S^T / P^T and dP^T / dS^T
+// (single buffers), and shared memory one stage per streamed tile, each freed by its reader.
+constexpr int QB = 64;
+constexpr uint32_t QB_BYTES = QB * D * 4;  // one streamed fp32 tile (16 KB)
+constexpr uint32_t QB_CHUNK = QB * 128;    // 8 KB per 32-column chunk
+constexpr uint32_t TSTAGE = 2 * QB_BYTES;  // a tile's hi and lo copies (32 KB)
+// Q_K, dO_K (K-major: the S / dP MMAs), dO_MN, Q_MN (MN-major: the dV / dK MMAs), then the
+// resident K lo and V lo. K hi and V hi wait in the Q_K and dO_K stages until they are in TMEM.
+constexpr uint32_t OFF_QK = 0, OFF_DOK = TSTAGE, OFF_DOMN = 2 * TSTAGE, OFF_QMN = 3 * TSTAGE;
+constexpr uint32_t OFF_KLO = 4 * TSTAGE, OFF_VLO = OFF_KLO + RES_BYTES;
 constexpr uint32_t OFF_BAR = OFF_VLO + RES_BYTES;
-// G_DONE[b]: the gradient MMAs that read buffer b finished (guards its reuse); CHAIN_DONE:
-// the last gradient MMAs of an accumulation chain finished (the fold may read); BLK_FREE: the
-// fold has read the block accumulators (the next chain may overwrite them).
-enum { KV_FULL, KV_READY, SS_FULL, SS_EMPTY = SS_FULL + NSS, SG_FULL = SS_EMPTY + NSS, SG_EMPTY = SG_FULL + NSG,
-       S_FULL = SG_EMPTY + NSG, P_FULL = S_FULL + 2, G_DONE = P_FULL + 2, CHAIN_DONE = G_DONE + 2, BLK_FREE,
-       DRAIN, DRAIN_G, NBAR };
+// Per block i: S^T (S_FULL) turned into P^T (P_READY); dP^T (DP_FULL) into dS^T (DS_READY);
+// dV (DV_DONE: P^T read, S^T_{i+1} may overwrite it) and dK (DK_DONE: dS^T read, dP^T_{i+1}
+// may overwrite it); DV_FREE / DK_FREE: the fold has read that accumulator.
+enum { KV_FULL, KV_READY, QK_FULL, QK_EMPTY, DOK_FULL, DOK_EMPTY, DOMN_FULL, DOMN_EMPTY, QMN_FULL, QMN_EMPTY,
+       S_FULL, DP_FULL, P_READY, DS_READY, DV_DONE, DK_DONE, DV_FREE, DK_FREE, DRAIN, DRAIN_G, NBAR };
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
-// TMEM: K hi | V hi | 2 x (S^T / P^T hi, P^T lo, dP^T / dS^T hi, dS^T lo) | dV_blk | dK_blk
-constexpr uint32_t C_KHI = 0, C_VHI = 64, C_DV = 384, C_DK = 448, TCOLS = 512;
-__device__ __forceinline__ constexpr uint32_t c_s(int b) { return 128 + b * 128; }
-__device__ __forceinline__ constexpr uint32_t c_plo(int b) { return 160 + b * 128; }
-__device__ __forceinline__ constexpr uint32_t c_dp(int b) { return 192 + b * 128; }
-__device__ __forceinline__ constexpr uint32_t c_dslo(int b) { return 224 + b * 128; }
-static_assert(2 * RES_BYTES <= 2 * SSTAGE, "K / V hi are staged in S stages 0-1");
+// TMEM: K hi | V hi | S^T / P^T hi | P^T lo | dP^T / dS^T hi | dS^T lo | dV_blk | dK_blk
+constexpr uint32_t C_KHI = 0, C_VHI = 64, C_S = 128, C_PLO = 192, C_DP = 256, C_DSLO = 320, C_DV = 384, C_DK = 448,
+                   TCOLS = 512;
+static_assert(RES_BYTES <= TSTAGE, "K / V hi are staged in the Q_K and dO_K stages");
 static_assert(SMEM <= 232448, "smem");
 }  // namespace kv
 
 // tm_k / tm_v: (64, S, Hkv, S2*B) over the hi / lo copies (lo at batch B + b), box 128 rows;
-// tm_q* / tm_do*: (64, L, H, S2*B), box 32 rows, K-major (128-byte swizzle) or MN-major
+// tm_q* / tm_do*: (64, L, H, S2*B), box 64 rows, K-major (128-byte swizzle) or MN-major
 // (32-byte-atom swizzle).
+//
+// MMA order per block i: S^T_i, dP^T_i (warp 9), dV_i, dK_i (warp 11). S^T_{i+1} waits for dV_i
+// and runs after dK_i; dP^T_{i+1} waits for dK_i. The softmax warps compute P^T_i while dP^T_i
+// runs and dS^T_i while dV_i runs.
 template <bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(168)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -336,8 +341,8 @@ __global__ void __maxnreg__(168)
     const int lo_b = (int)(p.B + b);  // batch coordinate of the lo copies
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
     const int64_t r_begin = p.causal ? min(k0, p.L) : 0;
-    const int qb_first = (int)(r_begin / BLK);
-    const int qb_per_head = (int)((p.L + BLK - 1) / BLK) - qb_first;
+    const int qb_first = (int)(r_begin / QB);
+    const int qb_per_head = (int)((p.L + QB - 1) / QB) - qb_first;
     const int nblk = qb_per_head * p.group;
     auto bar = [&](int i) { return sb + OFF_BAR + 8u * (uint32_t)i; };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + OFF_MISC);
@@ -345,27 +350,21 @@ __global__ void __maxnreg__(168)
     int *err = a.err;
     auto blk_coords = [&](int i, int64_t &h, int64_t &q0) {
         h = hk * p.group + i / qb_per_head;
-        q0 = (int64_t)(qb_first + i % qb_per_head) * BLK;
+        q0 = (int64_t)(qb_first + i % qb_per_head) * QB;
     };
 
     if (threadIdx.x == 0) {
         mbar_init(bar(KV_FULL), 1);
         mbar_init(bar(KV_READY), 256);
-        for (int s = 0; s < NSS; s++) {
-            mbar_init(bar(SS_FULL + s), 1);
-            mbar_init(bar(SS_EMPTY + s), 1);
-        }
-        for (int s = 0; s < NSG; s++) {
-            mbar_init(bar(SG_FULL + s), 1);
-            mbar_init(bar(SG_EMPTY + s), 1);
-        }
-        for (int s = 0; s < 2; s++) {
-            mbar_init(bar(S_FULL + s), 1);
-            mbar_init(bar(P_FULL + s), 256);
-            mbar_init(bar(G_DONE + s), 1);
-        }
-        mbar_init(bar(CHAIN_DONE), 1);
-        mbar_init(bar(BLK_FREE), 256);
+        for (int i = QK_FULL; i <= QMN_EMPTY; i++) mbar_init(bar(i), 1);
+        mbar_init(bar(S_FULL), 1);
+        mbar_init(bar(DP_FULL), 1);
+        mbar_init(bar(P_READY), 256);
+        mbar_init(bar(DS_READY), 256);
+        mbar_init(bar(DV_DONE), 1);
+        mbar_init(bar(DK_DONE), 1);
+        mbar_init(bar(DV_FREE), 128);
+        mbar_init(bar(DK_FREE), 128);
         mbar_init(bar(DRAIN), 1);
         mbar_init(bar(DRAIN_G), 1);
         *abort = 0;
@@ -380,15 +379,25 @@ __global__ void __maxnreg__(168)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // One streamed tile (hi and, with SPLIT, lo) of query block i into a stage.
+    auto load_tile = [&](const CUtensorMap *tm, uint32_t stage, uint32_t full, int i) {
+        int64_t h, q0;
+        blk_coords(i, h, q0);
+        mbar_expect_tx(full, (SPLIT ? 2 : 1) * QB_BYTES);
+        for (int c = 0; c < CHUNKS; c++) {
+            tma_load_4d(tm, stage + c * QB_CHUNK, full, 32 * c, (int)q0, (int)h, (int)b);
+            if (SPLIT) tma_load_4d(tm, stage + QB_BYTES + c * QB_CHUNK, full, 32 * c, (int)q0, (int)h, lo_b);
+        }
+    };
+
     if (warp == W_PROD) {
-        // ----------------------------------------- producer: K / V, then the K-major ring ----
+        // --------------------------------- producer: K / V, then the Q_K and dO_K tiles ----
         if (lane == 0) {
-            int issued = -1;
-            // K and V hi into S stages 0-1 (K at 0, V at RES_BYTES); lo straight to their slots.
+            int qk_issued = -1, dok_issued = -1;
             mbar_expect_tx(bar(KV_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
             for (int c = 0; c < CHUNKS; c++) {
-                tma_load_4d(&tm_k, sb + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
-                tma_load_4d(&tm_v, sb + RES_BYTES + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                tma_load_4d(&tm_k, sb + OFF_QK + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                tma_load_4d(&tm_v, sb + OFF_DOK + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 if (SPLIT) {
                     tma_load_4d(&tm_k, sb + OFF_KLO + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
                     tma_load_4d(&tm_v, sb + OFF_VLO + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
@@ -396,211 +405,219 @@ __global__ void __maxnreg__(168)
             }
             bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
             for (int i = 0; ok && i < nblk; i++) {
-                int64_t h, q0;
-                blk_coords(i, h, q0);
-                const int ss = i % NSS;
-                if (i >= NSS && !mbar_wait(bar(SS_EMPTY + ss), ((i / NSS) - 1) & 1, abort, err)) break;
-                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE, fs = bar(SS_FULL + ss);
-                mbar_expect_tx(fs, (SPLIT ? 4 : 2) * BLK_BYTES);
-                for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = c * BLK_CHUNK;
-                    tma_load_4d(&tm_qk, sst + SS_QK + o, fs, 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_dok, sst + SS_DOK + o, fs, 32 * c, (int)q0, (int)h, (int)b);
-                    if (SPLIT) {
-                        tma_load_4d(&tm_qk, sst + SS_QK + BLK_BYTES + o, fs, 32 * c, (int)q0, (int)h, lo_b);
-                        tma_load_4d(&tm_dok, sst + SS_DOK + BLK_BYTES + o, fs, 32 * c, (int)q0, (int)h, lo_b);
-                    }
-                }
-                issued = i;
+                if (i >= 1 && !mbar_wait(bar(QK_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_qk, sb + OFF_QK, bar(QK_FULL), i);
+                qk_issued = i;
+                if (i >= 1 && !mbar_wait(bar(DOK_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_dok, sb + OFF_DOK, bar(DOK_FULL), i);
+                dok_issued = i;
             }
             if (*abort) {  // let the copies in flight land before the CTA exits
                 volatile int never = 0;
                 mbar_wait(bar(KV_FULL), 0, &never, nullptr);
-                for (int i = max(0, issued - NSS + 1); i <= issued; i++)
-                    mbar_wait(bar(SS_FULL + i % NSS), (i / NSS) & 1, &never, nullptr);
+                if (qk_issued >= 0) mbar_wait(bar(QK_FULL), qk_issued & 1, &never, nullptr);
+                if (dok_issued >= 0) mbar_wait(bar(DOK_FULL), dok_issued & 1, &never, nullptr);
             }
         }
     } else if (warp == W_PROD2) {
-        // ------------------------------------------------ producer: the MN-major ring ----
+        // ------------------------------------------ producer: the dO_MN and Q_MN tiles ----
         if (lane == 0) {
-            int issued = -1;
+            int domn_issued = -1, qmn_issued = -1;
             for (int i = 0; i < nblk; i++) {
-                int64_t h, q0;
-                blk_coords(i, h, q0);
-                const int sgi = i % NSG;
-                if (i >= NSG && !mbar_wait(bar(SG_EMPTY + sgi), ((i / NSG) - 1) & 1, abort, err)) break;
-                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE, fg = bar(SG_FULL + sgi);
-                mbar_expect_tx(fg, (SPLIT ? 4 : 2) * BLK_BYTES);
-                for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = c * BLK_CHUNK;
-                    tma_load_4d(&tm_qmn, gst + SG_QMN + o, fg, 32 * c, (int)q0, (int)h, (int)b);
-                    tma_load_4d(&tm_domn, gst + SG_DOMN + o, fg, 32 * c, (int)q0, (int)h, (int)b);
-                    if (SPLIT) {
-                        tma_load_4d(&tm_qmn, gst + SG_QMN + BLK_BYTES + o, fg, 32 * c, (int)q0, (int)h, lo_b);
-                        tma_load_4d(&tm_domn, gst + SG_DOMN + BLK_BYTES + o, fg, 32 * c, (int)q0, (int)h, lo_b);
-                    }
-                }
-                issued = i;
+                if (i >= 1 && !mbar_wait(bar(DOMN_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_domn, sb + OFF_DOMN, bar(DOMN_FULL), i);
+                domn_issued = i;
+                if (i >= 1 && !mbar_wait(bar(QMN_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_qmn, sb + OFF_QMN, bar(QMN_FULL), i);
+                qmn_issued = i;
                 if (*abort) break;
             }
             if (*abort) {
                 volatile int never = 0;
-                for (int i = max(0, issued - NSG + 1); i <= issued; i++)
-                    mbar_wait(bar(SG_FULL + i % NSG), (i / NSG) & 1, &never, nullptr);
+                if (domn_issued >= 0) mbar_wait(bar(DOMN_FULL), domn_issued & 1, &never, nullptr);
+                if (qmn_issued >= 0) mbar_wait(bar(QMN_FULL), qmn_issued & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
-        // ------------------------------------------------------- MMA: S^T and dP^T ------
-        {  // the whole warp, converged; one elected lane issues
+        // ---------------------------------------------------- MMA: S^T and dP^T, one warp ----
+        {
             const uint64_t klo = sdesc_sw128(sb + OFF_KLO, 16, 1024), vlo = sdesc_sw128(sb + OFF_VLO, 16, 1024);
             bool ok = warp_wait(bar(KV_READY), 0, abort, err);
             tc_fence_after();
             for (int i = 0; ok && i < nblk; i++) {
-                const int ss = i % NSS, bb = i & 1;
-                const uint32_t sst = sb + OFF_SRING + ss * SSTAGE;
-                // Buffer bb holds P^T / dS^T of block i-2 until its gradient MMAs finish.
-                if (i >= 2 && !warp_wait(bar(G_DONE + bb), ((i - 2) >> 1) & 1, abort, err)) break;
-                if (!warp_wait(bar(SS_FULL + ss), (i / NSS) & 1, abort, err)) break;
+                if (!warp_wait(bar(QK_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(DV_DONE), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_s<SPLIT>(tmem + c_s(bb), tmem + C_KHI, klo, sdesc_sw128(sst + SS_QK, 16, 1024));
-                mma_s<SPLIT>(tmem + c_dp(bb), tmem + C_VHI, vlo, sdesc_sw128(sst + SS_DOK, 16, 1024));
-                tc_commit_w(bar(S_FULL + bb));
-                tc_commit_w(bar(SS_EMPTY + ss));
+                mma_s<SPLIT, QB>(tmem + C_S, tmem + C_KHI, klo, sdesc_sw128(sb + OFF_QK, 16, 1024));
+                tc_commit_w(bar(S_FULL));
+                tc_commit_w(bar(QK_EMPTY));
+                if (!warp_wait(bar(DOK_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(DK_DONE), (i - 1) & 1, abort, err)) break;
+                tc_fence_after();
+                mma_s<SPLIT, QB>(tmem + C_DP, tmem + C_VHI, vlo, sdesc_sw128(sb + OFF_DOK, 16, 1024));
+                tc_commit_w(bar(DP_FULL));
+                tc_commit_w(bar(DOK_EMPTY));
             }
+            // Every MMA this warp issued completes before TMEM is released.
             tc_commit_w(bar(DRAIN));
             volatile int never = 0;
             warp_wait(bar(DRAIN), 0, &never, nullptr);
         }
     } else if (warp == W_GMMA) {
-        // ------------------------------------------------ MMA: dV_blk and dK_blk ------
-        {  // the whole warp, converged; one elected lane issues
-            for (int i = 0; i < nblk; i++) {
-                const int sgi = i % NSG, bb = i & 1;
-                const uint32_t gst = sb + OFF_GRING + sgi * GSTAGE;
-                if (!warp_wait(bar(P_FULL + bb), (i >> 1) & 1, abort, err)) break;
-                const bool first = (i % FOLD) == 0;
-                if (first && i >= FOLD && !warp_wait(bar(BLK_FREE), ((i / FOLD) - 1) & 1, abort, err)) break;
-                if (!warp_wait(bar(SG_FULL + sgi), (i / NSG) & 1, abort, err)) break;
+        // ------------------------------------------------ MMA: dV_blk and dK_blk, one warp ----
+        {
+            bool ok = true;
+            for (int i = 0; ok && i < nblk; i++) {
+                if (!warp_wait(bar(P_READY), i & 1, abort, err)) break;
+                if (!warp_wait(bar(DOMN_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(DV_FREE), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_g<SPLIT>(tmem + C_DV, tmem + c_s(bb), tmem + c_plo(bb),
-                             sdesc_mn_sw128_32b(gst + SG_DOMN, BLK_CHUNK, 512), !first);
-                mma_g<SPLIT>(tmem + C_DK, tmem + c_dp(bb), tmem + c_dslo(bb),
-                             sdesc_mn_sw128_32b(gst + SG_QMN, BLK_CHUNK, 512), !first);
-                tc_commit_w(bar(G_DONE + bb));
-                if ((i % FOLD) == FOLD - 1 || i == nblk - 1) tc_commit_w(bar(CHAIN_DONE));
-                tc_commit_w(bar(SG_EMPTY + sgi));
+                mma_g<SPLIT, QB>(tmem + C_DV, tmem + C_S, tmem + C_PLO,
+                                 sdesc_mn_sw128_32b(sb + OFF_DOMN, QB_CHUNK, 512), false);
+                tc_commit_w(bar(DV_DONE));
+                tc_commit_w(bar(DOMN_EMPTY));
+                if (!warp_wait(bar(DS_READY), i & 1, abort, err)) break;
+                if (!warp_wait(bar(QMN_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(DK_FREE), (i - 1) & 1, abort, err)) break;
+                tc_fence_after();
+                mma_g<SPLIT, QB>(tmem + C_DK, tmem + C_DP, tmem + C_DSLO,
+                                 sdesc_mn_sw128_32b(sb + OFF_QMN, QB_CHUNK, 512), false);
+                tc_commit_w(bar(DK_DONE));
+                tc_commit_w(bar(QMN_EMPTY));
             }
             tc_commit_w(bar(DRAIN_G));
             volatile int never = 0;
             warp_wait(bar(DRAIN_G), 0, &never, nullptr);
         }
     } else if (warp < W_PROD) {
-        // ---------------------------------- P^T and dS^T, then the fp32 dV / dK folds ----
+        // ------------------------- P^T and dS^T, then the fp32 dV / dK folds, every block ----
         const int quad = warp & 3, half = warp >> 2;  // lane quadrant; query-column half / dV or dK
         const int row = quad * 32 + lane;             // key row of this CTA
         const int64_t key = k0 + row;
         const bool key_ok = key < p.S;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        const int cb = half * 16;  // this thread's query columns of a block
+        const int cb = half * 32;  // this thread's query columns of a block
         float acc[D];
 #pragma unroll
         for (int x = 0; x < D; x++) acc[x] = 0.0f;
         bool ok = warp_wait(bar(KV_FULL), 0, abort, err);
         if (ok) {  // K (half 0) or V (half 1) hi rows into TMEM
-            row_to_tmem(sg + half * RES_BYTES, row, tl, half ? C_VHI : C_KHI);
+            row_to_tmem(sg + (half ? OFF_DOK : OFF_QK), row, tl, half ? C_VHI : C_KHI);
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(bar(KV_READY));
         }
-        const int nchain = (nblk + FOLD - 1) / FOLD;
-        int folded = 0;
-        auto fold = [&]() -> bool {
-            if (!warp_wait(bar(CHAIN_DONE), folded & 1, abort, err)) return false;
+        // Lane c holds the lse (base 2) and the delta of this half's query column c of block i.
+        auto colvals = [&](int i, float &lse2, float &del) {
+            int64_t h, q0;
+            blk_coords(i, h, q0);
+            const int64_t q = q0 + cb + lane;
+            lse2 = del = 0.0f;
+            if (q < p.L) {
+                const int64_t idx = (b * p.H + h) * p.L + q;
+                lse2 = a.lse2[idx];
+                del = a.g.delta[idx];
+            }
+        };
+        // Adds block i's accumulator (dV for half 0, dK for half 1) into registers and frees it.
+        // (Deferring it until after the next block's P^T was measured slower: the fold's TMEM
+        // loads then sit on the path to dS^T.)
+        auto fold = [&](int i) -> bool {
+            if (!warp_wait(bar(half ? DK_DONE : DV_DONE), i & 1, abort, err)) return false;
             tc_fence_after();
             const uint32_t col = half ? C_DK : C_DV;
 #pragma unroll
             for (int c = 0; c < D / 16; c++) fold16(tl + col + 16 * c, acc + 16 * c);
             tc_fence_before();
-            mbar_arrive(bar(BLK_FREE));
-            folded++;
+            mbar_arrive(bar(half ? DK_FREE : DV_FREE));
             return true;
         };
-        // Lanes 0-15 hold this half's 16 lse values (base 2) of block i, lanes 16-31 its deltas.
-        auto rowvals = [&](int i) -> float {
-            int64_t h, q0;
-            blk_coords(i, h, q0);
-            const int64_t q = q0 + cb + (lane & 15);
-            if (q >= p.L) return 0.0f;
-            const int64_t idx = (b * p.H + h) * p.L + q;
-            return lane < 16 ? a.lse2[idx] : a.g.delta[idx];
-        };
-        float cur = (ok && nblk > 0) ? rowvals(0) : 0.0f;
+        float cur_l = 0.0f, cur_d = 0.0f;
+        if (ok && nblk > 0) colvals(0, cur_l, cur_d);
         for (int i = 0; ok && i < nblk; i++) {
-            const int bb = i & 1;
             int64_t h, q0;
             blk_coords(i, h, q0);
-            const float nxt = i + 1 < nblk ? rowvals(i + 1) : 0.0f;
+            float nxt_l = 0.0f, nxt_d = 0.0f;
+            if (i + 1 < nblk) colvals(i + 1, nxt_l, nxt_d);
             // Column c is query base + c: valid below L and, under causal masking, from `key` on.
             const int64_t base = q0 + cb;
-            const bool edge = MASKED || !key_ok || q0 + BLK > p.L || (p.causal && key > q0);
-            uint32_t vbits = 0xFFFFu;
-            if (edge) vbits = key_ok ? col_bits(p.causal ? key - base : 0, p.L - base) : 0u;
+            const bool edge = MASKED || !key_ok || q0 + QB > p.L || (p.causal && key > q0);
+            uint32_t vbits = 0xFFFFFFFFu;
+            if (edge) vbits = key_ok ? col_bits32(p.causal ? key - base : 0, p.L - base) : 0u;
             // The user mask down this key's column, loaded before the wait for S.
-            float mk[MASKED ? 16 : 1];
-            if constexpr (MASKED) mask_run<16>(p, b, h, base, key, p.ms[2], vbits, mk);
+            float mk[MASKED ? 32 : 1];
+            if constexpr (MASKED) mask_run<32>(p, b, h, base, key, p.ms[2], vbits, mk);
             // Dropout: the keep bits of (query base + c, this key). The weights that meet dO are
             // P * Z; dS = P (Z dP - delta), Z = keep_scale where kept, 0 where dropped.
             uint32_t zb = 0;
-            if constexpr (DROP) zb = key_ok ? keep_col16(p, b, h, base, key) : 0u;
-            if (!warp_wait(bar(S_FULL + bb), (i >> 1) & 1, abort, err)) {
+            if constexpr (DROP) zb = key_ok ? keep_col<32>(p, b, h, base, key) : 0u;
+            if (!warp_wait(bar(S_FULL), i & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t sr[16], dr[16], phi[16], plo[16];
-            tmem_ld16(tl + c_s(bb) + cb, sr);
-            tmem_ld16(tl + c_dp(bb) + cb, dr);
-            tmem_wait_ld();
+            float pv[32];  // P (undropped) of this key and the 32 query columns
+            {
+                uint32_t sr[32];
+                tmem_ld32(tl + C_S + cb, sr);
+                tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                float x = __uint_as_float(sr[c]) * a.scale_log2;
-                if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
-                sr[c] = __float_as_uint(x);
-            }
-#pragma unroll
-            for (int c = 0; c < 16; c++) {
-                const float lse2 = __shfl_sync(FULL, cur, c), del = __shfl_sync(FULL, cur, 16 + c);
-                const float pc = ((vbits >> c) & 1u) ? ex2_approx(__uint_as_float(sr[c]) - lse2) : 0.0f;
-                float pw = pc, dpv = __uint_as_float(dr[c]);
-                if constexpr (DROP) {
-                    const bool kept = (zb >> c) & 1u;
-                    pw = kept ? pc * p.keep_scale : 0.0f;
-                    dpv = kept ? dpv * p.keep_scale : 0.0f;
-                }
-                const float ds = pc * (dpv - del);
-                phi[c] = tf32_rna(pw);
-                sr[c] = tf32_rna(ds);
-                if (SPLIT) {
-                    plo[c] = tf32_lo(pw, phi[c]);
-                    dr[c] = tf32_lo(ds, sr[c]);
+                for (int c = 0; c < 32; c++) {
+                    float x = __uint_as_float(sr[c]) * a.scale_log2;
+                    if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                    const float lse2 = __shfl_sync(FULL, cur_l, c);
+                    pv[c] = ((vbits >> c) & 1u) ? ex2_approx(x - lse2) : 0.0f;
                 }
             }
-            tmem_st16(tl + c_s(bb) + cb, phi);
-            tmem_st16(tl + c_dp(bb) + cb, sr);
-            if (SPLIT) {
-                tmem_st16(tl + c_plo(bb) + cb, plo);
-                tmem_st16(tl + c_dslo(bb) + cb, dr);
+#pragma unroll
+            for (int r0 = 0; r0 < 32; r0 += 16) {
+                uint32_t xh[16], xl[16];
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    float pw = pv[r0 + c];
+                    if constexpr (DROP) pw = ((zb >> (r0 + c)) & 1u) ? pw * p.keep_scale : 0.0f;
+                    xh[c] = tf32_rna(pw);
+                    if (SPLIT) xl[c] = tf32_lo(pw, xh[c]);
+                }
+                tmem_st16(tl + C_S + cb + r0, xh);
+                if (SPLIT) tmem_st16(tl + C_PLO + cb + r0, xl);
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(P_FULL + bb));
-            cur = nxt;
-            // The chain that ended with block i-1 completes while this block was in softmax.
-            if (i >= 1 && ((i - 1) % FOLD) == FOLD - 1 && !fold()) ok = false;
+            mbar_arrive(bar(P_READY));
+            if (!warp_wait(bar(DP_FULL), i & 1, abort, err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int r0 = 0; r0 < 32; r0 += 16) {
+                uint32_t dr[16], xh[16], xl[16];
+                tmem_ld16(tl + C_DP + cb + r0, dr);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    const float del = __shfl_sync(FULL, cur_d, r0 + c);
+                    float dpv = __uint_as_float(dr[c]);
+                    if constexpr (DROP) dpv = ((zb >> (r0 + c)) & 1u) ? dpv * p.keep_scale : 0.0f;
+                    const float ds = pv[r0 + c] * (dpv - del);
+                    xh[c] = tf32_rna(ds);
+                    if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
+                }
+                tmem_st16(tl + C_DP + cb + r0, xh);
+                if (SPLIT) tmem_st16(tl + C_DSLO + cb + r0, xl);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(DS_READY));
+            cur_l = nxt_l;
+            cur_d = nxt_d;
+            if (!fold(i)) {
+                ok = false;
+                break;
+            }
         }
-        while (ok && folded < nchain)
-            if (!fold()) ok = false;
         const bool aborted = __any_sync(FULL, *abort != 0);
         if (ok && !aborted && key_ok) {
             if (half) {
@@ -1064,10 +1081,10 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
         CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
         st = make_tmap(&tk, pa.khl, D, p.S, p.Hkv, nb, kst, TILE);
         if (!st) st = make_tmap(&tv, pa.vhl, D, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tqk, pa.qhl, D, p.L, p.H, nb, qst, BLK);
-        if (!st) st = make_tmap(&tqmn, pa.qhl, D, p.L, p.H, nb, qst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-        if (!st) st = make_tmap(&tdok, pa.dohl, D, p.L, p.H, nb, qst, BLK);
-        if (!st) st = make_tmap(&tdomn, pa.dohl, D, p.L, p.H, nb, qst, BLK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        if (!st) st = make_tmap(&tqk, pa.qhl, D, p.L, p.H, nb, qst, kv::QB);
+        if (!st) st = make_tmap(&tqmn, pa.qhl, D, p.L, p.H, nb, qst, kv::QB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        if (!st) st = make_tmap(&tdok, pa.dohl, D, p.L, p.H, nb, qst, kv::QB);
+        if (!st) st = make_tmap(&tdomn, pa.dohl, D, p.L, p.H, nb, qst, kv::QB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
         if (st) return st;
         decltype(&attn_bwd_dkdv_tc_kernel<true, true, true>) kernel;
         if (drop)

@@ -127,19 +127,21 @@ __device__ __forceinline__ uint32_t keep_run32(const AttnProblem &p, int64_t b, 
     return __funnelshift_r(lo, hi, (uint32_t)(e & 31));
 }
 
-// Dropout keep bits of the weights (b, h, i0 + c, j), c = 0..15 (down one key's column), bit c.
-__device__ __forceinline__ uint32_t keep_col16(const AttnProblem &p, int64_t b, int64_t h, int64_t i0, int64_t j) {
+// Dropout keep bits of the weights (b, h, i0 + c, j), c = 0..N-1 (down one key's column), bit c.
+template <int N>
+__device__ __forceinline__ uint32_t keep_col(const AttnProblem &p, int64_t b, int64_t h, int64_t i0, int64_t j) {
+    static_assert(N <= 32, "one word of bits");
     const int64_t nw = (p.B * p.H * p.L * p.S + 31) >> 5;
     const int64_t e0 = ((b * p.H + h) * p.L + i0) * p.S + j;
-    uint32_t words[16];
+    uint32_t words[N];
 #pragma unroll
-    for (int c = 0; c < 16; c++) {
+    for (int c = 0; c < N; c++) {
         const int64_t w = (e0 + c * p.S) >> 5;
         words[c] = w < nw ? __ldg(p.keep + w) : 0u;
     }
     uint32_t bits = 0;
 #pragma unroll
-    for (int c = 0; c < 16; c++) bits |= ((words[c] >> ((e0 + c * p.S) & 31)) & 1u) << c;
+    for (int c = 0; c < N; c++) bits |= ((words[c] >> ((e0 + c * p.S) & 31)) & 1u) << c;
     return bits;
 }
 
