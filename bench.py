@@ -421,8 +421,12 @@ def main():
     # tensor-core backward's dK/dV and dQ kernels share the GPU (two streams): their joint
     # record "bwd_tc" is the unit, not either kernel alone.
     pk = peaks()
+    # Kernels without a roofline of their own (the dropout mask draw: integer generator work,
+    # neither HBM- nor tensor-bound) are named in "slowest_kernel" but are not the unit.
     concurrent = ("bwd_dkdv_tc", "bwd_dq_tc") if "bwd_tc" in kernels else ()
     candidates = {k_: v_ for k_, v_ in kernels.items() if k_ not in concurrent}
+    slowest = max(candidates.items(), key=lambda kv: kv[1][1])[0] if candidates else None
+    candidates = {k_: v_ for k_, v_ in candidates.items() if kernel_work(w, k_) > 0 or ring is not None}
     dom = max(candidates.items(), key=lambda kv: kv[1][1]) if candidates else None
     roofline = None
     if dom is not None:
@@ -448,7 +452,8 @@ def main():
             traffic = per.get(kname)
             if kname == "bwd_tc" and traffic is None and "bwd_dkdv_tc" in per and "bwd_dq_tc" in per:
                 traffic = per["bwd_dkdv_tc"] + per["bwd_dq_tc"]
-        roofline = {"kernel": kname, "bound": bound, "achieved": achieved, "peak": peak, "unit": ru,
+        roofline = {"kernel": kname, "slowest_kernel": slowest, "bound": bound, "achieved": achieved, "peak": peak,
+                    "unit": ru,
                     "frac": achieved / peak, "traffic": traffic, "avg_launch_ms": avg_ms,
                     "peak_source": (f"{pk['src']} hbm_gbs" if bound == "hbm"
                                     else f"{pk['src']} bf16_tflops / 2 (dense TF32 rate)")}
