@@ -1,45 +1,45 @@
-// attn_tc_bwd.cu -- tcgen05 tensor-core attention backward for sm_100a (head dim 64).
+// attn_tc_bwd.cu -- tcgen05 tensor-core attention backward for sm_100a (head dims 64 and 128).
 //
 // Replaces DenseCore's torch_attention::backward (src/torch_attention.rs:291-468), which per
 // (q block, kv block) recomputes P = exp(scale*S + mask - lse) (:338-380) and accumulates
 //   dV += P^T dO, dP = dO V^T, dS = P (dP - delta), dQ += scale dS K, dK += scale dS^T Q
 // (:381-446), with delta = sum(dO * O) per row (:327-330).
 //
-// Three launches:
+// Three launches (the last two run concurrently, on the caller's stream and a second one):
 //
 //   prep: one pass over q, grad_out, out, k and v (HBM-bound). Writes TF32 hi = tf32(x) and
 //         lo = tf32(x - hi) copies of q, grad_out, k and v into contiguous scratch (3xTF32:
 //         a*b ~ ah*bl + al*bh + ah*bh), delta per query row, and lse in base 2. The tensor-core
 //         kernels then load ready operands with TMA and never convert on the critical path;
 //         they also accept inputs of any strides.
-//   dkdv: a CTA owns 128 keys of one (batch, kv head). K and V are the A operands: hi in TMEM,
-//         lo in shared memory. 32-row blocks of Q and dO (hi and lo, each in the K-major
-//         128-byte swizzle and in the MN-major 32-byte-atom swizzle that tf32 requires) stream
-//         through two rings: the K-major tiles (3 stages) are free once the S / dP MMAs have
-//         read them, the MN-major tiles (2 stages) once the gradient MMAs have. Per block i:
-//         S^T = K Q^T and dP^T = V dO^T into one of two TMEM buffers; eight softmax warps
-//         (two per TMEM lane quadrant, 16 query columns each) turn them into P^T and dS^T
-//         (hi / lo, in place); then dV_blk += P^T dO and dK_blk += dS^T Q. S_{i+1} runs on the
-//         tensor core while the softmax warps work on block i. The same warps add the block
-//         accumulators into fp32 registers every FOLD blocks (the tensor core's accumulation is
-//         coarser than fp32 over long chains): the first four keep dV, the other four dK.
-//   dq:   a CTA owns 128 query rows of one (batch, head). Q and dO are the A operands (hi and
-//         lo in TMEM, so that no pass reads A from shared memory); 64-key blocks of K and V
-//         (K-major) and of K (MN-major) stream through three two-stage rings. Per
-//         block: S = Q K^T and dP = dO V^T (N = 64), dS in TMEM, dQ_blk = dS K, folded into
-//         fp32 registers (each softmax warp keeps 32 of the 64 dQ columns). The S, dP and dQ
-//         columns are single; the order in which one warp issues the MMAs keeps the tensor
+//   dkdv: a CTA owns 128 keys of one (batch, kv head) -- at head dim 128, one 64-column half of
+//         their dK and dV (two CTAs per tile, both recomputing S^T and dP^T). K and V are the A
+//         operands: hi in TMEM, lo in shared memory. Blocks of 64 (head dim 64) or 32 (128)
+//         query rows stream as four tiles, Q and dO each K-major (the S / dP MMAs) and MN-major
+//         (the gradient MMAs, this CTA's 64 columns), one stage each, each freed by its reader.
+//         Per block i: S^T = K Q^T and dP^T = V dO^T (one MMA warp), P^T while dP^T runs, dS^T
+//         while dV runs, dV_blk = P^T dO and dK_blk = dS^T Q (a second MMA warp); eight softmax
+//         warps (two per TMEM lane quadrant) then fold the block accumulators into fp32
+//         registers (the tensor core's accumulation is coarser than fp32 over long chains):
+//         the first four keep dV, the other four dK.
+//   dq:   a CTA owns 128 query rows of one (batch, head) -- at head dim 128, one 64-column half
+//         of their dQ. Q and dO are the A operands: hi and lo in TMEM at head dim 64, hi in TMEM
+//         and lo in shared memory at 128. Blocks of 64 (64) or 32 (128) keys of K and V
+//         (K-major) and of K (MN-major, this CTA's columns) stream through three rings, each
+//         freed by its reader. Per block: S = Q K^T and dP = dO V^T, dS in TMEM, dQ_blk = dS K,
+//         folded into fp32 registers (each softmax warp keeps 32 of the 64 columns). The S, dP
+//         and dQ columns are single; the order in which the MMAs are issued keeps the tensor
 //         core busy (see the kernel).
 //
 // Roles: warps 0-7 softmax + fold, warp 8 TMA producer, warp 9 MMA issuer (the whole warp,
 // converged, with one elected lane issuing; it also owns TMEM), warp 10 a second TMA producer
-// (the MN-major ring, so that the K-major ring can run ahead of it), warp 11 the gradient MMAs
-// (so that either issuer's barrier waits overlap the other's MMAs). Every wait is bounded; a timeout records an error and unwinds. The softmax loops stay
-// branch-free per column (validity as a bit mask; a user mask in a separate pass) to keep the
-// hot code small: twelve warps running different loops already crowd the instruction cache.
-// Grids are 1-D: groups of GROUP_HEADS (batch, head) pairs, and within a group the tiles with
-// the most causal work first. The group keeps the streamed operands of its heads in L2; the
-// order within it keeps the last wave short.
+// (the MN-major tiles), warp 11 the gradient MMAs (so that either issuer's barrier waits
+// overlap the other's MMAs). Every wait is bounded; a timeout records an error and unwinds.
+// The softmax loops stay branch-free per column (validity as a bit mask; a user mask in a
+// separate pass) to keep the hot code small: twelve warps running different loops already
+// crowd the instruction cache. Grids are 1-D: groups of GROUP_HEADS (batch, head[, half])
+// units, and within a group the tiles with the most causal work first. The group keeps the
+// streamed operands of its heads in L2; the order within it keeps the last wave short.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -58,11 +58,9 @@ namespace {
 using namespace sm100;
 
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr int D = 64;        // head dim of these kernels
-constexpr int CHUNKS = D / 32;
+constexpr int D = 64;        // head dim of the helpers' defaults; the MN-major gradient tiles are 64 wide
 constexpr int TILE = 128;    // rows owned by a CTA (the MMA M)
-constexpr int BLK = 32;      // streamed rows per step (the MMA N of S / dP, the K of the rest)
-constexpr int FOLD = 2;      // blocks per tensor-core accumulation chain
+constexpr int BLK = 32;      // default streamed rows per block of the MMA helpers
 constexpr int THREADS = 384; // 8 softmax / fold warps, 2 producers, 2 MMA issuers
 constexpr int W_PROD = 8, W_MMA = 9, W_PROD2 = 10, W_GMMA = 11;
 constexpr int GROUP_HEADS = 16;  // (batch, head) pairs whose tiles are handed out together
@@ -70,10 +68,7 @@ constexpr unsigned FULL = 0xffffffffu;
 
 constexpr uint32_t RES_BYTES = TILE * D * 4;      // one resident fp32 tile (32 KB)
 constexpr uint32_t RES_CHUNK = TILE * 128;        // 16 KB per 32-column chunk
-constexpr uint32_t BLK_BYTES = BLK * D * 4;       // one streamed fp32 tile (8 KB)
-constexpr uint32_t BLK_CHUNK = BLK * 128;         // 4 KB per chunk
 
-constexpr uint32_t IDESC_S = idesc_tf32(128, BLK, 0, 0);  // S / dP: N = 32, both K-major
 constexpr uint32_t IDESC_G = idesc_tf32(128, D, 0, 1);    // gradients: N = 64, B MN-major
 
 // k-step offsets in 16-byte units: K-major 128-byte swizzle (8 tf32 = 32 bytes per k-step,
@@ -85,44 +80,43 @@ __device__ __forceinline__ constexpr uint32_t koff(int kk) {
 }
 __device__ __forceinline__ constexpr uint32_t mnoff(int kk) { return (uint32_t)(kk * 64); }
 
-// S-type product over D (3 passes with SPLIT, cross terms first):
+// S-type product over the head dim DD (3 passes with SPLIT, cross terms first):
 //   d = A_hi B_lo + A_lo B_hi + A_hi B_hi,
 // A_hi in TMEM (columns a_hi + 8 kk), A_lo in shared memory (K-major, TILE rows, descriptor
-// a_lo), B hi / lo K-major NB-row tiles in shared memory (descriptor b_hi, lo NB * D * 4 bytes
+// a_lo), B hi / lo K-major NB-row tiles in shared memory (descriptor b_hi, lo NB * DD * 4 bytes
 // further); N = NB.
-template <bool SPLIT, int NB = BLK>
+template <bool SPLIT, int NB = BLK, int DD = D>
 __device__ __forceinline__ void mma_s(uint32_t d, uint32_t a_hi, uint64_t a_lo, uint64_t b_hi) {
-    constexpr uint32_t BLO = (uint32_t)(NB * D * 4) >> 4, CH = NB * 128;
+    constexpr uint32_t BLO = (uint32_t)(NB * DD * 4) >> 4, CH = NB * 128;
     constexpr uint32_t ID = idesc_tf32(128, NB, 0, 0);
     if (SPLIT) {
 #pragma unroll
-        for (int kk = 0; kk < D / 8; kk++) {
+        for (int kk = 0; kk < DD / 8; kk++) {
             mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<CH>(kk)), ID, kk > 0 ? 1u : 0u);
             mma_tf32_ss_w(d, a_lo + koff<RES_CHUNK>(kk), b_hi + koff<CH>(kk), ID, 1u);
         }
     }
 #pragma unroll
-    for (int kk = 0; kk < D / 8; kk++)
+    for (int kk = 0; kk < DD / 8; kk++)
         mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<CH>(kk), ID, (SPLIT || kk > 0) ? 1u : 0u);
 }
 
-// mma_s with A_lo in TMEM too (columns a_lo + 8 kk) and an NB-row streamed B tile (N = NB):
-// every pass reads A from TMEM and only the streamed B tile from shared memory. An A operand in
-// shared memory costs the tensor core 4 KB of shared-memory reads per k-step, more than the
-// whole N = 32 product.
-template <bool SPLIT, int NB = BLK>
+// mma_s with A_lo in TMEM too (columns a_lo + 8 kk): every pass reads A from TMEM and only
+// the streamed B tile from shared memory. An A operand in shared memory costs the tensor core
+// 4 KB of shared-memory reads per k-step, more than the whole N = 32 product.
+template <bool SPLIT, int NB = BLK, int DD = D>
 __device__ __forceinline__ void mma_s_t(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t b_hi) {
-    constexpr uint32_t BLO = (uint32_t)(NB * D * 4) >> 4, CH = NB * 128;
+    constexpr uint32_t BLO = (uint32_t)(NB * DD * 4) >> 4, CH = NB * 128;
     constexpr uint32_t ID = idesc_tf32(128, NB, 0, 0);
     if (SPLIT) {
 #pragma unroll
-        for (int kk = 0; kk < D / 8; kk++) {
+        for (int kk = 0; kk < DD / 8; kk++) {
             mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + (BLO + koff<CH>(kk)), ID, kk > 0 ? 1u : 0u);
             mma_tf32_ts_w(d, a_lo + kk * 8, b_hi + koff<CH>(kk), ID, 1u);
         }
     }
 #pragma unroll
-    for (int kk = 0; kk < D / 8; kk++)
+    for (int kk = 0; kk < DD / 8; kk++)
         mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + koff<CH>(kk), ID, (SPLIT || kk > 0) ? 1u : 0u);
 }
 
@@ -143,11 +137,12 @@ __device__ __forceinline__ void mma_g(uint32_t d, uint32_t a_hi, uint32_t a_lo, 
         mma_tf32_ts_w(d, a_hi + kk * 8, b_hi + mnoff(kk), IDESC_G, (accumulate || SPLIT || kk > 0) ? 1u : 0u);
 }
 
-// Row `row` of a 128-byte-swizzled TILE-row tile in shared memory into TMEM columns
-// [col, col + 64) of this thread's lane. A full warp calls it.
+// Row `row` of a 128-byte-swizzled TILE-row tile (DD columns) in shared memory into TMEM
+// columns [col, col + DD) of this thread's lane. A full warp calls it.
+template <int DD = D>
 __device__ __forceinline__ void row_to_tmem(const uint8_t *tile, int row, uint32_t tlane, uint32_t col) {
 #pragma unroll
-    for (int c = 0; c < CHUNKS; c++) {
+    for (int c = 0; c < DD / 32; c++) {
         uint32_t v[32];
 #pragma unroll
         for (int g = 0; g < 8; g++) {
@@ -255,13 +250,16 @@ __device__ __forceinline__ void split_store(float *hl, int64_t at, int64_t lo_of
     }
 }
 
-// 16 lanes per row of 64: rows of (q, grad_out, out) first, then rows of (k, v).
+// DD / 4 lanes per row of DD (a float4 each): rows of (q, grad_out, out) first, then rows of
+// (k, v).
+template <int DD>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
+    constexpr int LPR = DD / 4, RPB = 256 / LPR;  // lanes per row, rows per block
     const AttnProblem &p = a.p;
     const int64_t rows_a = p.B * p.H * p.L, rows_b = p.B * p.Hkv * p.S;
-    const int64_t r = (int64_t)blockIdx.x * 16 + threadIdx.x / 16;
-    const int j = threadIdx.x & 15;
-    const unsigned half_mask = 0xFFFFu << (threadIdx.x & 16);
+    const int64_t r = (int64_t)blockIdx.x * RPB + threadIdx.x / LPR;
+    const int j = threadIdx.x % LPR;
+    const unsigned group_mask = LPR == 32 ? FULL : (0xFFFFu << (threadIdx.x & 16));
     if (r < rows_a) {
         const int64_t l = r % p.L, bh = r / p.L, h = bh % p.H, b = bh / p.H;
         const float4 q4 = load4(p.q + b * p.qs[0] + h * p.qs[1] + l * p.qs[2], p.qs[3], j, a.vec);
@@ -269,9 +267,9 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
         const float4 o4 = load4(p.out + b * p.os[0] + h * p.os[1] + l * p.os[2], p.os[3], j, a.vec);
         float s = fmaf(d4.w, o4.w, fmaf(d4.z, o4.z, fmaf(d4.y, o4.y, d4.x * o4.x)));
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(half_mask, s, o);
-        split_store(a.qhl, r * D + 4 * j, rows_a * D, q4, a.split);
-        split_store(a.dohl, r * D + 4 * j, rows_a * D, d4, a.split);
+        for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(group_mask, s, o);
+        split_store(a.qhl, r * DD + 4 * j, rows_a * DD, q4, a.split);
+        split_store(a.dohl, r * DD + 4 * j, rows_a * DD, d4, a.split);
         if (j == 0) {
             a.g.delta[r] = s;
             a.lse2[r] = p.lse[b * p.ls[0] + h * p.ls[1] + l * p.ls[2]] * LOG2E;
@@ -281,53 +279,67 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
         const int64_t sidx = rr % p.S, bh = rr / p.S, hk = bh % p.Hkv, b = bh / p.Hkv;
         const float4 k4 = load4(p.k + b * p.ks[0] + hk * p.ks[1] + sidx * p.ks[2], p.ks[3], j, a.vec);
         const float4 v4 = load4(p.v + b * p.vs[0] + hk * p.vs[1] + sidx * p.vs[2], p.vs[3], j, a.vec);
-        split_store(a.khl, rr * D + 4 * j, rows_b * D, k4, a.split);
-        split_store(a.vhl, rr * D + 4 * j, rows_b * D, v4, a.split);
+        split_store(a.khl, rr * DD + 4 * j, rows_b * DD, k4, a.split);
+        split_store(a.vhl, rr * DD + 4 * j, rows_b * DD, v4, a.split);
     }
 }
 
 // ==================================================================== dK / dV ========
-namespace kv {
-// 64-query blocks: S^T and dP^T run at N = 64, where an MMA does twice the work of an N = 32
-// one for a little more time. Tensor memory then holds one block's S^T / P^T and dP^T / dS^T
-// (single buffers), and shared memory one stage per streamed tile, each freed by its reader.
-constexpr int QB = 64;
-constexpr uint32_t QB_BYTES = QB * D * 4;  // one streamed fp32 tile (16 KB)
-constexpr uint32_t QB_CHUNK = QB * 128;    // 8 KB per 32-column chunk
-constexpr uint32_t TSTAGE = 2 * QB_BYTES;  // a tile's hi and lo copies (32 KB)
-// Q_K, dO_K (K-major: the S / dP MMAs), dO_MN, Q_MN (MN-major: the dV / dK MMAs), then the
-// resident K lo and V lo. K hi and V hi wait in the Q_K and dO_K stages until they are in TMEM.
-constexpr uint32_t OFF_QK = 0, OFF_DOK = TSTAGE, OFF_DOMN = 2 * TSTAGE, OFF_QMN = 3 * TSTAGE;
-constexpr uint32_t OFF_KLO = 4 * TSTAGE, OFF_VLO = OFF_KLO + RES_BYTES;
-constexpr uint32_t OFF_BAR = OFF_VLO + RES_BYTES;
-// Per block i: S^T (S_FULL) turned into P^T (P_READY); dP^T (DP_FULL) into dS^T (DS_READY);
-// dV (DV_DONE: P^T read, S^T_{i+1} may overwrite it) and dK (DK_DONE: dS^T read, dP^T_{i+1}
-// may overwrite it); DV_FREE / DK_FREE: the fold has read that accumulator.
-enum { KV_FULL, KV_READY, QK_FULL, QK_EMPTY, DOK_FULL, DOK_EMPTY, DOMN_FULL, DOMN_EMPTY, QMN_FULL, QMN_EMPTY,
-       S_FULL, DP_FULL, P_READY, DS_READY, DV_DONE, DK_DONE, DV_FREE, DK_FREE, DRAIN, DRAIN_G, NBAR };
-constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
-// TMEM: K hi | V hi | S^T / P^T hi | P^T lo | dP^T / dS^T hi | dS^T lo | dV_blk | dK_blk
-constexpr uint32_t C_KHI = 0, C_VHI = 64, C_S = 128, C_PLO = 192, C_DP = 256, C_DSLO = 320, C_DV = 384, C_DK = 448,
-                   TCOLS = 512;
-static_assert(RES_BYTES <= TSTAGE, "K / V hi are staged in the Q_K and dO_K stages");
-static_assert(SMEM <= 232448, "smem");
-}  // namespace kv
+// Head dim DD = 64: a CTA computes all of dK and dV for its keys. DD = 128: two CTAs per key
+// tile, each computing one 64-column half of dK and dV (both recompute S^T and dP^T over the
+// whole head dim), so that tensor memory holds K hi and V hi (DD columns each), one S^T / dP^T
+// block and the two half accumulators.
+template <int DD>
+struct KvCfg {
+    static constexpr int NH = DD / 64;            // gradient column halves (CTAs per key tile)
+    static constexpr int QB = DD == 64 ? 64 : 32; // query rows per streamed block (S / dP's N)
+    static constexpr int CPT = QB / 2;            // query columns per softmax thread
+    static constexpr uint32_t RESB = TILE * DD * 4;     // resident K or V tile (hi or lo)
+    static constexpr uint32_t TK_BYTES = QB * DD * 4;   // K-major streamed tile (hi or lo)
+    static constexpr uint32_t TK_CHUNK = QB * 128;
+    static constexpr uint32_t TM_BYTES = QB * 64 * 4;   // MN-major half tile (hi or lo)
+    static constexpr uint32_t TM_CHUNK = QB * 128;
+    // Shared memory: K lo | V lo | Q_K | dO_K | dO_MN | Q_MN (hi + lo each), one stage per
+    // streamed tile, each freed by its own reader. K hi and V hi wait for the softmax warps to
+    // move them into TMEM: DD = 64 in the Q_K and dO_K stages, DD = 128 in the K lo / V lo
+    // areas (whose lo copies are loaded after).
+    static constexpr uint32_t OFF_KLO = 0, OFF_VLO = RESB, OFF_QK = 2 * RESB, OFF_DOK = OFF_QK + 2 * TK_BYTES,
+                              OFF_DOMN = OFF_DOK + 2 * TK_BYTES, OFF_QMN = OFF_DOMN + 2 * TM_BYTES,
+                              OFF_BAR = OFF_QMN + 2 * TM_BYTES;
+    static constexpr uint32_t OFF_KHI_STAGE = DD == 64 ? OFF_QK : OFF_KLO;
+    static constexpr uint32_t OFF_VHI_STAGE = DD == 64 ? OFF_DOK : OFF_VLO;
+    // Per block i: S^T (S_FULL) turned into P^T (P_READY); dP^T (DP_FULL) into dS^T (DS_READY);
+    // dV (DV_DONE: P^T read, S^T_{i+1} may overwrite it) and dK (DK_DONE: dS^T read, dP^T_{i+1}
+    // may overwrite it); DV_FREE / DK_FREE: the fold has read that accumulator. KVLO_FULL: the
+    // resident lo copies (DD = 128 loads them once the hi tiles are in TMEM).
+    enum { KV_FULL, KV_READY, KVLO_FULL, QK_FULL, QK_EMPTY, DOK_FULL, DOK_EMPTY, DOMN_FULL, DOMN_EMPTY, QMN_FULL,
+           QMN_EMPTY, S_FULL, DP_FULL, P_READY, DS_READY, DV_DONE, DK_DONE, DV_FREE, DK_FREE, DRAIN, DRAIN_G,
+           NBAR };
+    static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
+    static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
+    // TMEM: K hi | V hi | S^T / P^T hi | P^T lo | dP^T / dS^T hi | dS^T lo | dV_blk | dK_blk
+    static constexpr uint32_t C_KHI = 0, C_VHI = DD, C_S = 2 * DD, C_PLO = C_S + QB, C_DP = C_S + 2 * QB,
+                              C_DSLO = C_S + 3 * QB, C_DV = C_S + 4 * QB, C_DK = C_DV + 64, TCOLS = 512;
+    static_assert(C_DK + 64 <= TCOLS, "tensor memory budget");
+    static_assert(RESB <= 2 * TK_BYTES || DD != 64, "K / V hi are staged in the Q_K and dO_K stages");
+    static_assert(SMEM <= 232448, "smem");
+};
 
-// tm_k / tm_v: (64, S, Hkv, S2*B) over the hi / lo copies (lo at batch B + b), box 128 rows;
-// tm_q* / tm_do*: (64, L, H, S2*B), box 64 rows, K-major (128-byte swizzle) or MN-major
-// (32-byte-atom swizzle).
+// tm_k / tm_v: (DD, S, Hkv, S2*B) over the hi / lo copies (lo at batch B + b), box 128 rows;
+// tm_q* / tm_do*: (DD, L, H, S2*B), box QB rows, K-major (128-byte swizzle) or MN-major
+// (32-byte-atom swizzle; this CTA's 64-column half).
 //
 // MMA order per block i: S^T_i, dP^T_i (warp 9), dV_i, dK_i (warp 11). S^T_{i+1} waits for dV_i
 // and runs after dK_i; dP^T_{i+1} waits for dK_i. The softmax warps compute P^T_i while dP^T_i
 // runs and dS^T_i while dV_i runs.
-template <bool SPLIT, bool MASKED, bool DROP>
+template <int DD, bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(168)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_qmn,
                             const __grid_constant__ CUtensorMap tm_dok, const __grid_constant__ CUtensorMap tm_domn,
                             const TcBwdArgs a) {
-    using namespace kv;
+    using C = KvCfg<DD>;
+    constexpr int QB = C::QB, CPT = C::CPT;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -335,8 +347,10 @@ __global__ void __maxnreg__(168)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
     // Key tiles in ascending order: under causal masking tile 0 sees the most query rows.
-    int64_t kt, bh;
-    grouped_tile(blockIdx.x, (p.S + TILE - 1) / TILE, p.B * p.Hkv, kt, bh);
+    int64_t kt, bhd;
+    grouped_tile(blockIdx.x, (p.S + TILE - 1) / TILE, p.B * p.Hkv * C::NH, kt, bhd);
+    const int dh = (int)(bhd % C::NH);  // gradient column half
+    const int64_t bh = bhd / C::NH;
     const int64_t hk = bh % p.Hkv, b = bh / p.Hkv, k0 = kt * TILE;
     const int lo_b = (int)(p.B + b);  // batch coordinate of the lo copies
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
@@ -344,9 +358,9 @@ __global__ void __maxnreg__(168)
     const int qb_first = (int)(r_begin / QB);
     const int qb_per_head = (int)((p.L + QB - 1) / QB) - qb_first;
     const int nblk = qb_per_head * p.group;
-    auto bar = [&](int i) { return sb + OFF_BAR + 8u * (uint32_t)i; };
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + OFF_MISC);
-    volatile int *abort = reinterpret_cast<volatile int *>(sg + OFF_MISC + 4);
+    auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
+    volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
     int *err = a.err;
     auto blk_coords = [&](int i, int64_t &h, int64_t &q0) {
         h = hk * p.group + i / qb_per_head;
@@ -354,24 +368,25 @@ __global__ void __maxnreg__(168)
     };
 
     if (threadIdx.x == 0) {
-        mbar_init(bar(KV_FULL), 1);
-        mbar_init(bar(KV_READY), 256);
-        for (int i = QK_FULL; i <= QMN_EMPTY; i++) mbar_init(bar(i), 1);
-        mbar_init(bar(S_FULL), 1);
-        mbar_init(bar(DP_FULL), 1);
-        mbar_init(bar(P_READY), 256);
-        mbar_init(bar(DS_READY), 256);
-        mbar_init(bar(DV_DONE), 1);
-        mbar_init(bar(DK_DONE), 1);
-        mbar_init(bar(DV_FREE), 128);
-        mbar_init(bar(DK_FREE), 128);
-        mbar_init(bar(DRAIN), 1);
-        mbar_init(bar(DRAIN_G), 1);
+        mbar_init(bar(C::KV_FULL), 1);
+        mbar_init(bar(C::KV_READY), 256);
+        mbar_init(bar(C::KVLO_FULL), 1);
+        for (int i = C::QK_FULL; i <= C::QMN_EMPTY; i++) mbar_init(bar(i), 1);
+        mbar_init(bar(C::S_FULL), 1);
+        mbar_init(bar(C::DP_FULL), 1);
+        mbar_init(bar(C::P_READY), 256);
+        mbar_init(bar(C::DS_READY), 256);
+        mbar_init(bar(C::DV_DONE), 1);
+        mbar_init(bar(C::DK_DONE), 1);
+        mbar_init(bar(C::DV_FREE), 128);
+        mbar_init(bar(C::DK_FREE), 128);
+        mbar_init(bar(C::DRAIN), 1);
+        mbar_init(bar(C::DRAIN_G), 1);
         *abort = 0;
         fence_mbar_init();
     }
     if (warp == W_MMA) {
-        tmem_alloc(smem_addr(tmem_slot), TCOLS);
+        tmem_alloc(smem_addr(tmem_slot), C::TCOLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -379,44 +394,58 @@ __global__ void __maxnreg__(168)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // One streamed tile (hi and, with SPLIT, lo) of query block i into a stage.
-    auto load_tile = [&](const CUtensorMap *tm, uint32_t stage, uint32_t full, int i) {
+    // One streamed tile (hi and, with SPLIT, lo) of query block i into a stage: all DD columns
+    // (K-major) or this CTA's 64-column half (MN-major).
+    auto load_tile = [&](const CUtensorMap *tm, uint32_t stage, uint32_t full, int i, bool mn) {
         int64_t h, q0;
         blk_coords(i, h, q0);
-        mbar_expect_tx(full, (SPLIT ? 2 : 1) * QB_BYTES);
-        for (int c = 0; c < CHUNKS; c++) {
-            tma_load_4d(tm, stage + c * QB_CHUNK, full, 32 * c, (int)q0, (int)h, (int)b);
-            if (SPLIT) tma_load_4d(tm, stage + QB_BYTES + c * QB_CHUNK, full, 32 * c, (int)q0, (int)h, lo_b);
+        const int nch = mn ? 2 : DD / 32;
+        const uint32_t bytes = mn ? C::TM_BYTES : C::TK_BYTES, chunk = mn ? C::TM_CHUNK : C::TK_CHUNK;
+        const int col0 = mn ? 64 * dh : 0;
+        mbar_expect_tx(full, (SPLIT ? 2 : 1) * bytes);
+        for (int c = 0; c < nch; c++) {
+            tma_load_4d(tm, stage + c * chunk, full, col0 + 32 * c, (int)q0, (int)h, (int)b);
+            if (SPLIT) tma_load_4d(tm, stage + bytes + c * chunk, full, col0 + 32 * c, (int)q0, (int)h, lo_b);
         }
     };
 
     if (warp == W_PROD) {
-        // --------------------------------- producer: K / V, then the Q_K and dO_K tiles ----
+        // ------------------------ producer: K / V (hi, then lo), then the Q_K and dO_K tiles ----
         if (lane == 0) {
             int qk_issued = -1, dok_issued = -1;
-            mbar_expect_tx(bar(KV_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
-            for (int c = 0; c < CHUNKS; c++) {
-                tma_load_4d(&tm_k, sb + OFF_QK + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
-                tma_load_4d(&tm_v, sb + OFF_DOK + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
-                if (SPLIT) {
-                    tma_load_4d(&tm_k, sb + OFF_KLO + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
-                    tma_load_4d(&tm_v, sb + OFF_VLO + c * RES_CHUNK, bar(KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+            const bool lo_later = DD != 64;  // DD = 128 stages the hi tiles in the lo areas
+            mbar_expect_tx(bar(C::KV_FULL), ((SPLIT && !lo_later) ? 4 : 2) * C::RESB);
+            for (int c = 0; c < DD / 32; c++) {
+                tma_load_4d(&tm_k, sb + C::OFF_KHI_STAGE + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                tma_load_4d(&tm_v, sb + C::OFF_VHI_STAGE + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                if (SPLIT && !lo_later) {
+                    tma_load_4d(&tm_k, sb + C::OFF_KLO + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                    tma_load_4d(&tm_v, sb + C::OFF_VLO + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
                 }
             }
-            bool ok = mbar_wait(bar(KV_READY), 0, abort, err);
+            if (!SPLIT || !lo_later) mbar_arrive(bar(C::KVLO_FULL));
+            bool ok = mbar_wait(bar(C::KV_READY), 0, abort, err);
+            if (ok && SPLIT && lo_later) {
+                mbar_expect_tx(bar(C::KVLO_FULL), 2 * C::RESB);
+                for (int c = 0; c < DD / 32; c++) {
+                    tma_load_4d(&tm_k, sb + C::OFF_KLO + c * RES_CHUNK, bar(C::KVLO_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                    tma_load_4d(&tm_v, sb + C::OFF_VLO + c * RES_CHUNK, bar(C::KVLO_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                }
+            }
             for (int i = 0; ok && i < nblk; i++) {
-                if (i >= 1 && !mbar_wait(bar(QK_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_qk, sb + OFF_QK, bar(QK_FULL), i);
+                if (i >= 1 && !mbar_wait(bar(C::QK_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_qk, sb + C::OFF_QK, bar(C::QK_FULL), i, false);
                 qk_issued = i;
-                if (i >= 1 && !mbar_wait(bar(DOK_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_dok, sb + OFF_DOK, bar(DOK_FULL), i);
+                if (i >= 1 && !mbar_wait(bar(C::DOK_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_dok, sb + C::OFF_DOK, bar(C::DOK_FULL), i, false);
                 dok_issued = i;
             }
             if (*abort) {  // let the copies in flight land before the CTA exits
                 volatile int never = 0;
-                mbar_wait(bar(KV_FULL), 0, &never, nullptr);
-                if (qk_issued >= 0) mbar_wait(bar(QK_FULL), qk_issued & 1, &never, nullptr);
-                if (dok_issued >= 0) mbar_wait(bar(DOK_FULL), dok_issued & 1, &never, nullptr);
+                mbar_wait(bar(C::KV_FULL), 0, &never, nullptr);
+                if (ok && SPLIT && lo_later) mbar_wait(bar(C::KVLO_FULL), 0, &never, nullptr);
+                if (qk_issued >= 0) mbar_wait(bar(C::QK_FULL), qk_issued & 1, &never, nullptr);
+                if (dok_issued >= 0) mbar_wait(bar(C::DOK_FULL), dok_issued & 1, &never, nullptr);
             }
         }
     } else if (warp == W_PROD2) {
@@ -424,70 +453,70 @@ __global__ void __maxnreg__(168)
         if (lane == 0) {
             int domn_issued = -1, qmn_issued = -1;
             for (int i = 0; i < nblk; i++) {
-                if (i >= 1 && !mbar_wait(bar(DOMN_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_domn, sb + OFF_DOMN, bar(DOMN_FULL), i);
+                if (i >= 1 && !mbar_wait(bar(C::DOMN_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_domn, sb + C::OFF_DOMN, bar(C::DOMN_FULL), i, true);
                 domn_issued = i;
-                if (i >= 1 && !mbar_wait(bar(QMN_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_qmn, sb + OFF_QMN, bar(QMN_FULL), i);
+                if (i >= 1 && !mbar_wait(bar(C::QMN_EMPTY), (i - 1) & 1, abort, err)) break;
+                load_tile(&tm_qmn, sb + C::OFF_QMN, bar(C::QMN_FULL), i, true);
                 qmn_issued = i;
                 if (*abort) break;
             }
             if (*abort) {
                 volatile int never = 0;
-                if (domn_issued >= 0) mbar_wait(bar(DOMN_FULL), domn_issued & 1, &never, nullptr);
-                if (qmn_issued >= 0) mbar_wait(bar(QMN_FULL), qmn_issued & 1, &never, nullptr);
+                if (domn_issued >= 0) mbar_wait(bar(C::DOMN_FULL), domn_issued & 1, &never, nullptr);
+                if (qmn_issued >= 0) mbar_wait(bar(C::QMN_FULL), qmn_issued & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
         // ---------------------------------------------------- MMA: S^T and dP^T, one warp ----
         {
-            const uint64_t klo = sdesc_sw128(sb + OFF_KLO, 16, 1024), vlo = sdesc_sw128(sb + OFF_VLO, 16, 1024);
-            bool ok = warp_wait(bar(KV_READY), 0, abort, err);
+            const uint64_t klo = sdesc_sw128(sb + C::OFF_KLO, 16, 1024), vlo = sdesc_sw128(sb + C::OFF_VLO, 16, 1024);
+            bool ok = warp_wait(bar(C::KV_READY), 0, abort, err) && warp_wait(bar(C::KVLO_FULL), 0, abort, err);
             tc_fence_after();
             for (int i = 0; ok && i < nblk; i++) {
-                if (!warp_wait(bar(QK_FULL), i & 1, abort, err)) break;
-                if (i >= 1 && !warp_wait(bar(DV_DONE), (i - 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(C::QK_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(C::DV_DONE), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_s<SPLIT, QB>(tmem + C_S, tmem + C_KHI, klo, sdesc_sw128(sb + OFF_QK, 16, 1024));
-                tc_commit_w(bar(S_FULL));
-                tc_commit_w(bar(QK_EMPTY));
-                if (!warp_wait(bar(DOK_FULL), i & 1, abort, err)) break;
-                if (i >= 1 && !warp_wait(bar(DK_DONE), (i - 1) & 1, abort, err)) break;
+                mma_s<SPLIT, QB, DD>(tmem + C::C_S, tmem + C::C_KHI, klo, sdesc_sw128(sb + C::OFF_QK, 16, 1024));
+                tc_commit_w(bar(C::S_FULL));
+                tc_commit_w(bar(C::QK_EMPTY));
+                if (!warp_wait(bar(C::DOK_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(C::DK_DONE), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_s<SPLIT, QB>(tmem + C_DP, tmem + C_VHI, vlo, sdesc_sw128(sb + OFF_DOK, 16, 1024));
-                tc_commit_w(bar(DP_FULL));
-                tc_commit_w(bar(DOK_EMPTY));
+                mma_s<SPLIT, QB, DD>(tmem + C::C_DP, tmem + C::C_VHI, vlo, sdesc_sw128(sb + C::OFF_DOK, 16, 1024));
+                tc_commit_w(bar(C::DP_FULL));
+                tc_commit_w(bar(C::DOK_EMPTY));
             }
             // Every MMA this warp issued completes before TMEM is released.
-            tc_commit_w(bar(DRAIN));
+            tc_commit_w(bar(C::DRAIN));
             volatile int never = 0;
-            warp_wait(bar(DRAIN), 0, &never, nullptr);
+            warp_wait(bar(C::DRAIN), 0, &never, nullptr);
         }
     } else if (warp == W_GMMA) {
         // ------------------------------------------------ MMA: dV_blk and dK_blk, one warp ----
         {
             bool ok = true;
             for (int i = 0; ok && i < nblk; i++) {
-                if (!warp_wait(bar(P_READY), i & 1, abort, err)) break;
-                if (!warp_wait(bar(DOMN_FULL), i & 1, abort, err)) break;
-                if (i >= 1 && !warp_wait(bar(DV_FREE), (i - 1) & 1, abort, err)) break;
+                if (!warp_wait(bar(C::P_READY), i & 1, abort, err)) break;
+                if (!warp_wait(bar(C::DOMN_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(C::DV_FREE), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_g<SPLIT, QB>(tmem + C_DV, tmem + C_S, tmem + C_PLO,
-                                 sdesc_mn_sw128_32b(sb + OFF_DOMN, QB_CHUNK, 512), false);
-                tc_commit_w(bar(DV_DONE));
-                tc_commit_w(bar(DOMN_EMPTY));
-                if (!warp_wait(bar(DS_READY), i & 1, abort, err)) break;
-                if (!warp_wait(bar(QMN_FULL), i & 1, abort, err)) break;
-                if (i >= 1 && !warp_wait(bar(DK_FREE), (i - 1) & 1, abort, err)) break;
+                mma_g<SPLIT, QB>(tmem + C::C_DV, tmem + C::C_S, tmem + C::C_PLO,
+                                 sdesc_mn_sw128_32b(sb + C::OFF_DOMN, C::TM_CHUNK, 512), false);
+                tc_commit_w(bar(C::DV_DONE));
+                tc_commit_w(bar(C::DOMN_EMPTY));
+                if (!warp_wait(bar(C::DS_READY), i & 1, abort, err)) break;
+                if (!warp_wait(bar(C::QMN_FULL), i & 1, abort, err)) break;
+                if (i >= 1 && !warp_wait(bar(C::DK_FREE), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_g<SPLIT, QB>(tmem + C_DK, tmem + C_DP, tmem + C_DSLO,
-                                 sdesc_mn_sw128_32b(sb + OFF_QMN, QB_CHUNK, 512), false);
-                tc_commit_w(bar(DK_DONE));
-                tc_commit_w(bar(QMN_EMPTY));
+                mma_g<SPLIT, QB>(tmem + C::C_DK, tmem + C::C_DP, tmem + C::C_DSLO,
+                                 sdesc_mn_sw128_32b(sb + C::OFF_QMN, C::TM_CHUNK, 512), false);
+                tc_commit_w(bar(C::DK_DONE));
+                tc_commit_w(bar(C::QMN_EMPTY));
             }
-            tc_commit_w(bar(DRAIN_G));
+            tc_commit_w(bar(C::DRAIN_G));
             volatile int never = 0;
-            warp_wait(bar(DRAIN_G), 0, &never, nullptr);
+            warp_wait(bar(C::DRAIN_G), 0, &never, nullptr);
         }
     } else if (warp < W_PROD) {
         // ------------------------- P^T and dS^T, then the fp32 dV / dK folds, every block ----
@@ -496,42 +525,42 @@ __global__ void __maxnreg__(168)
         const int64_t key = k0 + row;
         const bool key_ok = key < p.S;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        const int cb = half * 32;  // this thread's query columns of a block
-        float acc[D];
+        const int cb = half * CPT;  // this thread's query columns of a block
+        float acc[64];              // this CTA's 64 columns of dV (half 0) or dK (half 1)
 #pragma unroll
-        for (int x = 0; x < D; x++) acc[x] = 0.0f;
-        bool ok = warp_wait(bar(KV_FULL), 0, abort, err);
+        for (int x = 0; x < 64; x++) acc[x] = 0.0f;
+        bool ok = warp_wait(bar(C::KV_FULL), 0, abort, err);
         if (ok) {  // K (half 0) or V (half 1) hi rows into TMEM
-            row_to_tmem(sg + (half ? OFF_DOK : OFF_QK), row, tl, half ? C_VHI : C_KHI);
+            row_to_tmem<DD>(sg + (half ? C::OFF_VHI_STAGE : C::OFF_KHI_STAGE), row, tl, half ? C::C_VHI : C::C_KHI);
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(bar(KV_READY));
+            mbar_arrive(bar(C::KV_READY));
         }
+        // Adds block i's accumulator (dV for half 0, dK for half 1) into registers and frees it.
+        // (Deferring it until after the next block's P^T was measured slower: the fold's TMEM
+        // loads then sit on the path to dS^T.)
+        auto fold = [&](int i) -> bool {
+            if (!warp_wait(bar(half ? C::DK_DONE : C::DV_DONE), i & 1, abort, err)) return false;
+            tc_fence_after();
+            const uint32_t col = half ? C::C_DK : C::C_DV;
+#pragma unroll
+            for (int c = 0; c < 4; c++) fold16(tl + col + 16 * c, acc + 16 * c);
+            tc_fence_before();
+            mbar_arrive(bar(half ? C::DK_FREE : C::DV_FREE));
+            return true;
+        };
         // Lane c holds the lse (base 2) and the delta of this half's query column c of block i.
         auto colvals = [&](int i, float &lse2, float &del) {
             int64_t h, q0;
             blk_coords(i, h, q0);
-            const int64_t q = q0 + cb + lane;
+            const int64_t q = q0 + cb + (lane % CPT);
             lse2 = del = 0.0f;
             if (q < p.L) {
                 const int64_t idx = (b * p.H + h) * p.L + q;
                 lse2 = a.lse2[idx];
                 del = a.g.delta[idx];
             }
-        };
-        // Adds block i's accumulator (dV for half 0, dK for half 1) into registers and frees it.
-        // (Deferring it until after the next block's P^T was measured slower: the fold's TMEM
-        // loads then sit on the path to dS^T.)
-        auto fold = [&](int i) -> bool {
-            if (!warp_wait(bar(half ? DK_DONE : DV_DONE), i & 1, abort, err)) return false;
-            tc_fence_after();
-            const uint32_t col = half ? C_DK : C_DV;
-#pragma unroll
-            for (int c = 0; c < D / 16; c++) fold16(tl + col + 16 * c, acc + 16 * c);
-            tc_fence_before();
-            mbar_arrive(bar(half ? DK_FREE : DV_FREE));
-            return true;
         };
         float cur_l = 0.0f, cur_d = 0.0f;
         if (ok && nblk > 0) colvals(0, cur_l, cur_d);
@@ -546,32 +575,33 @@ __global__ void __maxnreg__(168)
             uint32_t vbits = 0xFFFFFFFFu;
             if (edge) vbits = key_ok ? col_bits32(p.causal ? key - base : 0, p.L - base) : 0u;
             // The user mask down this key's column, loaded before the wait for S.
-            float mk[MASKED ? 32 : 1];
-            if constexpr (MASKED) mask_run<32>(p, b, h, base, key, p.ms[2], vbits, mk);
+            float mk[MASKED ? CPT : 1];
+            if constexpr (MASKED) mask_run<CPT>(p, b, h, base, key, p.ms[2], vbits, mk);
             // Dropout: the keep bits of (query base + c, this key). The weights that meet dO are
             // P * Z; dS = P (Z dP - delta), Z = keep_scale where kept, 0 where dropped.
             uint32_t zb = 0;
-            if constexpr (DROP) zb = key_ok ? keep_col<32>(p, b, h, base, key) : 0u;
-            if (!warp_wait(bar(S_FULL), i & 1, abort, err)) {
+            if constexpr (DROP) zb = key_ok ? keep_col<CPT>(p, b, h, base, key) : 0u;
+            if (!warp_wait(bar(C::S_FULL), i & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float pv[32];  // P (undropped) of this key and the 32 query columns
-            {
-                uint32_t sr[32];
-                tmem_ld32(tl + C_S + cb, sr);
+            float pv[CPT];  // P (undropped) of this key and the query columns
+#pragma unroll
+            for (int r0 = 0; r0 < CPT; r0 += 16) {
+                uint32_t sr[16];
+                tmem_ld16(tl + C::C_S + cb + r0, sr);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
+                for (int c = 0; c < 16; c++) {
                     float x = __uint_as_float(sr[c]) * a.scale_log2;
-                    if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
-                    const float lse2 = __shfl_sync(FULL, cur_l, c);
-                    pv[c] = ((vbits >> c) & 1u) ? ex2_approx(x - lse2) : 0.0f;
+                    if (MASKED) x += mk[MASKED ? r0 + c : 0] * LOG2E;
+                    const float lse2 = __shfl_sync(FULL, cur_l, r0 + c);
+                    pv[r0 + c] = ((vbits >> (r0 + c)) & 1u) ? ex2_approx(x - lse2) : 0.0f;
                 }
             }
 #pragma unroll
-            for (int r0 = 0; r0 < 32; r0 += 16) {
+            for (int r0 = 0; r0 < CPT; r0 += 16) {
                 uint32_t xh[16], xl[16];
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
@@ -580,21 +610,21 @@ __global__ void __maxnreg__(168)
                     xh[c] = tf32_rna(pw);
                     if (SPLIT) xl[c] = tf32_lo(pw, xh[c]);
                 }
-                tmem_st16(tl + C_S + cb + r0, xh);
-                if (SPLIT) tmem_st16(tl + C_PLO + cb + r0, xl);
+                tmem_st16(tl + C::C_S + cb + r0, xh);
+                if (SPLIT) tmem_st16(tl + C::C_PLO + cb + r0, xl);
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(P_READY));
-            if (!warp_wait(bar(DP_FULL), i & 1, abort, err)) {
+            mbar_arrive(bar(C::P_READY));
+            if (!warp_wait(bar(C::DP_FULL), i & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
 #pragma unroll
-            for (int r0 = 0; r0 < 32; r0 += 16) {
+            for (int r0 = 0; r0 < CPT; r0 += 16) {
                 uint32_t dr[16], xh[16], xl[16];
-                tmem_ld16(tl + C_DP + cb + r0, dr);
+                tmem_ld16(tl + C::C_DP + cb + r0, dr);
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
@@ -605,12 +635,12 @@ __global__ void __maxnreg__(168)
                     xh[c] = tf32_rna(ds);
                     if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
                 }
-                tmem_st16(tl + C_DP + cb + r0, xh);
-                if (SPLIT) tmem_st16(tl + C_DSLO + cb + r0, xl);
+                tmem_st16(tl + C::C_DP + cb + r0, xh);
+                if (SPLIT) tmem_st16(tl + C::C_DSLO + cb + r0, xl);
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(DS_READY));
+            mbar_arrive(bar(C::DS_READY));
             cur_l = nxt_l;
             cur_d = nxt_d;
             if (!fold(i)) {
@@ -621,11 +651,11 @@ __global__ void __maxnreg__(168)
         const bool aborted = __any_sync(FULL, *abort != 0);
         if (ok && !aborted && key_ok) {
             if (half) {
-                float *dkr = a.g.dk + b * a.g.dks[0] + hk * a.g.dks[1] + key * a.g.dks[2];
-                store_row<D>(dkr, a.g.dks[3], acc, p.scale);
+                float *dkr = a.g.dk + b * a.g.dks[0] + hk * a.g.dks[1] + key * a.g.dks[2] + (int64_t)(64 * dh) * a.g.dks[3];
+                store_row<64>(dkr, a.g.dks[3], acc, p.scale);
             } else {
-                float *dvr = a.g.dv + b * a.g.dvs[0] + hk * a.g.dvs[1] + key * a.g.dvs[2];
-                store_row<D>(dvr, a.g.dvs[3], acc, 1.0f);
+                float *dvr = a.g.dv + b * a.g.dvs[0] + hk * a.g.dvs[1] + key * a.g.dvs[2] + (int64_t)(64 * dh) * a.g.dvs[3];
+                store_row<64>(dvr, a.g.dvs[3], acc, 1.0f);
             }
         }
     }
@@ -634,54 +664,68 @@ __global__ void __maxnreg__(168)
     __syncthreads();
     if (warp == W_MMA) {
         tc_fence_after();
-        tmem_dealloc(tmem, kv::TCOLS);
+        tmem_dealloc(tmem, C::TCOLS);
     }
 }
 
 // ========================================================================= dQ ========
-namespace qq {
-// 64-key blocks: the S / dP products run at N = 64, where a tensor-core MMA does twice the work
-// of an N = 32 one for a little more time.
-constexpr int NB = 64;
-constexpr uint32_t NB_BYTES = NB * D * 4;  // one streamed fp32 tile (16 KB)
-constexpr uint32_t NB_CHUNK = NB * 128;    // 8 KB per 32-column chunk
-// Three rings of two stages, each stage a tile's hi and lo copies (32 KB), each freed by its
-// own reader: K (K-major) by the S MMAs, V (K-major) by the dP MMAs, K (MN-major) by the dQ
-// MMAs. Separate rings give every load about two blocks of lead time.
-constexpr int NST = 2;
-constexpr uint32_t STAGE = 2 * NB_BYTES;
-constexpr uint32_t OFF_KK = 0, OFF_VK = NST * STAGE, OFF_KMN = 2 * NST * STAGE;
-// Until they are in TMEM, Q hi / dO hi wait in the K ring and Q lo / dO lo in the V ring.
-constexpr uint32_t OFF_QHI = OFF_KK, OFF_DOHI = OFF_KK + RES_BYTES, OFF_QLO = OFF_VK, OFF_DOLO = OFF_VK + RES_BYTES;
-constexpr uint32_t OFF_BAR = 3 * NST * STAGE;
-// Per block j: S (S_FULL) read out by the softmax warps (S_READ: S_{j+1} may overwrite it);
-// dP (DP_FULL) turned into dS hi / lo (DS_READY); dQ_blk = dS K (DQ_DONE: dS read, dP_{j+1}
-// may overwrite it) folded into registers (DQ_FREE: the accumulator may restart).
-enum { QD_FULL, QD_READY, KK_FULL, KK_EMPTY = KK_FULL + NST, VK_FULL = KK_EMPTY + NST, VK_EMPTY = VK_FULL + NST,
-       SG_FULL = VK_EMPTY + NST, SG_EMPTY = SG_FULL + NST, S_FULL = SG_EMPTY + NST, S_READ, DP_FULL, DS_READY,
-       DQ_DONE, DQ_FREE, DRAIN, DRAIN_G, NBAR };
-constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
-// TMEM: Q hi | Q lo | dO hi | dO lo | S | dP / dS hi | dS lo | dQ_blk
-constexpr uint32_t C_QHI = 0, C_QLO = 64, C_DOHI = 128, C_DOLO = 192, C_S = 256, C_DP = 320, C_DSLO = 384,
-                   C_DQB = 448, TCOLS = 512;
-static_assert(2 * RES_BYTES <= NST * STAGE, "Q / dO tiles are staged in the K and V rings");
-static_assert(SMEM <= 232448, "smem");
-}  // namespace qq
+// Head dim DD = 64: a CTA computes all of dQ for its query rows, with Q and dO (hi and lo) in
+// TMEM. DD = 128: two CTAs per query tile, each computing one 64-column half of dQ (both
+// recompute S and dP over the whole head dim); Q hi and dO hi fill 256 TMEM columns, so their
+// lo copies stay in shared memory and those passes read A from there.
+template <int DD>
+struct QqCfg {
+    static constexpr int NH = DD / 64;             // dQ column halves (CTAs per query tile)
+    static constexpr int NB = DD == 64 ? 64 : 32;  // keys per streamed block (S / dP's N)
+    static constexpr int CPT = NB / 2;             // key columns per softmax thread
+    static constexpr bool LO_TMEM = DD == 64;      // Q lo / dO lo in TMEM, else in shared memory
+    static constexpr uint32_t RESB = TILE * DD * 4;                        // resident Q or dO tile
+    static constexpr uint32_t TK_BYTES = NB * DD * 4, TK_CHUNK = NB * 128;  // K-major K / V tile
+    static constexpr uint32_t TM_BYTES = NB * 64 * 4, TM_CHUNK = NB * 128;  // MN-major K half tile
+    // Rings (a stage holds a tile's hi and lo copies), each freed by its own reader: K (K-major)
+    // by the S MMAs, V (K-major) by the dP MMAs, K (MN-major) by the dQ MMAs.
+    static constexpr int NST_K = DD == 64 ? 2 : 1, NST_G = 2;
+    static constexpr uint32_t KSTAGE = 2 * TK_BYTES, GSTAGE = 2 * TM_BYTES;
+    static constexpr uint32_t OFF_QLO = 0, OFF_DOLO = RESB, OFF_KK = LO_TMEM ? 0 : 2 * RESB,
+                              OFF_VK = OFF_KK + NST_K * KSTAGE, OFF_KMN = OFF_VK + NST_K * KSTAGE,
+                              OFF_BAR = OFF_KMN + NST_G * GSTAGE;
+    // Where Q / dO wait until the softmax warps move them into TMEM: DD = 64, hi in the K ring
+    // and lo in the V ring; DD = 128, hi in the lo areas (the lo copies are loaded after).
+    static constexpr uint32_t OFF_QHI_STAGE = LO_TMEM ? OFF_KK : OFF_QLO,
+                              OFF_DOHI_STAGE = LO_TMEM ? OFF_KK + RESB : OFF_DOLO,
+                              OFF_QLO_STAGE = OFF_VK, OFF_DOLO_STAGE = OFF_VK + RESB;
+    // Per block j: S (S_FULL) read out by the softmax warps (S_READ: S_{j+1} may overwrite it);
+    // dP (DP_FULL) turned into dS hi / lo (DS_READY); dQ_blk = dS K (DQ_DONE: dS read, dP_{j+1}
+    // may overwrite it) folded into registers (DQ_FREE: the accumulator may restart).
+    // QDLO_FULL: the lo copies of Q / dO in shared memory (DD = 128).
+    enum { QD_FULL, QD_READY, QDLO_FULL, KK_FULL, KK_EMPTY = KK_FULL + NST_K, VK_FULL = KK_EMPTY + NST_K,
+           VK_EMPTY = VK_FULL + NST_K, SG_FULL = VK_EMPTY + NST_K, SG_EMPTY = SG_FULL + NST_G,
+           S_FULL = SG_EMPTY + NST_G, S_READ, DP_FULL, DS_READY, DQ_DONE, DQ_FREE, DRAIN, DRAIN_G, NBAR };
+    static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
+    static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
+    // TMEM: Q hi | [Q lo] | dO hi | [dO lo] | S | dP / dS hi | dS lo | dQ_blk
+    static constexpr uint32_t C_QHI = 0, C_QLO = DD, C_DOHI = LO_TMEM ? 2 * DD : DD, C_DOLO = C_DOHI + DD,
+                              C_S = LO_TMEM ? 4 * DD : 2 * DD, C_DP = C_S + NB, C_DSLO = C_S + 2 * NB,
+                              C_DQB = C_S + 3 * NB, TCOLS = 512;
+    static_assert(C_DQB + 64 <= TCOLS, "tensor memory budget");
+    static_assert(!LO_TMEM || 2 * RESB <= NST_K * KSTAGE, "Q / dO tiles are staged in the K and V rings");
+    static_assert(SMEM <= 232448, "smem");
+};
 
-// tm_q / tm_do: (64, L, H, S2*B), box 128 rows; tm_kk / tm_kmn / tm_vk: (64, S, Hkv, S2*B),
-// box 64 rows.
+// tm_q / tm_do: (DD, L, H, S2*B), box 128 rows; tm_kk / tm_kmn / tm_vk: (DD, S, Hkv, S2*B),
+// box NB rows (tm_kmn: this CTA's 64-column half).
 //
 // One MMA warp issues S_0, dP_0, then per block j: S_{j+1} (once the softmax warps have read
 // S_j) and dP_{j+1} (once dQ_j has read dS_j); a second issues dQ_j once dS_j is in TMEM. The
 // tensor core thus runs ... dQ_j, dP_{j+1}, S_{j+2}, dQ_{j+1} ... while the softmax warps
 // compute dS_{j+1} under S_{j+2} and P_{j+2} under dQ_{j+1}.
-template <bool SPLIT, bool MASKED, bool DROP>
+template <int DD, bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(168)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_kk, const __grid_constant__ CUtensorMap tm_kmn,
                           const __grid_constant__ CUtensorMap tm_vk, const TcBwdArgs a) {
-    using namespace qq;
+    using C = QqCfg<DD>;
+    constexpr int NB = C::NB, CPT = C::CPT, NST_K = C::NST_K, NST_G = C::NST_G;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -690,43 +734,48 @@ __global__ void __maxnreg__(168)
     const AttnProblem &p = a.p;
     // Query tiles in descending order: under causal masking the last tile sees the most keys.
     const int64_t ntiles = (p.L + TILE - 1) / TILE;
-    int64_t qt, bh;
-    grouped_tile(blockIdx.x, ntiles, p.B * p.H, qt, bh);
+    int64_t qt, bhd;
+    grouped_tile(blockIdx.x, ntiles, p.B * p.H * C::NH, qt, bhd);
     qt = ntiles - 1 - qt;
+    const int dh = (int)(bhd % C::NH);  // dQ column half
+    const int64_t bh = bhd / C::NH;
     const int64_t h = bh % p.H, b = bh / p.H, hk = h / p.group;
     const int lo_b = (int)(p.B + b);
     const int64_t q0 = qt * TILE;
     const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
     const int nblk = (int)((kv_end + NB - 1) / NB);
-    auto bar = [&](int i) { return sb + OFF_BAR + 8u * (uint32_t)i; };
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + OFF_MISC);
-    volatile int *abort = reinterpret_cast<volatile int *>(sg + OFF_MISC + 4);
+    auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
+    volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
     int *err = a.err;
 
     if (threadIdx.x == 0) {
-        mbar_init(bar(QD_FULL), 1);
-        mbar_init(bar(QD_READY), 256);
-        for (int s = 0; s < NST; s++) {
-            mbar_init(bar(KK_FULL + s), 1);
-            mbar_init(bar(KK_EMPTY + s), 1);
-            mbar_init(bar(VK_FULL + s), 1);
-            mbar_init(bar(VK_EMPTY + s), 1);
-            mbar_init(bar(SG_FULL + s), 1);
-            mbar_init(bar(SG_EMPTY + s), 1);
+        mbar_init(bar(C::QD_FULL), 1);
+        mbar_init(bar(C::QD_READY), 256);
+        mbar_init(bar(C::QDLO_FULL), 1);
+        for (int s = 0; s < NST_K; s++) {
+            mbar_init(bar(C::KK_FULL + s), 1);
+            mbar_init(bar(C::KK_EMPTY + s), 1);
+            mbar_init(bar(C::VK_FULL + s), 1);
+            mbar_init(bar(C::VK_EMPTY + s), 1);
         }
-        mbar_init(bar(S_FULL), 1);
-        mbar_init(bar(S_READ), 256);
-        mbar_init(bar(DP_FULL), 1);
-        mbar_init(bar(DS_READY), 256);
-        mbar_init(bar(DQ_DONE), 1);
-        mbar_init(bar(DQ_FREE), 256);
-        mbar_init(bar(DRAIN), 1);
-        mbar_init(bar(DRAIN_G), 1);
+        for (int s = 0; s < NST_G; s++) {
+            mbar_init(bar(C::SG_FULL + s), 1);
+            mbar_init(bar(C::SG_EMPTY + s), 1);
+        }
+        mbar_init(bar(C::S_FULL), 1);
+        mbar_init(bar(C::S_READ), 256);
+        mbar_init(bar(C::DP_FULL), 1);
+        mbar_init(bar(C::DS_READY), 256);
+        mbar_init(bar(C::DQ_DONE), 1);
+        mbar_init(bar(C::DQ_FREE), 256);
+        mbar_init(bar(C::DRAIN), 1);
+        mbar_init(bar(C::DRAIN_G), 1);
         *abort = 0;
         fence_mbar_init();
     }
     if (warp == W_MMA) {
-        tmem_alloc(smem_addr(tmem_slot), TCOLS);
+        tmem_alloc(smem_addr(tmem_slot), C::TCOLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -735,68 +784,80 @@ __global__ void __maxnreg__(168)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == W_PROD) {
-        // ----------------------------------------- producer: Q / dO, then the K-major ring ----
+        // ------------------------------ producer: Q / dO (hi, lo), then the K and V rings ----
         if (lane == 0) {
-            int issued = -1;
-            mbar_expect_tx(bar(QD_FULL), (SPLIT ? 4 : 2) * RES_BYTES);
-            for (int c = 0; c < CHUNKS; c++) {
-                tma_load_4d(&tm_q, sb + OFF_QHI + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
-                tma_load_4d(&tm_do, sb + OFF_DOHI + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
-                if (SPLIT) {
-                    tma_load_4d(&tm_q, sb + OFF_QLO + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
-                    tma_load_4d(&tm_do, sb + OFF_DOLO + c * RES_CHUNK, bar(QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
+            int k_issued = -1, v_issued = -1;
+            const bool lo_now = SPLIT && C::LO_TMEM;
+            mbar_expect_tx(bar(C::QD_FULL), (lo_now ? 4 : 2) * C::RESB);
+            for (int c = 0; c < DD / 32; c++) {
+                tma_load_4d(&tm_q, sb + C::OFF_QHI_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                tma_load_4d(&tm_do, sb + C::OFF_DOHI_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                if (lo_now) {
+                    tma_load_4d(&tm_q, sb + C::OFF_QLO_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                    tma_load_4d(&tm_do, sb + C::OFF_DOLO_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
                 }
             }
-            bool ok = mbar_wait(bar(QD_READY), 0, abort, err);
-            int k_issued = -1, v_issued = -1;
+            if (!(SPLIT && !C::LO_TMEM)) mbar_arrive(bar(C::QDLO_FULL));
+            bool ok = mbar_wait(bar(C::QD_READY), 0, abort, err);
+            const bool lo_later = ok && SPLIT && !C::LO_TMEM;
+            if (lo_later) {
+                mbar_expect_tx(bar(C::QDLO_FULL), 2 * C::RESB);
+                for (int c = 0; c < DD / 32; c++) {
+                    tma_load_4d(&tm_q, sb + C::OFF_QLO + c * RES_CHUNK, bar(C::QDLO_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                    tma_load_4d(&tm_do, sb + C::OFF_DOLO + c * RES_CHUNK, bar(C::QDLO_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                }
+            }
             for (int j = 0; ok && j < nblk; j++) {
-                const int st = j % NST;
-                if (j >= NST && !mbar_wait(bar(KK_EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
-                mbar_expect_tx(bar(KK_FULL + st), (SPLIT ? 2 : 1) * NB_BYTES);
-                for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = OFF_KK + st * STAGE + c * NB_CHUNK;
-                    tma_load_4d(&tm_kk, sb + o, bar(KK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_kk, sb + o + NB_BYTES, bar(KK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
+                const int st = j % NST_K;
+                if (j >= NST_K && !mbar_wait(bar(C::KK_EMPTY + st), ((j / NST_K) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(C::KK_FULL + st), (SPLIT ? 2 : 1) * C::TK_BYTES);
+                for (int c = 0; c < DD / 32; c++) {
+                    const uint32_t o = C::OFF_KK + st * C::KSTAGE + c * C::TK_CHUNK;
+                    tma_load_4d(&tm_kk, sb + o, bar(C::KK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_kk, sb + o + C::TK_BYTES, bar(C::KK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
                 }
                 k_issued = j;
-                if (j >= NST && !mbar_wait(bar(VK_EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
-                mbar_expect_tx(bar(VK_FULL + st), (SPLIT ? 2 : 1) * NB_BYTES);
-                for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = OFF_VK + st * STAGE + c * NB_CHUNK;
-                    tma_load_4d(&tm_vk, sb + o, bar(VK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_vk, sb + o + NB_BYTES, bar(VK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
+                if (j >= NST_K && !mbar_wait(bar(C::VK_EMPTY + st), ((j / NST_K) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(C::VK_FULL + st), (SPLIT ? 2 : 1) * C::TK_BYTES);
+                for (int c = 0; c < DD / 32; c++) {
+                    const uint32_t o = C::OFF_VK + st * C::KSTAGE + c * C::TK_CHUNK;
+                    tma_load_4d(&tm_vk, sb + o, bar(C::VK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_vk, sb + o + C::TK_BYTES, bar(C::VK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
                 }
                 v_issued = j;
             }
             if (*abort) {
                 volatile int never = 0;
-                mbar_wait(bar(QD_FULL), 0, &never, nullptr);
-                for (int j = max(0, k_issued - NST + 1); j <= k_issued; j++)
-                    mbar_wait(bar(KK_FULL + j % NST), (j / NST) & 1, &never, nullptr);
-                for (int j = max(0, v_issued - NST + 1); j <= v_issued; j++)
-                    mbar_wait(bar(VK_FULL + j % NST), (j / NST) & 1, &never, nullptr);
+                mbar_wait(bar(C::QD_FULL), 0, &never, nullptr);
+                if (lo_later) mbar_wait(bar(C::QDLO_FULL), 0, &never, nullptr);
+                for (int j = max(0, k_issued - NST_K + 1); j <= k_issued; j++)
+                    mbar_wait(bar(C::KK_FULL + j % NST_K), (j / NST_K) & 1, &never, nullptr);
+                for (int j = max(0, v_issued - NST_K + 1); j <= v_issued; j++)
+                    mbar_wait(bar(C::VK_FULL + j % NST_K), (j / NST_K) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_PROD2) {
         // ------------------------------------------------ producer: the MN-major ring ----
         if (lane == 0) {
             int issued = -1;
+            // DD = 64 stages Q / dO in the K and V rings only, so this ring may start at once.
             for (int j = 0; j < nblk; j++) {
-                const int st = j % NST;
-                if (j >= NST && !mbar_wait(bar(SG_EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
-                mbar_expect_tx(bar(SG_FULL + st), (SPLIT ? 2 : 1) * NB_BYTES);
-                for (int c = 0; c < CHUNKS; c++) {
-                    const uint32_t o = OFF_KMN + st * STAGE + c * NB_CHUNK;
-                    tma_load_4d(&tm_kmn, sb + o, bar(SG_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_kmn, sb + o + NB_BYTES, bar(SG_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
+                const int st = j % NST_G;
+                if (j >= NST_G && !mbar_wait(bar(C::SG_EMPTY + st), ((j / NST_G) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(C::SG_FULL + st), (SPLIT ? 2 : 1) * C::TM_BYTES);
+                for (int c = 0; c < 2; c++) {
+                    const uint32_t o = C::OFF_KMN + st * C::GSTAGE + c * C::TM_CHUNK;
+                    const int col = 64 * dh + 32 * c;
+                    tma_load_4d(&tm_kmn, sb + o, bar(C::SG_FULL + st), col, j * NB, (int)hk, (int)b);
+                    if (SPLIT) tma_load_4d(&tm_kmn, sb + o + C::TM_BYTES, bar(C::SG_FULL + st), col, j * NB, (int)hk, lo_b);
                 }
                 issued = j;
                 if (*abort) break;
             }
             if (*abort) {
                 volatile int never = 0;
-                for (int j = max(0, issued - NST + 1); j <= issued; j++)
-                    mbar_wait(bar(SG_FULL + j % NST), (j / NST) & 1, &never, nullptr);
+                for (int j = max(0, issued - NST_G + 1); j <= issued; j++)
+                    mbar_wait(bar(C::SG_FULL + j % NST_G), (j / NST_G) & 1, &never, nullptr);
             }
         }
     } else if (warp == W_MMA) {
@@ -805,22 +866,29 @@ __global__ void __maxnreg__(168)
         // wait of the issuing warp idles the tensor core: S / dP and dQ have a warp each, and
         // one warp's waits overlap the other's MMAs.
         {
+            const uint64_t qlo = sdesc_sw128(sb + C::OFF_QLO, 16, 1024), dolo = sdesc_sw128(sb + C::OFF_DOLO, 16, 1024);
             auto s_mma = [&](int j) {
-                const uint32_t st = OFF_KK + (j % NST) * STAGE;
-                mma_s_t<SPLIT, NB>(tmem + C_S, tmem + C_QHI, tmem + C_QLO, sdesc_sw128(sb + st, 16, 1024));
-                tc_commit_w(bar(S_FULL));
-                tc_commit_w(bar(KK_EMPTY + j % NST));
+                const uint32_t st = C::OFF_KK + (j % NST_K) * C::KSTAGE;
+                if constexpr (C::LO_TMEM)
+                    mma_s_t<SPLIT, NB, DD>(tmem + C::C_S, tmem + C::C_QHI, tmem + C::C_QLO, sdesc_sw128(sb + st, 16, 1024));
+                else
+                    mma_s<SPLIT, NB, DD>(tmem + C::C_S, tmem + C::C_QHI, qlo, sdesc_sw128(sb + st, 16, 1024));
+                tc_commit_w(bar(C::S_FULL));
+                tc_commit_w(bar(C::KK_EMPTY + j % NST_K));
             };
             auto dp_mma = [&](int j) {
-                const uint32_t st = OFF_VK + (j % NST) * STAGE;
-                mma_s_t<SPLIT, NB>(tmem + C_DP, tmem + C_DOHI, tmem + C_DOLO, sdesc_sw128(sb + st, 16, 1024));
-                tc_commit_w(bar(DP_FULL));
-                tc_commit_w(bar(VK_EMPTY + j % NST));
+                const uint32_t st = C::OFF_VK + (j % NST_K) * C::KSTAGE;
+                if constexpr (C::LO_TMEM)
+                    mma_s_t<SPLIT, NB, DD>(tmem + C::C_DP, tmem + C::C_DOHI, tmem + C::C_DOLO, sdesc_sw128(sb + st, 16, 1024));
+                else
+                    mma_s<SPLIT, NB, DD>(tmem + C::C_DP, tmem + C::C_DOHI, dolo, sdesc_sw128(sb + st, 16, 1024));
+                tc_commit_w(bar(C::DP_FULL));
+                tc_commit_w(bar(C::VK_EMPTY + j % NST_K));
             };
-            bool ok = warp_wait(bar(QD_READY), 0, abort, err);
+            bool ok = warp_wait(bar(C::QD_READY), 0, abort, err) && warp_wait(bar(C::QDLO_FULL), 0, abort, err);
             tc_fence_after();
             if (ok && nblk > 0) {
-                ok = warp_wait(bar(KK_FULL), 0, abort, err) && warp_wait(bar(VK_FULL), 0, abort, err);
+                ok = warp_wait(bar(C::KK_FULL), 0, abort, err) && warp_wait(bar(C::VK_FULL), 0, abort, err);
                 tc_fence_after();
                 if (ok) {
                     s_mma(0);
@@ -830,39 +898,39 @@ __global__ void __maxnreg__(168)
             for (int j = 0; ok && j + 1 < nblk; j++) {
                 const int nx = j + 1;
                 // S of block j+1 overwrites S_j once the softmax warps hold it in registers.
-                if (!warp_wait(bar(S_READ), j & 1, abort, err)) break;
-                if (!warp_wait(bar(KK_FULL + nx % NST), (nx / NST) & 1, abort, err)) break;
+                if (!warp_wait(bar(C::S_READ), j & 1, abort, err)) break;
+                if (!warp_wait(bar(C::KK_FULL + nx % NST_K), (nx / NST_K) & 1, abort, err)) break;
                 tc_fence_after();
                 s_mma(nx);
                 // dP of block j+1 overwrites dS_j once dQ_j has read it.
-                if (!warp_wait(bar(DQ_DONE), j & 1, abort, err)) break;
-                if (!warp_wait(bar(VK_FULL + nx % NST), (nx / NST) & 1, abort, err)) break;
+                if (!warp_wait(bar(C::DQ_DONE), j & 1, abort, err)) break;
+                if (!warp_wait(bar(C::VK_FULL + nx % NST_K), (nx / NST_K) & 1, abort, err)) break;
                 tc_fence_after();
                 dp_mma(nx);
             }
             // Every MMA this warp issued completes before TMEM is released.
-            tc_commit_w(bar(DRAIN));
+            tc_commit_w(bar(C::DRAIN));
             volatile int never = 0;
-            warp_wait(bar(DRAIN), 0, &never, nullptr);
+            warp_wait(bar(C::DRAIN), 0, &never, nullptr);
         }
     } else if (warp == W_GMMA) {
         // ------------------------------------------------------------- MMA: dQ_blk = dS K ----
         {
             bool ok = true;
             for (int j = 0; ok && j < nblk; j++) {
-                const int sgi = j % NST;
-                if (!warp_wait(bar(DS_READY), j & 1, abort, err)) break;
-                if (!warp_wait(bar(SG_FULL + sgi), (j / NST) & 1, abort, err)) break;
-                if (j >= 1 && !warp_wait(bar(DQ_FREE), (j - 1) & 1, abort, err)) break;
+                const int sgi = j % NST_G;
+                if (!warp_wait(bar(C::DS_READY), j & 1, abort, err)) break;
+                if (!warp_wait(bar(C::SG_FULL + sgi), (j / NST_G) & 1, abort, err)) break;
+                if (j >= 1 && !warp_wait(bar(C::DQ_FREE), (j - 1) & 1, abort, err)) break;
                 tc_fence_after();
-                mma_g<SPLIT, NB>(tmem + C_DQB, tmem + C_DP, tmem + C_DSLO,
-                                 sdesc_mn_sw128_32b(sb + OFF_KMN + sgi * STAGE, NB_CHUNK, 512), false);
-                tc_commit_w(bar(DQ_DONE));
-                tc_commit_w(bar(SG_EMPTY + sgi));
+                mma_g<SPLIT, NB>(tmem + C::C_DQB, tmem + C::C_DP, tmem + C::C_DSLO,
+                                 sdesc_mn_sw128_32b(sb + C::OFF_KMN + sgi * C::GSTAGE, C::TM_CHUNK, 512), false);
+                tc_commit_w(bar(C::DQ_DONE));
+                tc_commit_w(bar(C::SG_EMPTY + sgi));
             }
-            tc_commit_w(bar(DRAIN_G));
+            tc_commit_w(bar(C::DRAIN_G));
             volatile int never = 0;
-            warp_wait(bar(DRAIN_G), 0, &never, nullptr);
+            warp_wait(bar(C::DRAIN_G), 0, &never, nullptr);
         }
     } else if (warp < W_PROD) {
         // ----------------------------------------------------- dS, then the fp32 dQ fold --
@@ -871,23 +939,24 @@ __global__ void __maxnreg__(168)
         const int64_t q = q0 + row;
         const bool row_ok = q < p.L;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        const int cb = half * 32;  // this thread's key columns of a block
-        float acc[D / 2];          // dQ columns [32 half, 32 half + 32)
+        const int cb = half * CPT;  // this thread's key columns of a block
+        float acc[32];              // dQ columns [64 dh + 32 half, +32)
 #pragma unroll
-        for (int x = 0; x < D / 2; x++) acc[x] = 0.0f;
-        bool ok = warp_wait(bar(QD_FULL), 0, abort, err);
-        if (ok) {  // Q (half 0) or dO (half 1), hi and lo rows, into TMEM
-            row_to_tmem(sg + (half ? OFF_DOHI : OFF_QHI), row, tl, half ? C_DOHI : C_QHI);
-            if (SPLIT) row_to_tmem(sg + (half ? OFF_DOLO : OFF_QLO), row, tl, half ? C_DOLO : C_QLO);
+        for (int x = 0; x < 32; x++) acc[x] = 0.0f;
+        bool ok = warp_wait(bar(C::QD_FULL), 0, abort, err);
+        if (ok) {  // Q (half 0) or dO (half 1) rows into TMEM: hi, and lo when it lives there
+            row_to_tmem<DD>(sg + (half ? C::OFF_DOHI_STAGE : C::OFF_QHI_STAGE), row, tl, half ? C::C_DOHI : C::C_QHI);
+            if (SPLIT && C::LO_TMEM)
+                row_to_tmem<DD>(sg + (half ? C::OFF_DOLO_STAGE : C::OFF_QLO_STAGE), row, tl, half ? C::C_DOLO : C::C_QLO);
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(bar(QD_READY));
+            mbar_arrive(bar(C::QD_READY));
         }
         const int64_t ridx = (b * p.H + h) * p.L + q;
         const float lse2 = row_ok ? a.lse2[ridx] : 0.0f;
         const float del = row_ok ? a.g.delta[ridx] : 0.0f;
-        float pv[32];      // P of the block in flight, this thread's 32 columns
+        float pv[CPT];      // P of the block in flight, this thread's columns
         uint32_t zcur = 0;  // its dropout keep bits
         // Reads S_j, releases its columns, and leaves P_j in pv.
         auto load_p = [&](int j) -> bool {
@@ -897,18 +966,19 @@ __global__ void __maxnreg__(168)
             uint32_t vbits = 0xFFFFFFFFu;
             if (edge) vbits = row_ok ? col_bits32(0, (p.causal ? min(p.S, q + 1) : p.S) - base) : 0u;
             // The user mask along this query's row, loaded before the wait for S.
-            float mk[MASKED ? 32 : 1];
-            if constexpr (MASKED) mask_run<32>(p, b, h, q, base, p.ms[3], vbits, mk);
+            float mk[MASKED ? CPT : 1];
+            if constexpr (MASKED) mask_run<CPT>(p, b, h, q, base, p.ms[3], vbits, mk);
             if constexpr (DROP) zcur = row_ok ? keep_run32(p, b, h, q, base) : 0u;
-            if (!warp_wait(bar(S_FULL), j & 1, abort, err)) return false;
+            if (!warp_wait(bar(C::S_FULL), j & 1, abort, err)) return false;
             tc_fence_after();
-            uint32_t sr[32];
-            tmem_ld32(tl + C_S + cb, sr);
+            uint32_t sr[CPT];
+#pragma unroll
+            for (int r0 = 0; r0 < CPT; r0 += 16) tmem_ld16(tl + C::C_S + cb + r0, *reinterpret_cast<uint32_t(*)[16]>(&sr[r0]));
             tmem_wait_ld();
             tc_fence_before();
-            mbar_arrive(bar(S_READ));
+            mbar_arrive(bar(C::S_READ));
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
+            for (int c = 0; c < CPT; c++) {
                 float x = __uint_as_float(sr[c]) * a.scale_log2;
                 if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
                 pv[c] = ((vbits >> c) & 1u) ? ex2_approx(x - lse2) : 0.0f;
@@ -917,15 +987,15 @@ __global__ void __maxnreg__(168)
         };
         if (ok && nblk > 0) ok = load_p(0);
         for (int j = 0; ok && j < nblk; j++) {
-            if (!warp_wait(bar(DP_FULL), j & 1, abort, err)) {
+            if (!warp_wait(bar(C::DP_FULL), j & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
 #pragma unroll
-            for (int r0 = 0; r0 < 32; r0 += 16) {  // dS in 16-column pieces
+            for (int r0 = 0; r0 < CPT; r0 += 16) {  // dS in 16-column pieces
                 uint32_t dr[16], xh[16], xl[16];
-                tmem_ld16(tl + C_DP + cb + r0, dr);
+                tmem_ld16(tl + C::C_DP + cb + r0, dr);
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
@@ -936,31 +1006,32 @@ __global__ void __maxnreg__(168)
                     xh[c] = tf32_rna(ds);
                     if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
                 }
-                tmem_st16(tl + C_DP + cb + r0, xh);
-                if (SPLIT) tmem_st16(tl + C_DSLO + cb + r0, xl);
+                tmem_st16(tl + C::C_DP + cb + r0, xh);
+                if (SPLIT) tmem_st16(tl + C::C_DSLO + cb + r0, xl);
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(DS_READY));
+            mbar_arrive(bar(C::DS_READY));
             // P of the next block while the tensor core runs dQ_j.
             if (j + 1 < nblk && !load_p(j + 1)) {
                 ok = false;
                 break;
             }
-            if (!warp_wait(bar(DQ_DONE), j & 1, abort, err)) {
+            if (!warp_wait(bar(C::DQ_DONE), j & 1, abort, err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            fold16(tl + C_DQB + 32 * half, acc);
-            fold16(tl + C_DQB + 32 * half + 16, acc + 16);
+            fold16(tl + C::C_DQB + 32 * half, acc);
+            fold16(tl + C::C_DQB + 32 * half + 16, acc + 16);
             tc_fence_before();
-            mbar_arrive(bar(DQ_FREE));
+            mbar_arrive(bar(C::DQ_FREE));
         }
         const bool aborted = __any_sync(FULL, *abort != 0);
         if (ok && !aborted && row_ok) {
-            float *dqr = a.g.dq + b * a.g.dqs[0] + h * a.g.dqs[1] + q * a.g.dqs[2] + (int64_t)(32 * half) * a.g.dqs[3];
-            store_row<D / 2>(dqr, a.g.dqs[3], acc, p.scale);
+            float *dqr = a.g.dq + b * a.g.dqs[0] + h * a.g.dqs[1] + q * a.g.dqs[2] +
+                         (int64_t)(64 * dh + 32 * half) * a.g.dqs[3];
+            store_row<32>(dqr, a.g.dqs[3], acc, p.scale);
         }
     }
 
@@ -968,7 +1039,7 @@ __global__ void __maxnreg__(168)
     __syncthreads();
     if (warp == W_MMA) {
         tc_fence_after();
-        tmem_dealloc(tmem, qq::TCOLS);
+        tmem_dealloc(tmem, C::TCOLS);
     }
 }
 
@@ -1023,18 +1094,30 @@ int stream_edge(cudaStream_t from, cudaStream_t to) {
 
 bool tc_backward_supported(const AttnProblem &p, const AttnGrads &g) {
     (void)g;
-    if (p.E != D || p.Ev != D) return false;
+    if (p.E != p.Ev || (p.E != 64 && p.E != 128)) return false;
     if (p.L >= (1ll << 31) - TILE || p.S >= (1ll << 31) - TILE) return false;
-    // 1-D grids of tiles x heads x batch.
+    // 1-D grids of tiles x heads x batch (x column halves at head dim 128).
     const int64_t tiles = (max(p.L, p.S) + TILE - 1) / TILE;
-    return 2 * p.B < (1ll << 31) && tiles * p.H * p.B < (1ll << 31);
+    return 2 * p.B < (1ll << 31) && tiles * p.H * p.B * (p.E / 64) < (1ll << 31);
 }
 
-int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
+namespace {
+
+// The instantiation of a backward kernel for (split, masked, dropout).
+template <class F>
+F pick_kernel(bool split, bool masked, bool drop, F ttt, F ttf, F tft, F tff, F ftt, F ftf, F fft, F fff) {
+    if (split) return masked ? (drop ? ttt : ttf) : (drop ? tft : tff);
+    return masked ? (drop ? ftt : ftf) : (drop ? fft : fff);
+}
+
+template <int DD>
+int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
+    using KC = KvCfg<DD>;
+    using QC = QqCfg<DD>;
     const bool split = precision != DC_PREC_TF32;
     const int64_t S2 = split ? 2 : 1;
     const int64_t rows_a = p.B * p.H * p.L, rows_b = p.B * p.Hkv * p.S;
-    const size_t bytes = sizeof(float) * (size_t)(S2 * 2 * (rows_a + rows_b) * D + rows_a);
+    const size_t bytes = sizeof(float) * (size_t)(S2 * 2 * (rows_a + rows_b) * DD + rows_a);
     PoolScratch ws;
     ws.stream = stream;
     int st = pool_alloc(&ws.ptr, bytes, stream);
@@ -1043,16 +1126,17 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     pa.p = p;
     pa.g = g;
     pa.qhl = static_cast<float *>(ws.ptr);
-    pa.dohl = pa.qhl + S2 * rows_a * D;
-    pa.khl = pa.dohl + S2 * rows_a * D;
-    pa.vhl = pa.khl + S2 * rows_b * D;
-    pa.lse2 = pa.vhl + S2 * rows_b * D;
+    pa.dohl = pa.qhl + S2 * rows_a * DD;
+    pa.khl = pa.dohl + S2 * rows_a * DD;
+    pa.vhl = pa.khl + S2 * rows_b * DD;
+    pa.lse2 = pa.vhl + S2 * rows_b * DD;
     pa.split = split ? 1 : 0;
     pa.vec = rows_vec(p.q, p.qs) && rows_vec(p.k, p.ks) && rows_vec(p.v, p.vs) && rows_vec(g.dout, g.dos) &&
              rows_vec(p.out, p.os);
     if (rows_a + rows_b > 0) {
+        constexpr int rpb = 256 / (DD / 4);  // rows per block
         KernelTrace tr("bwd_prep", stream);
-        bwd_prep_kernel<<<(unsigned)((rows_a + rows_b + 15) / 16), 256, 0, stream>>>(pa);
+        bwd_prep_kernel<DD><<<(unsigned)((rows_a + rows_b + rpb - 1) / rpb), 256, 0, stream>>>(pa);
         if ((st = check_launch("bwd_prep"))) return st;
     }
 
@@ -1064,10 +1148,11 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     a.err = device_error_word();
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
     // Strides (batch, head, row) of the contiguous hi / lo copies.
-    const int64_t qst[3] = {p.H * p.L * D, p.L * D, D}, kst[3] = {p.Hkv * p.S * D, p.S * D, D};
+    const int64_t qst[3] = {p.H * p.L * DD, p.L * DD, DD}, kst[3] = {p.Hkv * p.S * DD, p.S * DD, DD};
     const int64_t nb = S2 * p.B;
     const bool masked = p.mask_kind != MASK_NONE;
     const bool drop = p.keep != nullptr;
+    constexpr CUtensorMapSwizzle MN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     // The two tensor-core kernels run concurrently; with tracing on, this record spans both
     // (from before the fork to after the join, on the caller's stream).
     KernelTrace pair("bwd_tc", stream);
@@ -1079,54 +1164,62 @@ int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStr
     }
     if (p.S > 0) {
         CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
-        st = make_tmap(&tk, pa.khl, D, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tv, pa.vhl, D, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tqk, pa.qhl, D, p.L, p.H, nb, qst, kv::QB);
-        if (!st) st = make_tmap(&tqmn, pa.qhl, D, p.L, p.H, nb, qst, kv::QB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-        if (!st) st = make_tmap(&tdok, pa.dohl, D, p.L, p.H, nb, qst, kv::QB);
-        if (!st) st = make_tmap(&tdomn, pa.dohl, D, p.L, p.H, nb, qst, kv::QB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        st = make_tmap(&tk, pa.khl, DD, p.S, p.Hkv, nb, kst, TILE);
+        if (!st) st = make_tmap(&tv, pa.vhl, DD, p.S, p.Hkv, nb, kst, TILE);
+        if (!st) st = make_tmap(&tqk, pa.qhl, DD, p.L, p.H, nb, qst, KC::QB);
+        if (!st) st = make_tmap(&tqmn, pa.qhl, DD, p.L, p.H, nb, qst, KC::QB, MN);
+        if (!st) st = make_tmap(&tdok, pa.dohl, DD, p.L, p.H, nb, qst, KC::QB);
+        if (!st) st = make_tmap(&tdomn, pa.dohl, DD, p.L, p.H, nb, qst, KC::QB, MN);
         if (st) return st;
-        decltype(&attn_bwd_dkdv_tc_kernel<true, true, true>) kernel;
-        if (drop)
-            kernel = split ? (masked ? attn_bwd_dkdv_tc_kernel<true, true, true> : attn_bwd_dkdv_tc_kernel<true, false, true>)
-                           : (masked ? attn_bwd_dkdv_tc_kernel<false, true, true> : attn_bwd_dkdv_tc_kernel<false, false, true>);
-        else
-            kernel = split ? (masked ? attn_bwd_dkdv_tc_kernel<true, true, false> : attn_bwd_dkdv_tc_kernel<true, false, false>)
-                           : (masked ? attn_bwd_dkdv_tc_kernel<false, true, false> : attn_bwd_dkdv_tc_kernel<false, false, false>);
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::SMEM);
+        auto kernel = pick_kernel(split, masked, drop, attn_bwd_dkdv_tc_kernel<DD, true, true, true>,
+                                  attn_bwd_dkdv_tc_kernel<DD, true, true, false>,
+                                  attn_bwd_dkdv_tc_kernel<DD, true, false, true>,
+                                  attn_bwd_dkdv_tc_kernel<DD, true, false, false>,
+                                  attn_bwd_dkdv_tc_kernel<DD, false, true, true>,
+                                  attn_bwd_dkdv_tc_kernel<DD, false, true, false>,
+                                  attn_bwd_dkdv_tc_kernel<DD, false, false, true>,
+                                  attn_bwd_dkdv_tc_kernel<DD, false, false, false>);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)KC::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
-        const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B);
+        const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B * KC::NH);
         KernelTrace tr("bwd_dkdv_tc", stream);
-        kernel<<<grid, THREADS, kv::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
+        kernel<<<grid, THREADS, KC::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
         if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
     }
     if (p.L > 0) {
         CUtensorMap tq, tdo, tkk, tkmn, tvk;
-        st = make_tmap(&tq, pa.qhl, D, p.L, p.H, nb, qst, TILE);
-        if (!st) st = make_tmap(&tdo, pa.dohl, D, p.L, p.H, nb, qst, TILE);
-        if (!st) st = make_tmap(&tkk, pa.khl, D, p.S, p.Hkv, nb, kst, qq::NB);
-        if (!st) st = make_tmap(&tkmn, pa.khl, D, p.S, p.Hkv, nb, kst, qq::NB, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-        if (!st) st = make_tmap(&tvk, pa.vhl, D, p.S, p.Hkv, nb, kst, qq::NB);
+        st = make_tmap(&tq, pa.qhl, DD, p.L, p.H, nb, qst, TILE);
+        if (!st) st = make_tmap(&tdo, pa.dohl, DD, p.L, p.H, nb, qst, TILE);
+        if (!st) st = make_tmap(&tkk, pa.khl, DD, p.S, p.Hkv, nb, kst, QC::NB);
+        if (!st) st = make_tmap(&tkmn, pa.khl, DD, p.S, p.Hkv, nb, kst, QC::NB, MN);
+        if (!st) st = make_tmap(&tvk, pa.vhl, DD, p.S, p.Hkv, nb, kst, QC::NB);
         if (st) return st;
-        decltype(&attn_bwd_dq_tc_kernel<true, true, true>) kernel;
-        if (drop)
-            kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true, true> : attn_bwd_dq_tc_kernel<true, false, true>)
-                           : (masked ? attn_bwd_dq_tc_kernel<false, true, true> : attn_bwd_dq_tc_kernel<false, false, true>);
-        else
-            kernel = split ? (masked ? attn_bwd_dq_tc_kernel<true, true, false> : attn_bwd_dq_tc_kernel<true, false, false>)
-                           : (masked ? attn_bwd_dq_tc_kernel<false, true, false> : attn_bwd_dq_tc_kernel<false, false, false>);
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qq::SMEM);
+        auto kernel = pick_kernel(split, masked, drop, attn_bwd_dq_tc_kernel<DD, true, true, true>,
+                                  attn_bwd_dq_tc_kernel<DD, true, true, false>,
+                                  attn_bwd_dq_tc_kernel<DD, true, false, true>,
+                                  attn_bwd_dq_tc_kernel<DD, true, false, false>,
+                                  attn_bwd_dq_tc_kernel<DD, false, true, true>,
+                                  attn_bwd_dq_tc_kernel<DD, false, true, false>,
+                                  attn_bwd_dq_tc_kernel<DD, false, false, true>,
+                                  attn_bwd_dq_tc_kernel<DD, false, false, false>);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QC::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
-        const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B);
+        const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B * QC::NH);
         {
             KernelTrace tr("bwd_dq_tc", side);
-            kernel<<<grid, THREADS, qq::SMEM, side>>>(tq, tdo, tkk, tkmn, tvk, a);
+            kernel<<<grid, THREADS, QC::SMEM, side>>>(tq, tdo, tkk, tkmn, tvk, a);
         }
         const int launched = check_launch("attn_bwd_dq_tc");
         if ((st = stream_edge(side, stream))) return st;
         if (launched) return launched;
     }
     return DC_OK;
+}
+
+}  // namespace
+
+int tc_backward(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
+    return p.E == 64 ? tc_backward_dd<64>(p, g, precision, stream) : tc_backward_dd<128>(p, g, precision, stream);
 }
 
 }  // namespace dc

@@ -126,13 +126,16 @@ def test_config_shapes_against_oracle(name, precision):
 
 
 PERSISTENT_CASES = {
-    # More tiles than a B200 has SMs, so the persistent backward kernels loop over several tiles
-    # per CTA: ragged lengths with grouped-query heads (dQ 5 x 80 = 400 tiles, dK/dV 6 x 40 =
-    # 240), keys past the last query under causal masking (dK/dV tiles without query rows), and
-    # a per-batch bool mask.
+    # More tiles than a B200 has SMs (several waves of CTAs): ragged lengths with grouped-query
+    # heads (dQ 5 x 80 = 400 tiles, dK/dV 6 x 40 = 240), keys past the last query under causal
+    # masking (dK/dV tiles without query rows), a per-batch bool mask; and the same at head dim
+    # 128, where two CTAs share each tile (one per 64-column half of the gradients).
     "many_tiles_ragged_gqa": ((4, 20, 640, 64), (4, 10, 700, 64), True, None),
     "keys_past_queries": ((4, 8, 256, 64), (4, 8, 1024, 64), True, None),
     "many_tiles_bool_mask": ((2, 24, 512, 64), (2, 24, 512, 64), False, "bool"),
+    "d128_many_tiles_causal": ((2, 16, 512, 128), (2, 16, 512, 128), True, None),
+    "d128_gqa_bool_mask_ragged": ((2, 8, 400, 128), (2, 4, 333, 128), False, "bool"),
+    "d128_keys_past_queries": ((1, 4, 200, 128), (1, 4, 700, 128), True, None),
 }
 
 
