@@ -275,8 +275,10 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // Round to the nearest TF32 value, ties away from zero (what cvt.rna.tf32.f32 computes): on
 // the sign-magnitude encoding, add half a TF32 ulp (bit 12) to the magnitude and clear the 13
 // low mantissa bits. A carry into the exponent gives the next power of two, as rounding
-// should; +-Inf and NaN come out unchanged. Two integer ops on the full-rate ALU pipe instead
-// of a conversion instruction.
+// should; +-Inf comes out unchanged, and so does every NaN with a payload bit above the 13 low
+// bits (the quiet NaNs arithmetic produces). A NaN whose payload lies only in those bits turns
+// into +-Inf here; its low part (x - hi) is NaN, so a 3xTF32 product still yields NaN. Two
+// integer ops on the full-rate ALU pipe instead of a conversion instruction.
 __device__ __forceinline__ uint32_t tf32_rna(float x) {
     return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
