@@ -101,6 +101,7 @@ CONFIG_CASES = {
     "cfg4_long_d128": ((1, 1, 2048, 128), (1, 1, 2048, 128), True, None, 0.5),
     "odd_tiles": ((2, 3, 333, 64), (2, 3, 517, 64), False, "bool", 1.0),
     "causal_l_ne_s": ((1, 2, 300, 128), (1, 2, 200, 128), True, None, 1.0),
+    "d128_floatmask": ((1, 2, 384, 128), (1, 2, 512, 128), False, "float", 1.0),
 }
 
 
@@ -193,10 +194,11 @@ def test_value_dim_differs_and_rank3():
         _assert_close(nm, a, r.numpy(), 1e-5)
 
 
-def test_strided_views_need_no_copy(precision):
+@pytest.mark.parametrize("D", [64, 128])
+def test_strided_views_need_no_copy(precision, D):
     # nanoGPT's layout: (B, T, H, D) viewed as (B, H, T, D).
     rng = np.random.default_rng(15)
-    B, T, H, D = 2, 200, 4, 64
+    B, T, H = 2, 200, 4
     base = [rng.normal(size=(B, T, H, D)).astype(np.float32) for _ in range(3)]
     g = rng.normal(size=(B, H, T, D)).astype(np.float32)
     ts = [_cuda(a).transpose(1, 2).requires_grad_(True) for a in base]
