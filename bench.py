@@ -9,6 +9,7 @@ Workloads (synthetic seeded inputs of each config's sha
   nanogpt_causal_fwd_bwd  cfg 1: [64,6,256,64], causal, forward+backward
   mha_core_fwd_bwd        cfg 2 core: [32,8,128,64] with key padding lengths U[16,128], forward+backward
   long_causal_fwd         cfg 4: [1,16,32768,128] N(0,1)*0.5, causal, forward only
+  long_causal_fwd_8k      cfg 4's shape at 8192 keys (a profiling case)
   decode_splitkv          cfg 5: q [64,32,1,128], K/V [64,32,8192,128], split-KV decode (GB/s)
 
 Scaling is weak: under torchrun every rank runs the full workload on its own GPU (its shard of
@@ -52,6 +53,10 @@ WORKLOADS = {
     # Config 3 with attention dropout (GPT-2's 0.1): the keep mask is drawn every step.
     "gpt2_dropout_fwd_bwd": dict(q=(8, 12, 1024, 64), kv=(8, 12, 1024, 64), causal=True, mask=None, amp=1.0,
                                  bwd=True, cfg=3, dropout=0.1),
+    # Config 4's shape at a quarter of its length: a case small enough for a full ncu capture
+    # of the D = 128 forward (its DRAM traffic scales with the key blocks each tile streams).
+    "long_causal_fwd_8k": dict(q=(1, 16, 8192, 128), kv=(1, 16, 8192, 128), causal=True, mask=None, amp=0.5,
+                               bwd=False, cfg=4),
 }
 
 
