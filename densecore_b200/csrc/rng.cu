@@ -21,11 +21,14 @@
 //     twisted first, so the canonical block starts at B0 = 0 or 624 and pos >= B0;
 //   * G = B0 + 624; chunk c >= 1 covers words [G + cJ, G + (c+1)J), chunk 0 covers
 //     [pos, G + J) -- J = 624 * 840 words, so every chunk start is a block start;
-//   * a CTA owns the 32-element mask words whose first word lies in its chunk. CTA c >= 1
-//     reaches its chunk start by one jump with x^(c J) mod phi (a table computed on the host
-//     as needed, 2048 entries at most), then generates 224 words per phase in a mirrored
-//     2048-word shared ring while other warps turn earlier words into keep bits;
-//   * the CTA whose chunk holds the block of the last consumed word writes the new state in
+//   * the chunks are split into contiguous runs, one per CTA (at most one CTA per SM), and a
+//     CTA owns the 32-element mask words whose first word lies in its run. A run that starts
+//     at chunk c >= 1 is reached by one jump with x^(c J) mod phi (a table computed on the
+//     host as needed, 2048 entries at most); the CTA then makes 576 words per phase in a
+//     mirrored 4096-word shared ring (three words per thread, chained at distance 227), two
+//     phases per CTA barrier, while other warps turn the words of the previous two phases
+//     into keep bits;
+//   * the CTA whose run holds the block of the last consumed word writes the new state in
 //     DenseCore's form (that block, left = 625 - next, next = words of it consumed).
 #include <cuda_runtime.h>
 #include <math.h>
@@ -50,13 +53,23 @@ constexpr int DEG = 19937;                  // degree of phi
 constexpr int PW = (DEG + 63) / 64;         // 64-bit words of a reduced polynomial (312)
 constexpr int64_t CHUNK = 624LL * 840;      // words per chunk (524,160)
 constexpr int MAX_CHUNKS = 2048;            // jump table entries x^(c J), c < MAX_CHUNKS
-constexpr int RING = 2048;                  // shared ring of state words (power of two)
-constexpr int GEN_WARPS = 7;                // warps generating the stream
-constexpr int STEP = GEN_WARPS * 32;        // words generated per phase (224 <= 624 - 397)
-constexpr int CONV_WARPS = 4;               // warps turning words into keep bits
-constexpr int THREADS = (GEN_WARPS + CONV_WARPS) * 32;
-constexpr int JW = 4;                       // window words per thread in a jump (156 threads)
-static_assert(MT_N + 2 * STEP <= RING, "a jump phase must not overwrite words still being read");
+constexpr int LAG = MT_N - MT_M;            // 227: X[k] = X[k - LAG] ^ twist(X[k - 624], X[k - 623])
+constexpr int RING = 4096;                  // shared ring of state words (power of two), mirrored
+constexpr int PHASE = 576;                  // words generated per barrier (nine 64-word mask words)
+constexpr int GEN_WARPS = (LAG + 31) / 32;  // 8: thread t < LAG makes three chained words a phase
+constexpr int TURN = 2 * PHASE;             // words per CTA barrier: two phases, the generating
+                                            // warps syncing among themselves between them
+constexpr int CONV_WARPS = PHASE / 64;      // 9: two mask words (one element per lane) a turn each
+constexpr int WARPS = GEN_WARPS + CONV_WARPS;
+constexpr int THREADS = WARPS * 32;         // 544
+constexpr int JW = 2;                       // window words per thread in a jump
+constexpr int JT = MT_N / JW;               // 312 threads accumulate a jump
+constexpr int LIST_WARP = WARPS - 1;        // the warp that lists the set bits of a jump block
+static_assert(PHASE <= MT_N - 1 && PHASE - 2 * LAG <= MT_N - 1 - 2 * LAG,
+              "a thread's third word must only read words made before the phase");
+static_assert(PHASE % 64 == 0 && JT <= LIST_WARP * 32, "warp roles");
+static_assert(2 * PHASE + MT_N <= RING, "a jump phase must not overwrite words still being read");
+static_assert(2 * TURN + MT_N <= RING, "a turn must not overwrite words still being read");
 
 __host__ __device__ __forceinline__ int64_t imin(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ uint32_t twist(uint32_t u, uint32_t v) {
@@ -335,143 +348,230 @@ struct KeepArgs {
     int *err;             // the library's device error word
 };
 
-// Generates X[P, P + cnt) (cnt <= STEP) into both copies of the ring, threads 0..cnt-1. Ring
-// slot k % RING and its mirror RING + k % RING hold X[k], so a run of up to RING words read
-// from any slot below RING needs no wrap-around. Slot arithmetic is 32-bit (RING divides 2^32).
-__device__ __forceinline__ void gen_step(uint32_t *ring, uint32_t P, int cnt) {
+// Writes X[k] into slot k % RING and its mirror RING + k % RING, so that a run of up to RING
+// words read from any slot below RING needs no wrap-around. Slot arithmetic is 32-bit (RING
+// divides 2^32).
+__device__ __forceinline__ void put(uint32_t *ring, uint32_t k, uint32_t v) {
+    const uint32_t s = k & (RING - 1);
+    ring[s] = v;
+    ring[s + RING] = v;
+}
+
+// Generates X[P, P + cnt), cnt <= PHASE, with every word below P already in the ring. Thread
+// t < LAG makes the chain X[P + t], X[P + t + LAG], X[P + t + 2 LAG] (those below P + cnt):
+// a chain word takes X[k - LAG] from the thread's previous word and X[k - 624], X[k - 623]
+// from below P (t + 2 LAG < PHASE keeps the third word's operands there), so no thread reads
+// a word made in the same phase by another thread, and all reads come before the writes.
+__device__ __forceinline__ void gen_words(uint32_t *ring, uint32_t P, int cnt) {
     const int t = threadIdx.x;
-    if (t < cnt) {
-        const uint32_t k = P + t;
-        const uint32_t v = ring[(k - MT_N + MT_M) & (RING - 1)] ^
-                           twist(ring[(k - MT_N) & (RING - 1)], ring[(k - MT_N + 1) & (RING - 1)]);
-        ring[k & (RING - 1)] = v;
-        ring[(k & (RING - 1)) + RING] = v;
+    if (t >= LAG || t >= cnt) return;
+    const uint32_t k = P + (uint32_t)t;
+    const uint32_t *r = ring + (k & (RING - 1)) + RING;  // r[-d] = X[k - d], 0 < d <= RING
+    const bool two = t + LAG < cnt, three = t + 2 * LAG < cnt;
+    const uint32_t a0 = r[-LAG], a1 = r[-MT_N], a2 = r[-MT_N + 1];
+    const uint32_t b1 = two ? r[LAG - MT_N] : 0u, b2 = two ? r[LAG - MT_N + 1] : 0u;
+    const uint32_t c1 = three ? r[2 * LAG - MT_N] : 0u, c2 = three ? r[2 * LAG - MT_N + 1] : 0u;
+    uint32_t x = a0 ^ twist(a1, a2);
+    put(ring, k, x);
+    if (two) {
+        x ^= twist(b1, b2);
+        put(ring, k + LAG, x);
+        if (three) {
+            x ^= twist(c1, c2);
+            put(ring, k + 2 * LAG, x);
+        }
     }
 }
 
+// Mask word q from the ring: element 32 q + lane uses the words k + 2 lane (high half of the
+// 64-bit draw) and k + 2 lane + 1, where k = pos + 64 q and `slot` = k + 2 lane (mod 2^32).
+__device__ __forceinline__ void load_pair(const uint32_t *ring, uint32_t slot, uint32_t &hi, uint32_t &lo) {
+    const uint32_t s = slot & (RING - 1);
+    hi = ring[s];
+    lo = ring[s + 1];  // s + 1 <= RING: the mirror
+}
+
+// Stores mask word q from the untempered pair (hi, lo) of each lane. One warp, all lanes.
+__device__ __forceinline__ void store_word(const KeepArgs &a, uint32_t hi, uint32_t lo, int64_t q, int lane) {
+    const uint32_t hi32 = temper(hi), lo32 = temper(lo);
+    const uint64_t m = ((uint64_t)(hi32 & 0x1fffffu) << 32) | lo32;
+    const uint32_t word = __ballot_sync(0xffffffffu, 32 * q + lane < a.n && m < a.thresh);
+    if (lane == 0) a.bits[q] = word;
+}
+
+// The set bits of jump block j (coefficients PHASE j .. PHASE j + PHASE - 1 of g) as offsets
+// within the block, in `list`, and their number in `count`. One warp.
+__device__ __forceinline__ void list_bits(const uint32_t *__restrict__ g, int j, uint16_t *list, int *count,
+                                          int lane) {
+    constexpr int GW = PHASE / 32;
+    const int gi = j * GW + lane;
+    const uint32_t mine = lane < GW && gi < 2 * PW ? __ldg(g + gi) : 0u;
+    int c = 0;
+#pragma unroll
+    for (int u = 0; u < GW; u++) {
+        const uint32_t w = __shfl_sync(0xffffffffu, mine, u);
+        const bool set = (w >> lane) & 1u;
+        const uint32_t bal = __ballot_sync(0xffffffffu, set);
+        if (set) list[c + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(32 * u + lane);
+        c += __popc(bal);
+    }
+    if (lane == 0) *count = c;
+}
+
 // Jumps the window X[b, b + 624) in the ring (P == b + 624 on entry) by the polynomial g
-// (DEG bits in 2 PW 32-bit words): on return the ring holds X[b + dist, b + dist + 624) and
-// P == b + dist + 624. Thread t < 156 accumulates window words t + 156 d, d < 4 (a warp reads
-// consecutive words: no bank conflicts), two set bits of g per loop turn.
-__device__ void jump_window(uint32_t *ring, const uint32_t *__restrict__ g, int64_t &b, int64_t &P, int64_t dist) {
-    const int tid = threadIdx.x;
-    constexpr int NT = MT_N / JW;
-    uint32_t acc[JW] = {0u, 0u, 0u, 0u};
-    const uint32_t b32 = (uint32_t)b;
-    for (int j = 0; j * STEP < DEG; j++) {
-        gen_step(ring, (uint32_t)P, STEP);
-        P += STEP;
+// (DEG coefficients in 2 PW 32-bit words): on return the ring holds X[b + dist, b + dist + 624)
+// and P == b + dist + 624. Block j of g's coefficients is handled after the phase that makes
+// X[.., b + 624 + PHASE (j + 1)): thread t < JT adds X[b + i + w] into window words
+// w = t + JT d, d < JW, for the block's set bits i (a warp reads consecutive words: no bank
+// conflicts). The list warp writes the set bits of block j + 1 while block j is summed
+// (three list buffers: a buffer is rewritten two barriers after its last reader started).
+__device__ void jump_window(uint32_t *ring, uint16_t (*list)[PHASE], int *count, const uint32_t *__restrict__ g,
+                            int64_t &b, int64_t &P, int64_t dist) {
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    constexpr int NBLK = (DEG + PHASE - 1) / PHASE;
+    uint32_t acc[JW] = {};
+    if (warp == LIST_WARP) list_bits(g, 0, list[0], &count[0], lane);
+    for (int j = 0; j < NBLK; j++) {
+        gen_words(ring, (uint32_t)P, PHASE);
+        if (warp == LIST_WARP && j + 1 < NBLK) list_bits(g, j + 1, list[(j + 1) % 3], &count[(j + 1) % 3], lane);
         __syncthreads();
-        if (tid < NT) {
-            // X[b + STEP j + i + w], i < STEP, w < 624: all below P and held (624 + 2 STEP <= RING).
-            const uint32_t *p = ring + ((b32 + (uint32_t)(j * STEP)) & (RING - 1)) + tid;
+        P += PHASE;
+        if (tid < JT) {
+            // X[b + PHASE j + i + w], i < PHASE, w < 624: below P, and no later phase reaches
+            // their slots before the next barrier (2 PHASE + 624 <= RING).
+            const uint32_t *p = ring + (((uint32_t)b + (uint32_t)(j * PHASE)) & (RING - 1)) + tid;
+            const uint16_t *L = list[j % 3];
+            const int cnt = count[j % 3];
+            int i = 0;
+            for (; i + 4 <= cnt; i += 4) {
+                const uint2 v = *reinterpret_cast<const uint2 *>(L + i);
+                const uint32_t o0 = v.x & 0xffffu, o1 = v.x >> 16, o2 = v.y & 0xffffu, o3 = v.y >> 16;
 #pragma unroll
-            for (int u = 0; u < STEP / 32; u++) {
-                const int gi = j * (STEP / 32) + u;
-                uint32_t gw = gi < 2 * PW ? __ldg(g + gi) : 0u;
-                while (gw) {
-                    const int t1 = __ffs(gw) - 1;
-                    gw &= gw - 1;
-                    const int t2 = gw ? __ffs(gw) - 1 : t1;
-                    const uint32_t m2 = gw ? ~0u : 0u;
-                    gw &= gw - 1;
-                    const uint32_t *r1 = p + 32 * u + t1, *r2 = p + 32 * u + t2;
+                for (int d = 0; d < JW; d++) acc[d] ^= p[o0 + JT * d] ^ p[o1 + JT * d] ^ p[o2 + JT * d] ^ p[o3 + JT * d];
+            }
+            for (; i < cnt; i++) {
+                const uint32_t o = L[i];
 #pragma unroll
-                    for (int d = 0; d < JW; d++) acc[d] ^= r1[NT * d] ^ (r2[NT * d] & m2);
-                }
+                for (int d = 0; d < JW; d++) acc[d] ^= p[o + JT * d];
             }
         }
     }
     __syncthreads();
     b += dist;
-    if (tid < NT) {
+    if (tid < JT) {
 #pragma unroll
-        for (int d = 0; d < JW; d++) {
-            const uint32_t k = ((uint32_t)b + tid + NT * d) & (RING - 1);
-            ring[k] = acc[d];
-            ring[k + RING] = acc[d];
-        }
+        for (int d = 0; d < JW; d++) put(ring, (uint32_t)b + (uint32_t)(tid + JT * d), acc[d]);
     }
     P = b + MT_N;
     __syncthreads();
 }
 
-// Warps 0..6 generate the stream, STEP words per phase; warps 7..10 turn words produced in
-// earlier phases into keep bits (one element per lane, one 32-bit mask word per warp) and
-// copy out the end state, so conversion overlaps generation.
+// CTA c of K owns the chunks [c nch / K, (c + 1) nch / K) of the call's nch chunks: it reaches
+// the first one's start by one jump (none for chunk 0), then makes TURN words per CTA barrier
+// (eight generating warps) and turns each turn's words into eighteen mask words in the next
+// turn of the loop (nine conversion warps), while the following turn is made. The CTA whose
+// chunks hold the block of the last consumed word copies out the end state.
 __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
     __shared__ uint32_t ring[2 * RING];
+    __shared__ __align__(8) uint16_t list[3][PHASE];
+    __shared__ int count[3];
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int c = blockIdx.x;
 
     const uint32_t left = a.st_in[MT_N];
     if (left == 0 || left > (uint32_t)MT_N) {  // not a state DenseCore's engine can be in
-        if (c == 0 && threadIdx.x == 0) atomicExch(a.err, sm100::DEV_BAD_GENERATOR_STATE);
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(a.err, sm100::DEV_BAD_GENERATOR_STATE);
         return;
     }
     const int64_t pos = 625 - (int64_t)left;          // 1..624
     const int64_t B0 = pos == MT_N ? MT_N : 0;        // canonical block start
     const int64_t G = B0 + MT_N;
-    const int64_t W = 2 * a.n;                        // words consumed
-    const int64_t last = pos + W - 1;                 // last consumed word
+    const int64_t last = pos + 2 * a.n - 1;           // last consumed word
     const int64_t E = B0 + MT_N * ((last - B0) / MT_N);  // its block
-    const int64_t lo = c == 0 ? pos : G + c * CHUNK, hi = G + (c + 1) * CHUNK;
-    // Owned mask words: first word pos + 64 q in [lo, hi).
-    int64_t q = c == 0 ? 0 : (lo - pos + 63) / 64;
-    int64_t q_end = (hi - pos + 63) / 64;
-    if (q_end > a.nmask) q_end = a.nmask;
-    const bool owns_end = (E < G ? 0 : (E - G) / CHUNK) == c;
-    if (q >= q_end && !owns_end) return;  // uniform across the CTA
+    // Chunk 0 is [pos, G + CHUNK), chunk c >= 1 is [G + c CHUNK, G + (c + 1) CHUNK); a mask
+    // word belongs to the chunk of its first word pos + 64 q.
+    const int64_t cE = E < G ? 0 : (E - G) / CHUNK;
+    const int64_t qlast = pos + 64 * (a.nmask - 1);
+    const int64_t cQ = qlast < G ? 0 : (qlast - G) / CHUNK;
+    const int64_t nch = 1 + (cE > cQ ? cE : cQ);
+    const int64_t K = gridDim.x, c0 = blockIdx.x * nch / K, c1 = (blockIdx.x + 1) * nch / K;
+    if (c0 >= c1) return;  // uniform across the CTA
+    const int64_t lo = c0 == 0 ? pos : G + c0 * CHUNK, hi = G + c1 * CHUNK;
+    const int64_t q_lo = c0 == 0 ? 0 : (lo - pos + 63) / 64;
+    const int64_t q_hi = imin((hi - pos + 63) / 64, a.nmask);
+    const bool owns_end = cE >= c0 && cE < c1;
+    if (q_lo >= q_hi && !owns_end) return;
 
     for (int i = tid; i < MT_N; i += THREADS) ring[i] = ring[i + RING] = a.st_in[i];
     __syncthreads();
     int64_t b = 0, P = MT_N;  // window X[b, b + 624), produced up to P
-    if (c > 0) {
+    if (c0 > 0) {
         while (P < G + MT_N) {  // the base window at G
-            const int cnt = (int)imin(STEP, G + MT_N - P);
-            gen_step(ring, (uint32_t)P, cnt);
-            P += cnt;
+            const int cnt = (int)imin(PHASE, G + MT_N - P);
+            gen_words(ring, (uint32_t)P, cnt);
             __syncthreads();
+            P += cnt;
         }
         b = G;
-        jump_window(ring, a.tab + (size_t)c * 2 * PW, b, P, c * CHUNK);
+        jump_window(ring, list, count, a.tab + (size_t)c0 * 2 * PW, b, P, c0 * CHUNK);
     }
-    // Every phase: words below P are visible; generation writes X[P, P + STEP) over the slots
-    // of X[P - RING, P - RING + STEP), while conversion reads at or above pos + 64 q >= P - 624
-    // and the end-state copy at or above E > P - 624 - STEP.
+    // Phases start at P = pos (mod 64), so that each one holds nine whole mask words.
+    const int align = (int)((pos - P) & 63);
+    if (align) {
+        gen_words(ring, (uint32_t)P, align);
+        __syncthreads();
+        P += align;
+    }
+    // Owned mask words whose words are already made: those of the window.
+    const int64_t q_pre = imin(q_hi, (P - pos) / 64);
+    for (int64_t q = q_lo + warp; q < q_pre; q += WARPS) {
+        uint32_t hi, lo;
+        load_pair(ring, (uint32_t)(pos + 64 * q) + 2u * (uint32_t)lane, hi, lo);
+        store_word(a, hi, lo, q, lane);
+    }
+
+    int64_t target = pos + 64 * q_hi;
+    if (owns_end && E + MT_N > target) target = E + MT_N;
+    const int64_t nturn = target > P ? (target - P + TURN - 1) / TURN : 0;
     bool captured = !owns_end;
-    while (q < q_end || !captured) {
-        const int64_t ready = (P - (pos + 64 * q)) / 64;  // mask words whose words are all below P
-        int cnt = (int)imin(imin(CONV_WARPS, q_end - q), ready);
-        if (cnt < 0) cnt = 0;
-        const bool capture = !captured && P >= E + MT_N;
+    // Turn u: copy out the end state once its block is made; the generating warps make the two
+    // phases [P, P + PHASE) and [P + PHASE, P + TURN) (a named barrier of their own between
+    // them; the slots written are those of words at least RING - TURN below P: neither read
+    // nor copied here) while each conversion warp turns two mask words of the words of turn
+    // u - 1 ([P - TURN, P)), two independent chains.
+    const int cw = warp - GEN_WARPS;
+    int64_t qw = (P - pos) / 64 + cw;  // this conversion warp's first mask word in turn 1
+    uint32_t slot = (uint32_t)(pos + 64 * qw) + 2u * (uint32_t)lane;
+    uint32_t P32 = (uint32_t)P;
+    for (int64_t u = 0; u <= nturn; u++) {
+        if (!captured && P >= E + MT_N) {
+            for (int i = tid; i < MT_N; i += THREADS) a.st_out[i] = ring[((uint32_t)E + (uint32_t)i) & (RING - 1)];
+            if (tid == 0) {
+                const uint32_t next = (uint32_t)(last - E + 1);
+                a.st_out[MT_N] = 625u - next;
+                a.st_out[MT_N + 1] = next;
+            }
+            captured = true;
+        }
         if (warp < GEN_WARPS) {
-            gen_step(ring, (uint32_t)P, STEP);
-        } else {
-            const int cw = warp - GEN_WARPS;
-            if (cw < cnt) {
-                const int64_t e = 32 * (q + cw) + lane;
-                const uint32_t k = (uint32_t)(pos + 2 * e) & (RING - 1);
-                const uint32_t hi32 = temper(ring[k]), lo32 = temper(ring[k + 1]);  // k + 1 < 2 RING
-                const uint64_t m = ((uint64_t)(hi32 & 0x1fffffu) << 32) | lo32;
-                const uint32_t word = __ballot_sync(0xffffffffu, e < a.n && m < a.thresh);
-                if (lane == 0) a.bits[q + cw] = word;
+            if (u < nturn) {
+                gen_words(ring, P32, PHASE);
+                asm volatile("bar.sync 1, %0;" ::"r"(GEN_WARPS * 32) : "memory");
+                gen_words(ring, P32 + PHASE, PHASE);
             }
-            if (capture) {
-                const int ct = tid - GEN_WARPS * 32;
-                for (int i = ct; i < MT_N; i += THREADS - GEN_WARPS * 32)
-                    a.st_out[i] = ring[((uint32_t)E + i) & (RING - 1)];
-                if (ct == 0) {
-                    const uint32_t next = (uint32_t)(last - E + 1);
-                    a.st_out[MT_N] = 625u - next;
-                    a.st_out[MT_N + 1] = next;
-                }
-            }
+        } else if (u > 0) {
+            const int64_t q1 = qw + CONV_WARPS;
+            const bool t0 = qw >= q_lo && qw < q_hi, t1 = q1 >= q_lo && q1 < q_hi;
+            uint32_t h0 = 0u, l0 = 0u, h1 = 0u, l1 = 0u;
+            if (t0) load_pair(ring, slot, h0, l0);
+            if (t1) load_pair(ring, slot + 64u * CONV_WARPS, h1, l1);
+            if (t0) store_word(a, h0, l0, qw, lane);
+            if (t1) store_word(a, h1, l1, q1, lane);
+            qw += 2 * CONV_WARPS;
+            slot += 128u * CONV_WARPS;
         }
         __syncthreads();
-        P += STEP;
-        q += cnt;
-        captured = captured || capture;
+        P += TURN;
+        P32 += TURN;
     }
 }
 
@@ -542,12 +642,16 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
         st = pool_alloc(reinterpret_cast<void **>(&tmp), 2 * (MT_N + 2) * 4, stream);
         if (st) return st;
     }
+    // One CTA per SM at most: each CTA pays one jump (shared-memory bound, the same for every
+    // distance); a second CTA per SM measured no faster.
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint32_t *src = st_in;
     for (int64_t l = 0; l < launches; l++) {
         const int64_t e0 = l * kMaxElemsPerLaunch, ne = imin(kMaxElemsPerLaunch, n - e0);
         uint32_t *dst = l == launches - 1 && st_out != st_in ? st_out : tmp + (l & 1) * (MT_N + 2);
         KeepArgs a{src, dst, tab, bits + e0 / 32, ne, (ne + 31) / 32, thresh, err};
-        const int64_t grid = 2 + (2 * ne - 1) / CHUNK;
+        const int64_t grid = imin(1 + (2 * ne - 1) / CHUNK, sms > 0 ? sms : 1);  // >= the chunks' count
         {
             KernelTrace tr("dropout_keep_bits", stream);
             keep_bits_kernel<<<(unsigned)grid, THREADS, 0, stream>>>(a);

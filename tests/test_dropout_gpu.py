@@ -3,7 +3,7 @@
 * dc_dropout_keep_bits: the packed keep mask and the advanced engine state are bit-identical
   to the oracle's sequential mt19937 + bernoulli (src/torch_random.rs:43-110, :242-254), from
   seeded, part-used and block-end states, for sizes from one element to several chunks of the
-  parallel walk (one and two jump levels);
+  parallel walk per CTA (one and two jump levels);
 * scaled_dot_product_attention with dropout_p > 0: the reference's case list
   (tests/test_random_exact.py:90-103, fixtures from PyTorch's CPU SDPA) at the reference's
   tolerances (tests/test_attention.py:34, :39), and masks, grouped-query heads, rank 3 and
@@ -44,7 +44,9 @@ def _device_bits(state, n, keep_prob, in_place=False):
 
 @pytest.mark.parametrize("seed,pre,n", [
     (5, 0, 1), (5, 0, 31), (5, 0, 32), (5, 0, 33), (7, 1, 1000), (9, 623, 4099), (11, 624, 100_000),
-    (13, 300, CHUNK_ELEMS - 3), (2, 0, 3 * CHUNK_ELEMS + 77), (4, 17, 35 * CHUNK_ELEMS + 5)])
+    (13, 300, CHUNK_ELEMS - 3), (2, 0, 3 * CHUNK_ELEMS + 77), (4, 17, 35 * CHUNK_ELEMS + 5),
+    # more chunks than SMs: CTAs own runs of several chunks (the last: config 3's weights)
+    (6, 400, 160 * CHUNK_ELEMS + 11), (3, 0, 8 * 12 * 1024 * 1024)])
 @pytest.mark.parametrize("keep_prob", [0.8, 0.5])
 def test_keep_bits_match_oracle(seed, pre, n, keep_prob):
     g = oracle.MtGenerator(seed).discard(pre)
