@@ -20,7 +20,7 @@
 //   * pos = 625 - left is the next output; a seeded or fully used block (left == 1) is
 //     twisted first, so the canonical block starts at B0 = 0 or 624 and pos >= B0;
 //   * G = B0 + 624; chunk c >= 1 covers words [G + cJ, G + (c+1)J), chunk 0 covers
-//     [pos, G + J) -- J = 624 * 840 words, so every chunk start is a block start;
+//     [pos, G + J) -- J = 624 * 210 words, so every chunk start is a block start;
 //   * the chunks are split into contiguous runs, one per CTA (at most one CTA per SM), and a
 //     CTA owns the 32-element mask words whose first word lies in its run. A run that starts
 //     at chunk c >= 1 is reached by one jump with x^(c J) mod phi (a table computed on the
@@ -51,7 +51,7 @@ constexpr int MT_N = 624, MT_M = 397;
 constexpr uint32_t MATRIX_A = 0x9908b0dfu, UMASK = 0x80000000u, LMASK = 0x7fffffffu;
 constexpr int DEG = 19937;                  // degree of phi
 constexpr int PW = (DEG + 63) / 64;         // 64-bit words of a reduced polynomial (312)
-constexpr int64_t CHUNK = 624LL * 840;      // words per chunk (524,160)
+constexpr int64_t CHUNK = 624LL * 210;      // words per chunk (131,040): runs of chunks balance CTAs
 constexpr int MAX_CHUNKS = 2048;            // jump table entries x^(c J), c < MAX_CHUNKS
 constexpr int LAG = MT_N - MT_M;            // 227: X[k] = X[k - LAG] ^ twist(X[k - 624], X[k - 623])
 constexpr int RING = 4096;                  // shared ring of state words (power of two), mirrored
@@ -64,10 +64,20 @@ constexpr int WARPS = GEN_WARPS + CONV_WARPS;
 constexpr int THREADS = WARPS * 32;         // 544
 constexpr int JW = 2;                       // window words per thread in a jump
 constexpr int JT = MT_N / JW;               // 312 threads accumulate a jump
-constexpr int LIST_WARP = WARPS - 1;        // the warp that lists the set bits of a jump block
+constexpr int LIST_WARP = WARPS - 1;        // the warp that lists the nibbles of a jump block
+// Dynamic shared memory, in 32-bit words: the mirrored ring, then the eleven jump tables (sums
+// of two to four of four consecutive words, TABW each), then two lists of NIB 16-bit entries
+// and their two counts.
+constexpr int NIB = PHASE / 4;              // coefficient nibbles per jump block
+constexpr int TABW = 1200;                  // >= 4 (NIB - 1) + MT_N: a table's words per block
+constexpr int NTAB = 11;
+constexpr int TAB0 = 2 * RING, LST0 = TAB0 + NTAB * TABW, CNT0 = LST0 + NIB;
+constexpr int SMEM_WORDS = CNT0 + 2;
+static_assert(SMEM_WORDS < 65536, "list entries are 16-bit word offsets");
 static_assert(PHASE <= MT_N - 1 && PHASE - 2 * LAG <= MT_N - 1 - 2 * LAG,
               "a thread's third word must only read words made before the phase");
-static_assert(PHASE % 64 == 0 && JT <= LIST_WARP * 32, "warp roles");
+static_assert(PHASE % 64 == 0 && JT <= LIST_WARP * 32 && JT % 8 == 0, "warp roles");
+static_assert(4 * (NIB - 1) + MT_N <= TABW && (LST0 % 2) == 0, "jump table layout");
 static_assert(2 * PHASE + MT_N <= RING, "a jump phase must not overwrite words still being read");
 static_assert(2 * TURN + MT_N <= RING, "a turn must not overwrite words still being read");
 
@@ -399,10 +409,12 @@ __device__ __forceinline__ void store_word(const KeepArgs &a, uint32_t hi, uint3
     if (lane == 0) a.bits[q] = word;
 }
 
-// The set bits of jump block j (coefficients PHASE j .. PHASE j + PHASE - 1 of g) as offsets
-// within the block, in `list`, and their number in `count`. One warp.
-__device__ __forceinline__ void list_bits(const uint32_t *__restrict__ g, int j, uint16_t *list, int *count,
-                                          int lane) {
+// The nonzero nibbles of jump block j (coefficients PHASE j .. PHASE j + PHASE - 1 of g), as
+// 16-bit word offsets into shared memory: a nibble v at coefficient 4 n reads X[B + 4 n + s + w]
+// from the ring when v has one bit s, and word 4 n + w of table v otherwise (B = the block's
+// first word, at ring slot sB). Their number goes to `count`. One warp.
+__device__ __forceinline__ void list_nibbles(const uint32_t *__restrict__ g, int j, uint32_t sB, uint16_t *list,
+                                             int *count, int lane) {
     constexpr int GW = PHASE / 32;
     const int gi = j * GW + lane;
     const uint32_t mine = lane < GW && gi < 2 * PW ? __ldg(g + gi) : 0u;
@@ -410,9 +422,15 @@ __device__ __forceinline__ void list_bits(const uint32_t *__restrict__ g, int j,
 #pragma unroll
     for (int u = 0; u < GW; u++) {
         const uint32_t w = __shfl_sync(0xffffffffu, mine, u);
-        const bool set = (w >> lane) & 1u;
-        const uint32_t bal = __ballot_sync(0xffffffffu, set);
-        if (set) list[c + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(32 * u + lane);
+        const uint32_t v = lane < 8 ? (w >> (4 * lane)) & 15u : 0u;
+        const uint32_t bal = __ballot_sync(0xffffffffu, v != 0u);
+        if (v) {
+            const int n = 8 * u + lane;
+            // tables hold the values with two or more bits: 3, 5, 6, 7, 9, ..., 15 -> 0 .. 10
+            const int idx = (int)v - 1 - (v > 1u) - (v > 2u) - (v > 4u) - (v > 8u);
+            const uint32_t base = __popc(v) == 1 ? sB + (uint32_t)(__ffs(v) - 1) : (uint32_t)(TAB0 + idx * TABW);
+            list[c + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(base + 4u * (uint32_t)n);
+        }
         c += __popc(bal);
     }
     if (lane == 0) *count = c;
@@ -420,39 +438,69 @@ __device__ __forceinline__ void list_bits(const uint32_t *__restrict__ g, int j,
 
 // Jumps the window X[b, b + 624) in the ring (P == b + 624 on entry) by the polynomial g
 // (DEG coefficients in 2 PW 32-bit words): on return the ring holds X[b + dist, b + dist + 624)
-// and P == b + dist + 624. Block j of g's coefficients is handled after the phase that makes
-// X[.., b + 624 + PHASE (j + 1)): thread t < JT adds X[b + i + w] into window words
-// w = t + JT d, d < JW, for the block's set bits i (a warp reads consecutive words: no bank
-// conflicts). The list warp writes the set bits of block j + 1 while block j is summed
-// (three list buffers: a buffer is rewritten two barriers after its last reader started).
-__device__ void jump_window(uint32_t *ring, uint16_t (*list)[PHASE], int *count, const uint32_t *__restrict__ g,
-                            int64_t &b, int64_t &P, int64_t dist) {
+// and P == b + dist + 624. Block j of g (coefficients [PHASE j, PHASE j + PHASE), first word
+// B = b + PHASE j) is taken four coefficients at a time (the method of four Russians): once
+// the phase that makes X[.., B + 1200) is done, the CTA writes the eleven tables
+// T_v[k] = XOR over the bits s of v of X[B + k + s], then thread t < JT adds, for each nonzero
+// nibble v at 4 n, the word 4 n + w of T_v (or of the ring when v has one bit) into window
+// words w = t + JT d, d < JW. A warp reads consecutive words: no bank conflicts. The list warp
+// writes block j's entries while the phase is made (two list buffers: a buffer is rewritten
+// two barriers after its last reader finished).
+__device__ void jump_window(uint32_t *sm, const uint32_t *__restrict__ g, int64_t &b, int64_t &P, int64_t dist) {
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     constexpr int NBLK = (DEG + PHASE - 1) / PHASE;
+    uint16_t *lists = reinterpret_cast<uint16_t *>(sm + LST0);
+    int *counts = reinterpret_cast<int *>(sm + CNT0);
     uint32_t acc[JW] = {};
-    if (warp == LIST_WARP) list_bits(g, 0, list[0], &count[0], lane);
     for (int j = 0; j < NBLK; j++) {
-        gen_words(ring, (uint32_t)P, PHASE);
-        if (warp == LIST_WARP && j + 1 < NBLK) list_bits(g, j + 1, list[(j + 1) % 3], &count[(j + 1) % 3], lane);
+        const uint32_t sB = ((uint32_t)b + (uint32_t)(j * PHASE)) & (RING - 1);
+        gen_words(sm, (uint32_t)P, PHASE);
+        if (warp == LIST_WARP) list_nibbles(g, j, sB, lists + (j & 1) * NIB, &counts[j & 1], lane);
         __syncthreads();
         P += PHASE;
-        if (tid < JT) {
-            // X[b + PHASE j + i + w], i < PHASE, w < 624: below P, and no later phase reaches
-            // their slots before the next barrier (2 PHASE + 624 <= RING).
-            const uint32_t *p = ring + (((uint32_t)b + (uint32_t)(j * PHASE)) & (RING - 1)) + tid;
-            const uint16_t *L = list[j % 3];
-            const int cnt = count[j % 3];
-            int i = 0;
-            for (; i + 4 <= cnt; i += 4) {
-                const uint2 v = *reinterpret_cast<const uint2 *>(L + i);
-                const uint32_t o0 = v.x & 0xffffu, o1 = v.x >> 16, o2 = v.y & 0xffffu, o3 = v.y >> 16;
+        // X[B + k + s], k < TABW, s < 4: below P = B + 1200 + 4... made; sB + k + s < 2 RING.
+        for (int k = tid; k < TABW; k += THREADS) {
+            const uint32_t *x = sm + sB + k;
+            const uint32_t x0 = x[0], x1 = x[1], x2 = x[2], x3 = x[3];
+            const uint32_t t3 = x0 ^ x1, t5 = x0 ^ x2, t6 = x1 ^ x2, t7 = t3 ^ x2;
+            uint32_t *t = sm + TAB0 + k;
+            t[0 * TABW] = t3;
+            t[1 * TABW] = t5;
+            t[2 * TABW] = t6;
+            t[3 * TABW] = t7;
+            t[4 * TABW] = x0 ^ x3;
+            t[5 * TABW] = x1 ^ x3;
+            t[6 * TABW] = t3 ^ x3;
+            t[7 * TABW] = x2 ^ x3;
+            t[8 * TABW] = t5 ^ x3;
+            t[9 * TABW] = t6 ^ x3;
+            t[10 * TABW] = t7 ^ x3;
+        }
+        __syncthreads();
+        if (warp < JT / 32 + (JT % 32 != 0)) {
+            // Lanes past JT (warp 9, lanes 24..31) read in-bounds words and keep no result. A
+            // warp loads 32 entries at once and broadcasts them, so the word loads of 32
+            // entries are in flight together.
+            const uint32_t *p = sm + tid;
+            const uint16_t *L = lists + (j & 1) * NIB;
+            const int cnt = counts[j & 1];
+            int i0 = 0;
+            for (; i0 + 32 <= cnt; i0 += 32) {
+                const uint32_t mine = L[i0 + lane];
 #pragma unroll
-                for (int d = 0; d < JW; d++) acc[d] ^= p[o0 + JT * d] ^ p[o1 + JT * d] ^ p[o2 + JT * d] ^ p[o3 + JT * d];
+                for (int e = 0; e < 32; e++) {
+                    const uint32_t o = __shfl_sync(0xffffffffu, mine, e);
+#pragma unroll
+                    for (int d = 0; d < JW; d++) acc[d] ^= p[o + JT * d];
+                }
             }
-            for (; i < cnt; i++) {
-                const uint32_t o = L[i];
+            if (i0 < cnt) {
+                const uint32_t mine = i0 + lane < cnt ? L[i0 + lane] : 0u;
+                for (int e = 0; e < cnt - i0; e++) {
+                    const uint32_t o = __shfl_sync(0xffffffffu, mine, e);
 #pragma unroll
-                for (int d = 0; d < JW; d++) acc[d] ^= p[o + JT * d];
+                    for (int d = 0; d < JW; d++) acc[d] ^= p[o + JT * d];
+                }
             }
         }
     }
@@ -460,7 +508,7 @@ __device__ void jump_window(uint32_t *ring, uint16_t (*list)[PHASE], int *count,
     b += dist;
     if (tid < JT) {
 #pragma unroll
-        for (int d = 0; d < JW; d++) put(ring, (uint32_t)b + (uint32_t)(tid + JT * d), acc[d]);
+        for (int d = 0; d < JW; d++) put(sm, (uint32_t)b + (uint32_t)(tid + JT * d), acc[d]);
     }
     P = b + MT_N;
     __syncthreads();
@@ -472,9 +520,8 @@ __device__ void jump_window(uint32_t *ring, uint16_t (*list)[PHASE], int *count,
 // turn of the loop (nine conversion warps), while the following turn is made. The CTA whose
 // chunks hold the block of the last consumed word copies out the end state.
 __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
-    __shared__ uint32_t ring[2 * RING];
-    __shared__ __align__(8) uint16_t list[3][PHASE];
-    __shared__ int count[3];
+    extern __shared__ __align__(16) uint32_t sm[];
+    uint32_t *ring = sm;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 
     const uint32_t left = a.st_in[MT_N];
@@ -512,7 +559,7 @@ __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
             P += cnt;
         }
         b = G;
-        jump_window(ring, list, count, a.tab + (size_t)c0 * 2 * PW, b, P, c0 * CHUNK);
+        jump_window(sm, a.tab + (size_t)c0 * 2 * PW, b, P, c0 * CHUNK);
     }
     // Phases start at P = pos (mod 64), so that each one holds nine whole mask words.
     const int align = (int)((pos - P) & 63);
@@ -609,6 +656,24 @@ int device_table(int need, const uint32_t **tab) {
     return DC_OK;
 }
 
+// The kernel's shared memory (above the 48 KB default), granted once per device.
+int allow_keep_smem() {
+    static std::mutex mu;
+    static bool done[kTableDevices];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "dropout: current device");
+    if (dev < 0 || dev >= kTableDevices)
+        return fail(DC_ERR_UNSUPPORTED, "dropout: device ordinal " + std::to_string(dev) + " is above 63");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+        e = cudaFuncSetAttribute(keep_bits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_WORDS * 4);
+        if (e != cudaSuccess) return cuda_fail(e, "dropout: keep-bits shared memory");
+        done[dev] = true;
+    }
+    return DC_OK;
+}
+
 }  // namespace
 
 // Elements per launch: MAX_CHUNKS - 2 chunks of words (one chunk may be taken by the head and
@@ -635,6 +700,8 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
     if (st) return st;
     int *err = device_error_word();
     if (!err) return fail(DC_ERR_CUDA, "device error word is unavailable");
+    st = allow_keep_smem();
+    if (st) return st;
     // keep iff m * 2^-53 < keep_prob  <=>  m < ceil(keep_prob * 2^53) (the scaling is exact)
     const uint64_t thresh = (uint64_t)ceil(keep_prob * 9007199254740992.0);
     uint32_t *tmp = nullptr;
@@ -654,7 +721,7 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
         const int64_t grid = imin(1 + (2 * ne - 1) / CHUNK, sms > 0 ? sms : 1);  // >= the chunks' count
         {
             KernelTrace tr("dropout_keep_bits", stream);
-            keep_bits_kernel<<<(unsigned)grid, THREADS, 0, stream>>>(a);
+            keep_bits_kernel<<<(unsigned)grid, THREADS, SMEM_WORDS * 4, stream>>>(a);
         }
         st = check_launch("dropout keep bits");
         if (st) {

@@ -27,7 +27,7 @@ from densecore_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-CHUNK_ELEMS = 624 * 840 // 2  # elements per chunk of the parallel walk
+CHUNK_ELEMS = 624 * 210 // 2  # elements per chunk of the parallel walk
 
 
 def _device_bits(state, n, keep_prob, in_place=False):

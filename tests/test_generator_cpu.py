@@ -12,7 +12,7 @@ import oracle
 from densecore_b200 import _lib
 
 _U32P = ctypes.POINTER(ctypes.c_uint32)
-CHUNK = 624 * 840  # words per chunk of the library's parallel walk
+CHUNK = 624 * 210  # words per chunk of the library's parallel walk
 
 
 def _skip(state, outputs):
@@ -39,9 +39,9 @@ def test_skip_matches_sequential_generation(seed, pre, n):
 
 
 def test_skip_beyond_one_table_reach():
-    # More than 1024 chunks: the host walk chains its largest jump.
+    # More chunks than the jump table holds (2048): the host walk chains its largest jump.
     g = oracle.MtGenerator(21)
-    n = 1030 * CHUNK + 999
+    n = 2100 * CHUNK + 999
     got = _skip(g.state.copy(), n)
     g.discard(n)
     assert np.array_equal(got, g.state)
