@@ -83,7 +83,9 @@ static_assert(2 * TURN + MT_N <= RING, "a turn must not overwrite words still be
 
 __host__ __device__ __forceinline__ int64_t imin(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ uint32_t twist(uint32_t u, uint32_t v) {
-    return (((u & UMASK) | (v & LMASK)) >> 1) ^ ((v & 1u) ? MATRIX_A : 0u);
+    // (v & 1) * MATRIX_A selects the constant with a multiply (the FMA pipe on the device; the
+    // integer ALU pipe is the kernel's busiest)
+    return (((u & UMASK) | (v & LMASK)) >> 1) ^ ((v & 1u) * MATRIX_A);
 }
 __host__ __device__ __forceinline__ uint32_t temper(uint32_t y) {
     y ^= y >> 11;
@@ -401,12 +403,19 @@ __device__ __forceinline__ void load_pair(const uint32_t *ring, uint32_t slot, u
     lo = ring[s + 1];  // s + 1 <= RING: the mirror
 }
 
-// Stores mask word q from the untempered pair (hi, lo) of each lane. One warp, all lanes.
+// Stores mask word q from the untempered pair (hi, lo) of each lane. The draw is
+// m = (temper(hi) & (2^21 - 1)) 2^32 + temper(lo), kept when m < thresh: the high 21 bits
+// decide unless they equal those of thresh (probability 2^-21), so the low word is tempered
+// only then. Elements past n are cleared in the last word. One warp, all lanes.
 __device__ __forceinline__ void store_word(const KeepArgs &a, uint32_t hi, uint32_t lo, int64_t q, int lane) {
-    const uint32_t hi32 = temper(hi), lo32 = temper(lo);
-    const uint64_t m = ((uint64_t)(hi32 & 0x1fffffu) << 32) | lo32;
-    const uint32_t word = __ballot_sync(0xffffffffu, 32 * q + lane < a.n && m < a.thresh);
-    if (lane == 0) a.bits[q] = word;
+    const uint32_t th_hi = (uint32_t)(a.thresh >> 32), h = temper(hi) & 0x1fffffu;
+    bool keep = h < th_hi;
+    if (h == th_hi) keep = temper(lo) < (uint32_t)a.thresh;
+    uint32_t word = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) {
+        if (q == a.nmask - 1 && (a.n & 31)) word &= (1u << (a.n & 31)) - 1u;
+        a.bits[q] = word;
+    }
 }
 
 // The nonzero nibbles of jump block j (coefficients PHASE j .. PHASE j + PHASE - 1 of g), as
