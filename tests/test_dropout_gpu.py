@@ -67,6 +67,25 @@ def test_keep_bits_edge_probabilities(keep_prob):
     assert full.all() if keep_prob == 1.0 else not full.any()
 
 
+@pytest.mark.parametrize("e0", [5, 700, 3 * CHUNK_ELEMS + 17])
+def test_keep_bits_threshold_ties(e0):
+    # The device decides most draws on the high 21 bits alone and tempers the low word only
+    # when those equal the threshold's: put the threshold on draw e0 (just above and exactly
+    # at it), so e0 takes that path, in the first chunk and past a jump.
+    g = oracle.MtGenerator(17).discard(3)
+    n = 4 * CHUNK_ELEMS
+    words = oracle.MtGenerator(17).discard(3).random(2 * e0 + 2)
+    m = (int(words[2 * e0]) & 0x1FFFFF) << 32 | int(words[2 * e0 + 1])
+    for thresh, kept in ((m + 1, True), (m, False)):
+        keep_prob = thresh / 2.0 ** 53  # exact: thresh < 2^53
+        bits, state = _device_bits(g.state.copy(), n, keep_prob)
+        gg = oracle.MtGenerator(17).discard(3)
+        ref = gg.keep_bits(n, keep_prob)
+        assert np.array_equal(bits, ref)
+        assert np.array_equal(state, gg.state)
+        assert bool((bits[e0 // 32] >> (e0 % 32)) & 1) == kept
+
+
 def test_keep_bits_in_place_state():
     g = oracle.MtGenerator(8).discard(5)
     n = 2 * CHUNK_ELEMS + 1
