@@ -94,6 +94,16 @@ def test_keep_bits_in_place_state():
     assert np.array_equal(state, g.state)
 
 
+def test_keep_bits_across_launches():
+    # Past (2048 - 2) chunks of words one call takes a second launch, which starts from the
+    # first launch's end state (in place: through the library's temporary state copies).
+    g = oracle.MtGenerator(12).discard(77)
+    n = 2046 * CHUNK_ELEMS + 12_345
+    bits, state = _device_bits(g.state.copy(), n, 0.75, in_place=True)
+    assert np.array_equal(bits, g.keep_bits(n, 0.75))
+    assert np.array_equal(state, g.state)
+
+
 def test_invalid_state_is_reported_not_used():
     L = _lib.load()
     L.dc_device_status(1)
