@@ -186,7 +186,9 @@ DC_API int dc_rng_skip(const uint32_t *state_in, uint64_t outputs, uint32_t *sta
  * keep_scale when bit ((b*H + h)*L + i)*S + j of keep_bits is set and by 0 otherwise (the
  * mask of dc_dropout_keep_bits over B*H*L*S elements; keep_scale = float32(1) /
  * float32(1 - p), as _dropout_noise divides). lse is the logsumexp of the undropped scores.
- * Runs the CUDA-core fp32 kernels whatever the precision (which is still validated).
+ * Shapes that dc_sdpa_fwd gives the tensor-core kernels take them here too, with the keep
+ * bits applied to the weights inside; every other shape (the q_len = 1 decode shapes
+ * included) takes the CUDA-core fp32 kernel, whatever the precision.
  * Replaces the math path of scaled_dot_product_attention with dropout (functional.py:318-340). */
 DC_API int dc_sdpa_fwd_dropout(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
                                const dc_tensor_t *mask, int causal, int has_scale, double scale,
@@ -194,7 +196,9 @@ DC_API int dc_sdpa_fwd_dropout(const dc_tensor_t *q, const dc_tensor_t *k, const
                                dc_tensor_t *out, dc_tensor_t *lse, void *stream);
 
 /* The backward of dc_sdpa_fwd_dropout (same keep_bits and keep_scale; out and lse from it):
- * dV = (P Z)^T dO, dS = P (Z (dO V^T) - rowsum(dO * out)) with Z the dropout factors. */
+ * dV = (P Z)^T dO, dS = P (Z (dO V^T) - rowsum(dO * out)) with Z the dropout factors. The
+ * kernels are chosen as dc_sdpa_bwd chooses them (tensor cores unless DC_PREC_FP32 or an
+ * unsupported shape). */
 DC_API int dc_sdpa_bwd_dropout(const dc_tensor_t *grad_out, const dc_tensor_t *q,
                                const dc_tensor_t *k, const dc_tensor_t *v, const dc_tensor_t *out,
                                const dc_tensor_t *lse, const dc_tensor_t *mask, int causal,
