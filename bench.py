@@ -390,6 +390,27 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # The timed forward + backward steps replay a CUDA graph of one step (every kernel of the
+    # step is launched by each replay): small workloads would otherwise wait on the host's
+    # launches. Dropout (its generator state and temporary copies), decode and the ring (NCCL)
+    # run eagerly.
+    timed_step = step
+    launch = "eager"
+    if w["bwd"] and not w.get("dropout") and ring is None:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        timed_step = graph.replay
+        launch = "cuda graph of one step"
+        for _ in range(2):
+            timed_step()
+        torch.cuda.synchronize()
 
     def barrier():
         if dist is not None:
@@ -398,19 +419,27 @@ def main():
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    _lib.kernel_timing_report(reset=True)
     barrier()
     with ClockSampler(physical_gpu(local)) as clocks:
-        _lib.kernel_timing(True)
         for i in range(args.steps):
             flush.zero_()
             starts[i].record()
-            step()
+            timed_step()
             ends[i].record()
         torch.cuda.synchronize()
-        _lib.kernel_timing(False)
     barrier()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    # The per-kernel breakdown (and the roofline's kernel durations) comes from a second pass
+    # of the same steps with the library's tracing on: it records two CUDA events around every
+    # launch, host work that would otherwise sit inside the timed steps of small workloads.
+    _lib.kernel_timing_report(reset=True)
+    _lib.kernel_timing(True)
+    for i in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    _lib.kernel_timing(False)
+    barrier()
     kernels = _lib.kernel_timing_report(reset=True)
     ms_max = ms
     if dist is not None:
@@ -485,7 +514,9 @@ def main():
                            "per_rank": ("zig-zag sequence shard (ring attention, NCCL send/recv)"
                                         if ring is not None else "full workload (weak scaling)"),
                            "parallelism": f"ring{world}" if ring is not None else f"dp{world}",
-                           "precision": args.precision, "l2": "flushed (256 MB write) before every timed step"},
+                           "precision": args.precision, "l2": "flushed (256 MB write) before every timed step",
+                           "launch": launch,
+                           "kernel_breakdown": "a second, untimed pass of the same steps with per-launch tracing"},
                 "roofline": roofline, "kernels": {k_: {"launches": v_[0], "total_ms": v_[1]}
                                                   for k_, v_ in kernels.items()},
                 "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cb, "clocks": clocks.summary()}
