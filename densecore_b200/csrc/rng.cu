@@ -25,8 +25,8 @@
 //     CTA owns the 32-element mask words whose first word lies in its run. A run that starts
 //     at chunk c >= 1 is reached by one jump with x^(c J) mod phi (a table computed on the
 //     host as needed, 2048 entries at most); the CTA then makes 576 words per phase in a
-//     mirrored 4096-word shared ring (three words per thread, chained at distance 227), two
-//     phases per CTA barrier, while other warps turn the words of the previous two phases
+//     mirrored 4096-word shared ring (three words per thread, chained at distance 227), three
+//     phases per CTA barrier, while other warps turn the words of the previous three phases
 //     into keep bits;
 //   * the CTA whose run holds the block of the last consumed word writes the new state in
 //     DenseCore's form (that block, left = 625 - next, next = words of it consumed).
@@ -57,9 +57,9 @@ constexpr int LAG = MT_N - MT_M;            // 227: X[k] = X[k - LAG] ^ twist(X[
 constexpr int RING = 4096;                  // shared ring of state words (power of two), mirrored
 constexpr int PHASE = 576;                  // words generated per barrier (nine 64-word mask words)
 constexpr int GEN_WARPS = (LAG + 31) / 32;  // 8: thread t < LAG makes three chained words a phase
-constexpr int TURN = 2 * PHASE;             // words per CTA barrier: two phases, the generating
-                                            // warps syncing among themselves between them
-constexpr int CONV_WARPS = PHASE / 64;      // 9: two mask words (one element per lane) a turn each
+constexpr int NPH = 3;                      // phases per CTA barrier (the generating warps sync
+constexpr int TURN = NPH * PHASE;           // among themselves between them): words per turn
+constexpr int CONV_WARPS = PHASE / 64;      // 9: NPH mask words (one element per lane) a turn each
 constexpr int WARPS = GEN_WARPS + CONV_WARPS;
 constexpr int THREADS = WARPS * 32;         // 544
 constexpr int JW = 2;                       // window words per thread in a jump
@@ -525,8 +525,8 @@ __device__ void jump_window(uint32_t *sm, const uint32_t *__restrict__ g, int64_
 
 // CTA c of K owns the chunks [c nch / K, (c + 1) nch / K) of the call's nch chunks: it reaches
 // the first one's start by one jump (none for chunk 0), then makes TURN words per CTA barrier
-// (eight generating warps) and turns each turn's words into eighteen mask words in the next
-// turn of the loop (nine conversion warps), while the following turn is made. The CTA whose
+// (eight generating warps) and turns each turn's words into 9 NPH mask words in the next turn
+// of the loop (nine conversion warps), while the following turn is made. The CTA whose
 // chunks hold the block of the last consumed word copies out the end state.
 __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
     extern __shared__ __align__(16) uint32_t sm[];
@@ -589,11 +589,11 @@ __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
     if (owns_end && E + MT_N > target) target = E + MT_N;
     const int64_t nturn = target > P ? (target - P + TURN - 1) / TURN : 0;
     bool captured = !owns_end;
-    // Turn u: copy out the end state once its block is made; the generating warps make the two
-    // phases [P, P + PHASE) and [P + PHASE, P + TURN) (a named barrier of their own between
-    // them; the slots written are those of words at least RING - TURN below P: neither read
-    // nor copied here) while each conversion warp turns two mask words of the words of turn
-    // u - 1 ([P - TURN, P)), two independent chains.
+    // Turn u: copy out the end state once its block is made; the generating warps make the NPH
+    // phases of [P, P + TURN) (a named barrier of their own between them; the slots written are
+    // those of words at least RING - TURN below P: neither read nor copied here) while each
+    // conversion warp turns NPH mask words of the words of turn u - 1 ([P - TURN, P)), NPH
+    // independent chains.
     const int cw = warp - GEN_WARPS;
     int64_t qw = (P - pos) / 64 + cw;  // this conversion warp's first mask word in turn 1
     uint32_t slot = (uint32_t)(pos + 64 * qw) + 2u * (uint32_t)lane;
@@ -610,20 +610,27 @@ __global__ void __launch_bounds__(THREADS) keep_bits_kernel(KeepArgs a) {
         }
         if (warp < GEN_WARPS) {
             if (u < nturn) {
-                gen_words(ring, P32, PHASE);
-                asm volatile("bar.sync 1, %0;" ::"r"(GEN_WARPS * 32) : "memory");
-                gen_words(ring, P32 + PHASE, PHASE);
+#pragma unroll
+                for (int f = 0; f < NPH; f++) {
+                    if (f > 0) asm volatile("bar.sync 1, %0;" ::"r"(GEN_WARPS * 32) : "memory");
+                    gen_words(ring, P32 + (uint32_t)(f * PHASE), PHASE);
+                }
             }
         } else if (u > 0) {
-            const int64_t q1 = qw + CONV_WARPS;
-            const bool t0 = qw >= q_lo && qw < q_hi, t1 = q1 >= q_lo && q1 < q_hi;
-            uint32_t h0 = 0u, l0 = 0u, h1 = 0u, l1 = 0u;
-            if (t0) load_pair(ring, slot, h0, l0);
-            if (t1) load_pair(ring, slot + 64u * CONV_WARPS, h1, l1);
-            if (t0) store_word(a, h0, l0, qw, lane);
-            if (t1) store_word(a, h1, l1, q1, lane);
-            qw += 2 * CONV_WARPS;
-            slot += 128u * CONV_WARPS;
+            uint32_t hi[NPH], lo[NPH];
+#pragma unroll
+            for (int f = 0; f < NPH; f++) {
+                const int64_t q = qw + f * CONV_WARPS;
+                hi[f] = lo[f] = 0u;
+                if (q >= q_lo && q < q_hi) load_pair(ring, slot + 64u * CONV_WARPS * (uint32_t)f, hi[f], lo[f]);
+            }
+#pragma unroll
+            for (int f = 0; f < NPH; f++) {
+                const int64_t q = qw + f * CONV_WARPS;
+                if (q >= q_lo && q < q_hi) store_word(a, hi[f], lo[f], q, lane);
+            }
+            qw += NPH * CONV_WARPS;
+            slot += 64u * NPH * CONV_WARPS;
         }
         __syncthreads();
         P += TURN;
