@@ -25,8 +25,8 @@
 //     CTA owns the 32-element mask words whose first word lies in its run. A run that starts
 //     at chunk c >= 1 is reached by one jump with x^(c J) mod phi (a table computed on the
 //     host as needed, 2048 entries at most); the CTA then makes 576 words per phase in a
-//     mirrored 4096-word shared ring (three words per thread, chained at distance 227), three
-//     phases per CTA barrier, while other warps turn the words of the previous three phases
+//     mirrored 8192-word shared ring (three words per thread, chained at distance 227), four
+//     phases per CTA barrier, while other warps turn the words of the previous four phases
 //     into keep bits;
 //   * the CTA whose run holds the block of the last consumed word writes the new state in
 //     DenseCore's form (that block, left = 625 - next, next = words of it consumed).
@@ -54,10 +54,10 @@ constexpr int PW = (DEG + 63) / 64;         // 64-bit words of a reduced polynom
 constexpr int64_t CHUNK = 624LL * 210;      // words per chunk (131,040): runs of chunks balance CTAs
 constexpr int MAX_CHUNKS = 2048;            // jump table entries x^(c J), c < MAX_CHUNKS
 constexpr int LAG = MT_N - MT_M;            // 227: X[k] = X[k - LAG] ^ twist(X[k - 624], X[k - 623])
-constexpr int RING = 4096;                  // shared ring of state words (power of two), mirrored
+constexpr int RING = 8192;                  // shared ring of state words (power of two), mirrored
 constexpr int PHASE = 576;                  // words generated per barrier (nine 64-word mask words)
 constexpr int GEN_WARPS = (LAG + 31) / 32;  // 8: thread t < LAG makes three chained words a phase
-constexpr int NPH = 3;                      // phases per CTA barrier (the generating warps sync
+constexpr int NPH = 4;                      // phases per CTA barrier (the generating warps sync
 constexpr int TURN = NPH * PHASE;           // among themselves between them): words per turn
 constexpr int CONV_WARPS = PHASE / 64;      // 9: NPH mask words (one element per lane) a turn each
 constexpr int WARPS = GEN_WARPS + CONV_WARPS;
