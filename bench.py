@@ -531,7 +531,7 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
     pinned host memory and its outputs (out and, with a backward, the three gradients) back.
     Steps are pipelined the way a training or serving loop would run them: step i+1's inputs go
     up on one stream while step i computes on a second and step i-1's results come down on a
-    third (two buffer slots, events guarding their reuse)."""
+    third (three buffer slots, events guarding their reuse, the host at most three steps ahead)."""
     import densecore_b200 as dc
     ins = [q, k, v] + ([g] if g is not None else [])
     if w["cfg"] == 5:
@@ -544,7 +544,7 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
         outs_shape = [tuple(w["q"]), tuple(w["q"]), tuple(w["kv"]), tuple(w["kv"])]
     else:
         outs_shape = [tuple(w["q"])]
-    nslot = 2
+    nslot = 3  # a slot's copy back can overlap the next two steps' copies up and compute
     host_in = [[t.detach().cpu().pin_memory() for t in ins] for _ in range(nslot)]
     dev_in = [[torch.empty_like(t) for t in ins] for _ in range(nslot)]
     host_out = [[torch.empty(s_, dtype=torch.float32).pin_memory() for s_ in outs_shape] for _ in range(nslot)]
@@ -573,6 +573,12 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
 
     def step(i):
         sl = i % nslot
+        if used[sl]:
+            # The host stays at most nslot steps ahead, as a loop that reads its results back
+            # does: the slot's previous results are on the host before its buffers are reused
+            # (an event wait, not a device synchronisation: the other slot's step keeps the
+            # copy engines and the GPU busy meanwhile).
+            ev_out[sl].synchronize()
         with torch.cuda.stream(s_h2d):
             if used[sl]:
                 s_h2d.wait_event(ev_used[sl])  # the slot's previous compute read its inputs
@@ -593,21 +599,29 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
             ev_out[sl].record(s_d2h)
         used[sl] = True
 
-    for i in range(args.warmup):
+    # Results freed on the compute stream stay reserved until their copy stream is done with
+    # them, so the caching allocator grows over the first pipelined steps; a cudaMalloc inside
+    # the timed steps would stall the pipeline. With the host at most nslot steps ahead the
+    # warm-up reaches its steady state; the allocations left inside the timed steps are
+    # reported.
+    warm = max(args.warmup, 12)
+    for i in range(warm):
         step(i)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
+    allocs0 = torch.cuda.memory_stats(device).get("num_device_alloc", 0)
     cur = torch.cuda.current_stream(device)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(cur)
     s_h2d.wait_event(s)
     for i in range(args.steps):
-        step(args.warmup + i)
+        step(warm + i)
     for sl in range(nslot):
         cur.wait_event(ev_out[sl])
     e.record(cur)
     torch.cuda.synchronize()
+    allocs = torch.cuda.memory_stats(device).get("num_device_alloc", 0) - allocs0
     ms = s.elapsed_time(e) / args.steps
     world = 1
     if dist is not None:
@@ -619,7 +633,8 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
         world = 1  # the ranks share one sequence
     return {"value": world * amount / (ms / 1e3) / scale, "unit": "GB/s" if scale == 1e9 else "TFLOP/s",
             "ms_per_step": ms, "h2d_bytes_per_step": sum(t.numel() * 4 for t in host_in[0]),
-            "d2h_bytes_per_step": sum(t.numel() * 4 for t in host_out[0]), "pipelined": True}
+            "d2h_bytes_per_step": sum(t.numel() * 4 for t in host_out[0]), "pipelined": True,
+            "warmup_steps": warm, "device_allocs_in_timed_steps": allocs}
 
 
 if __name__ == "__main__":
