@@ -35,8 +35,10 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -304,16 +306,42 @@ JumpTables &tables() {
 }
 
 // Makes entries 0 .. need - 1 (need <= MAX_CHUNKS) available; returns the table.
+// Entries are x^(c J) = x^((c - 1) J) * x^J, one multiplication each (about a millisecond).
+// Many new entries are shared out over host threads: each thread starts its range with
+// x^(c0 J) by square-and-multiply and writes disjoint entries.
 const uint64_t *table_upto(JumpTables &T, int need) {
     std::lock_guard<std::mutex> lock(T.mu);
-    while (T.count < need) {
-        const int c = T.count;
-        Poly r = c == 1 ? T.f.powx((uint64_t)CHUNK)
-                        : T.f.mul(Poly(T.t.begin() + (size_t)(c - 1) * PW, T.t.begin() + (size_t)c * PW),
-                                  Poly(T.t.begin() + PW, T.t.begin() + 2 * PW));
-        memcpy(&T.t[(size_t)c * PW], r.data(), PW * 8);
-        T.count = c + 1;
+    if (T.count >= need) return T.t.data();
+    auto entry = [&](int c) { return Poly(T.t.begin() + (size_t)c * PW, T.t.begin() + (size_t)(c + 1) * PW); };
+    auto store = [&](int c, const Poly &r) { memcpy(&T.t[(size_t)c * PW], r.data(), PW * 8); };
+    if (T.count < 2) {
+        store(1, T.f.powx((uint64_t)CHUNK));
+        T.count = 2;
     }
+    const int from = T.count, todo = need - from;
+    if (todo <= 0) return T.t.data();
+    const Poly xj = entry(1);
+    auto run = [&](int a, int b) {  // entries [a, b)
+        Poly cur = a - 1 < from ? T.f.mul(entry(a - 1), xj) : T.f.powx((uint64_t)a * (uint64_t)CHUNK);
+        store(a, cur);
+        for (int c = a + 1; c < b; c++) {
+            cur = T.f.mul(cur, xj);
+            store(c, cur);
+        }
+    };
+    const unsigned hw = std::thread::hardware_concurrency();
+    const int nth = (int)std::min<int64_t>({(int64_t)todo / 64, hw > 0 ? (int64_t)hw : 1, 16});
+    if (nth <= 1) {
+        run(from, need);
+    } else {
+        std::vector<std::thread> pool;
+        for (int i = 0; i < nth; i++) {
+            const int a = from + (int)((int64_t)todo * i / nth), b = from + (int)((int64_t)todo * (i + 1) / nth);
+            if (a < b) pool.emplace_back(run, a, b);
+        }
+        for (auto &t : pool) t.join();
+    }
+    T.count = need;
     return T.t.data();
 }
 

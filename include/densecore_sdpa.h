@@ -172,8 +172,8 @@ DC_API int dc_attn_probs(const dc_tensor_t *q, const dc_tensor_t *k, const dc_te
  * state after the 2n outputs is written to state_out (which may equal state_in). A state
  * whose `left` is not in 1..624 sets dc_device_status() to 2 and writes nothing.
  * The first call in a process computes the generator's jump tables on the host (a fraction
- * of a second), and the first call on each device copies them there with synchronous copies:
- * make that call before any stream capture. */
+ * of a second, on up to 16 host threads), and the first call on each device copies them there
+ * with synchronous copies: make that call before any stream capture. */
 DC_API int dc_dropout_keep_bits(const uint32_t *state_in, uint32_t *state_out, int64_t n,
                                 double keep_prob, uint32_t *bits, void *stream);
 
