@@ -578,9 +578,13 @@ __global__ void __maxnreg__(168)
             float mk[MASKED ? CPT : 1];
             if constexpr (MASKED) mask_run<CPT>(p, b, h, base, key, p.ms[2], vbits, mk);
             // Dropout: the keep bits of (query base + c, this key). The weights that meet dO are
-            // P * Z; dS = P (Z dP - delta), Z = keep_scale where kept, 0 where dropped.
+            // P * Z; dS = P (Z dP - delta), Z = keep_scale where kept, 0 where dropped. The
+            // warp's lanes are 32 consecutive keys: one row read per lane, transposed by ballots.
             uint32_t zb = 0;
-            if constexpr (DROP) zb = key_ok ? keep_col<CPT>(p, b, h, base, key) : 0u;
+            if constexpr (DROP) {
+                zb = transpose_bits32(lane < CPT ? keep_run32(p, b, h, base + lane, key - lane) : 0u, lane);
+                if (!key_ok) zb = 0u;  // every lane took part in the ballots
+            }
             if (!warp_wait(bar(C::S_FULL), i & 1, abort, err)) {
                 ok = false;
                 break;

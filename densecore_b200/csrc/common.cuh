@@ -127,22 +127,18 @@ __device__ __forceinline__ uint32_t keep_run32(const AttnProblem &p, int64_t b, 
     return __funnelshift_r(lo, hi, (uint32_t)(e & 31));
 }
 
-// Dropout keep bits of the weights (b, h, i0 + c, j), c = 0..N-1 (down one key's column), bit c.
-template <int N>
-__device__ __forceinline__ uint32_t keep_col(const AttnProblem &p, int64_t b, int64_t h, int64_t i0, int64_t j) {
-    static_assert(N <= 32, "one word of bits");
-    const int64_t nw = (p.B * p.H * p.L * p.S + 31) >> 5;
-    const int64_t e0 = ((b * p.H + h) * p.L + i0) * p.S + j;
-    uint32_t words[N];
+// Dropout keep bits down key columns, for a warp whose lane l owns key j0 + l: lane r holds
+// w_r = keep_run32(row i0 + r, keys j0 .. j0 + 31) and gets back bit c = bit r of w_c, i.e.
+// lane l's bits over rows i0 + c. 32 ballots transpose the 32 x 32 bit block, so a warp reads
+// one word pair per lane instead of one word per (row, lane). All 32 lanes must call it.
+__device__ __forceinline__ uint32_t transpose_bits32(uint32_t w, int lane) {
+    uint32_t mine = 0;
 #pragma unroll
-    for (int c = 0; c < N; c++) {
-        const int64_t w = (e0 + c * p.S) >> 5;
-        words[c] = w < nw ? __ldg(p.keep + w) : 0u;
+    for (int j = 0; j < 32; j++) {
+        const uint32_t col = __ballot_sync(0xffffffffu, (w >> j) & 1u);
+        mine = lane == j ? col : mine;
     }
-    uint32_t bits = 0;
-#pragma unroll
-    for (int c = 0; c < N; c++) bits |= ((words[c] >> ((e0 + c * p.S) & 31)) & 1u) << c;
-    return bits;
+    return mine;
 }
 
 // Whether key j is visible to query row i under top-left causal alignment.
