@@ -128,17 +128,23 @@ __device__ __forceinline__ uint32_t keep_run32(const AttnProblem &p, int64_t b, 
 }
 
 // Dropout keep bits down key columns, for a warp whose lane l owns key j0 + l: lane r holds
-// w_r = keep_run32(row i0 + r, keys j0 .. j0 + 31) and gets back bit c = bit r of w_c, i.e.
-// lane l's bits over rows i0 + c. 32 ballots transpose the 32 x 32 bit block, so a warp reads
-// one word pair per lane instead of one word per (row, lane). All 32 lanes must call it.
+// w_r = keep_run32(row i0 + r, keys j0 .. j0 + 31) and gets back the word whose bit c is bit l
+// of w_c, i.e. lane l's bits over rows i0 + c. The 32 x 32 bit block is transposed in five
+// butterfly stages: at stage j, lanes l and l ^ j swap the j x j sub-blocks off the diagonal of
+// each 2j x 2j block (a lane with bit j clear keeps the low j bits of every 2j-bit group and
+// takes its partner's low bits shifted up; the other keeps the high bits and takes its
+// partner's high bits shifted down). A warp reads one word pair per lane instead of one word
+// per (row, lane). All 32 lanes must call it.
 __device__ __forceinline__ uint32_t transpose_bits32(uint32_t w, int lane) {
-    uint32_t mine = 0;
+    constexpr uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
 #pragma unroll
-    for (int j = 0; j < 32; j++) {
-        const uint32_t col = __ballot_sync(0xffffffffu, (w >> j) & 1u);
-        mine = lane == j ? col : mine;
+    for (int s = 0; s < 5; s++) {
+        const int j = 16 >> s;
+        const uint32_t m = masks[s];
+        const uint32_t y = __shfl_xor_sync(0xffffffffu, w, j);
+        w = (lane & j) ? ((w & ~m) | ((y >> j) & m)) : ((w & m) | ((y << j) & ~m));
     }
-    return mine;
+    return w;
 }
 
 // Whether key j is visible to query row i under top-left causal alignment.
