@@ -224,7 +224,7 @@ def cpu_baseline(w, name, budget_s=12.0, threads=None):
     if w["cfg"] == 4:
         # Causal prefix sample: the first R rows of `heads` heads (keys <= row), extrapolated by
         # visible pairs; per-pair cost does not depend on the row.
-        R, heads = 4096, threads
+        R, heads = (4096 if budget_s >= 10 else 2048), threads
         q, k, v = (rng.normal(size=(1, heads, R, D)).astype(np.float32) * w["amp"] for _ in range(3))
         t0 = time.perf_counter()
         oracle.flash_forward(q, k, v, causal=True, threads=threads)
@@ -283,6 +283,16 @@ def cpu_baseline(w, name, budget_s=12.0, threads=None):
                       f"({'fwd+bwd' if w['bwd'] else 'fwd'}), {dt:.1f} s"}
 
 
+def config_of(name, w, world, ring=False):
+    """The workload a line measures (both arms print the same dict for the same run)."""
+    return {"workload": name, "baseline_cfg": w["cfg"], "shape_q": list(w["q"]), "shape_kv": list(w["kv"]),
+            "causal": w["causal"], "mask": w["mask"], "dropout_p": w.get("dropout", 0.0),
+            "per_rank": ("zig-zag sequence shard (ring attention, NCCL send/recv)" if ring
+                         else "full workload (weak scaling)"),
+            "parallelism": f"ring{world}" if ring else f"dp{world}",
+            "l2": "GPU arm: flushed (256 MB write) before every timed step"}
+
+
 def run_reference(args, w, name, rank, world):
     """--impl reference: DenseCore's CPU algorithm (the oracle port; the Rust reference cannot
     be built here) on the host cores, each step a bounded sample of the workload."""
@@ -298,66 +308,46 @@ def run_reference(args, w, name, rank, world):
     value = statistics.mean(vals)
     _, unit = work(w)
     cb["value"] = value
+    ring = w["cfg"] == 4 and world > 1
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": name, "shape_q": list(w["q"]), "shape_kv": list(w["kv"]),
-                       "causal": w["causal"], "mask": w["mask"], "dropout_p": w.get("dropout", 0.0),
-                       "baseline_cfg": w["cfg"]},
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong" if ring else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) of the config's shape)",
+            "config": config_of(name, w, world, ring),
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="gpt2_causal_fwd_bwd", choices=sorted(WORKLOADS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32", "fp32"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true")
-    args = ap.parse_args()
-    if args.warmup < 3:
-        ap.error("--warmup must be >= 3")
-    name = args.workload
-    w = WORKLOADS[name]
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
-    if args.impl == "reference":
-        run_reference(args, w, name, rank, world)
-        return
+def _max_over_ranks(x, dist, device):
+    if dist is None:
+        return x
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
+
+def _barrier(dist):
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def measure(name, w, device, dist, steps, warmup, *, agg_amount=None, inputs=None, ring=None, e2e=False,
+            e2e_args=None, cpu=False, cpu_budget=12.0, clocks=False, seed=1234):
+    """One workload on this rank's GPU: W untimed steps, then K timed steps (CUDA events around
+    each, L2 flushed before each), max over ranks; a second, untimed pass of the same steps with
+    the library's per-launch tracing gives the kernel breakdown and the roofline's unit.
+    ``agg_amount`` is the algorithmic work all ranks do in one step together (default: this
+    rank's workload times the world size). Every rank must call this with the same arguments
+    (it takes barriers and all-reduces)."""
     import densecore_b200 as dc
     from densecore_b200 import _lib, _native
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-    dc.set_sdpa_precision(args.precision)
-    _lib.load()
-
-    # Config 4 on several GPUs is sequence-parallel (ring attention over zig-zag shards of one
-    # sequence: strong scaling); every other run gives each rank a whole workload (weak scaling).
-    ring = None
-    if w["cfg"] == 4 and world > 1:
-        from densecore_b200.ring import RingAttention, zigzag_shard
-        full = make_inputs(w, device, seed=1234)
-        q, k, v = (zigzag_shard(t, rank, world) for t in full[:3])
-        g, mask = None, None
-        del full
-        ring = RingAttention(q.shape, k.shape, device, causal=True)
+    if inputs is None:
+        q, k, v, g, mask = make_inputs(w, device, seed=seed)
     else:
-        q, k, v, g, mask = make_inputs(w, device, seed=1234 + rank)
+        q, k, v, g, mask = inputs
     causal = w["causal"]
     if ring is not None:
         def step():
@@ -372,7 +362,7 @@ def main():
     elif w.get("dropout"):
         from densecore_b200.functional import _keep_mask
         n_weights = q.shape[0] * q.shape[1] * q.shape[2] * k.shape[2]
-        dc.manual_seed(1234 + rank)
+        dc.manual_seed(seed)
 
         def step():
             keep, ks = _keep_mask(n_weights, w["dropout"], device)
@@ -387,7 +377,7 @@ def main():
             _native._flash_attention(q, k, v, causal, None, mask)
 
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MB > 126 MB L2
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     # The timed forward + backward steps replay a CUDA graph of one step (every kernel of the
@@ -396,6 +386,7 @@ def main():
     # run eagerly.
     timed_step = step
     launch = "eager"
+    graph = None
     if w["bwd"] and not w.get("dropout") and ring is None:
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
@@ -412,48 +403,63 @@ def main():
             timed_step()
         torch.cuda.synchronize()
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    with ClockSampler(physical_gpu(local)) as clocks:
-        for i in range(args.steps):
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    _barrier(dist)
+    local = device.index if device.index is not None else 0
+    sampler = ClockSampler(physical_gpu(local)) if clocks else None
+    if sampler is not None:
+        sampler.__enter__()
+    try:
+        for i in range(steps):
             flush.zero_()
             starts[i].record()
             timed_step()
             ends[i].record()
         torch.cuda.synchronize()
-    barrier()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
-    # The per-kernel breakdown (and the roofline's kernel durations) comes from a second pass
-    # of the same steps with the library's tracing on: it records two CUDA events around every
-    # launch, host work that would otherwise sit inside the timed steps of small workloads.
+    finally:
+        if sampler is not None:
+            sampler.__exit__(None, None, None)
+    _barrier(dist)
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / steps
+    # Per-kernel breakdown from a second pass of the same steps with the library's tracing on:
+    # it records two CUDA events around every launch, host work that would otherwise sit inside
+    # the timed steps of small workloads.
     _lib.kernel_timing_report(reset=True)
     _lib.kernel_timing(True)
-    for i in range(args.steps):
+    for i in range(steps):
         flush.zero_()
         step()
     torch.cuda.synchronize()
     _lib.kernel_timing(False)
-    barrier()
+    _barrier(dist)
     kernels = _lib.kernel_timing_report(reset=True)
-    ms_max = ms
-    if dist is not None:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    del graph
+    ms_max = _max_over_ranks(ms, dist, device)
+    world = dist.get_world_size() if dist is not None else 1
     amount, unit = work(w)
+    if agg_amount is None:
+        agg_amount = amount * world
     scale = 1e9 if unit == "GB/s" else 1e12
-    ranks_work = 1 if ring is not None else world  # strong scaling: the ranks share one workload
-    value = ranks_work * amount / (ms_max / 1e3) / scale
+    value = agg_amount / (ms_max / 1e3) / scale
+    roofline = roofline_of(name, w, kernels, steps, ring, world, agg_amount / world if ring is not None else amount)
+    launches = sum(v_[0] for k_, v_ in kernels.items() if k_ != "bwd_tc")  # bwd_tc spans two launches
+    res = {"ms_per_step": ms_max, "value": value, "unit": unit, "launch": launch, "roofline": roofline,
+           "kernels": {k_: {"launches": v_[0], "total_ms": v_[1]} for k_, v_ in kernels.items()},
+           "gpu_launches": launches}
+    if e2e:
+        res["e2e"] = run_e2e(w, q, k, v, g, mask, e2e_args, device, scale, agg_amount, dist, ring)
+    if cpu:
+        res["cpu_baseline"] = cpu_baseline(w, name, budget_s=cpu_budget)
+    if sampler is not None:
+        res["clocks"] = sampler.summary()
+    return res
 
-    # Roofline of the dominant kernel (largest total device time in the timed region). The
-    # tensor-core backward's dK/dV and dQ kernels share the GPU (two streams): their joint
-    # record "bwd_tc" is the unit, not either kernel alone.
+
+def roofline_of(name, w, kernels, steps, ring, world, rank_amount):
+    """Roofline of the dominant kernel (largest total device time in the traced pass). The
+    tensor-core backward's dK/dV and dQ kernels share the GPU (two streams): their joint record
+    "bwd_tc" is the unit, not either kernel alone."""
     pk = peaks()
     # Kernels without a roofline of their own (the dropout mask draw: integer generator work,
     # neither HBM- nor tensor-bound) are named in "slowest_kernel" but are not the unit.
@@ -462,64 +468,209 @@ def main():
     slowest = max(candidates.items(), key=lambda kv: kv[1][1])[0] if candidates else None
     candidates = {k_: v_ for k_, v_ in candidates.items() if kernel_work(w, k_) > 0 or ring is not None}
     dom = max(candidates.items(), key=lambda kv: kv[1][1]) if candidates else None
-    roofline = None
-    if dom is not None:
-        kname, (launches, total_ms) = dom
-        per_launch = kernel_work(w, kname)
-        avg_ms = total_ms / max(launches, 1)
-        if ring is not None:
-            # Ring launches differ in size; per step the rank's forward launches together do
-            # 1/world of the sequence's algorithmic flops.
-            per_launch = amount / world / (launches / args.steps)
-        if unit == "GB/s":
-            achieved = per_launch / (avg_ms / 1e3) / 1e9
-            peak, ru, bound = pk["hbm"], "GB/s", "hbm"
+    if dom is None:
+        return None
+    kname, (launches, total_ms) = dom
+    per_launch = kernel_work(w, kname)
+    avg_ms = total_ms / max(launches, 1)
+    if ring is not None:
+        # Ring launches differ in size; per step the rank's forward launches together do
+        # 1/world of the sequence's algorithmic flops.
+        per_launch = rank_amount / (launches / steps)
+    if kname == "decode_split" or w["cfg"] == 5:
+        achieved = per_launch / (avg_ms / 1e3) / 1e9
+        peak, ru, bound = pk["hbm"], "GB/s", "hbm"
+    else:
+        achieved = per_launch / (avg_ms / 1e3) / 1e12
+        # Dense TF32 on sm_100 issues at half the bf16 rate: half the measured bf16 burst.
+        peak, ru, bound = pk["bf16"] / 2.0, "TFLOP/s", "tensor"
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            per = json.load(f).get(name, {})
+        traffic = per.get(kname)
+        if kname == "bwd_tc" and traffic is None and "bwd_dkdv_tc" in per and "bwd_dq_tc" in per:
+            traffic = per["bwd_dkdv_tc"] + per["bwd_dq_tc"]
+    return {"kernel": kname, "slowest_kernel": slowest, "bound": bound, "achieved": achieved, "peak": peak,
+            "unit": ru, "frac": achieved / peak, "traffic": traffic, "avg_launch_ms": avg_ms,
+            "peak_source": (f"{pk['src']} hbm_gbs" if bound == "hbm"
+                            else f"{pk['src']} bf16_tflops / 2 (dense TF32 rate)")}
+
+
+# The other configs of the baseline, measured on one GPU beside the headline (short runs, the
+# CPU baseline on a short budget): (key, workload, precision).
+SINGLE_GPU_EXTRAS = (
+    ("cfg1_nanogpt", "nanogpt_causal_fwd_bwd", "3xtf32"),
+    ("cfg2_mha_core", "mha_core_fwd_bwd", "3xtf32"),
+    ("cfg3b_floatmask", "gpt2_floatmask_fwd_bwd", "3xtf32"),
+    ("cfg3_tf32", "gpt2_causal_fwd_bwd", "tf32"),
+    ("cfg4_long", "long_causal_fwd", "3xtf32"),
+    ("cfg5_decode", "decode_splitkv", "3xtf32"),
+)
+
+
+def single_gpu_extras(device, steps):
+    import densecore_b200 as dc
+    out = {}
+    for key, name, prec in SINGLE_GPU_EXTRAS:
+        dc.set_sdpa_precision(prec)
+        try:
+            w = WORKLOADS[name]
+            r = measure(name, w, device, None, steps, 3, cpu=prec == "3xtf32", cpu_budget=3.0)
+        finally:
+            dc.set_sdpa_precision(None)
+        r.update(workload=name, precision=prec)
+        out[key] = r
+        torch.cuda.empty_cache()
+    return out
+
+
+def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
+    """At N > 1: config 3 strong-scaled over its 96 (batch, head) units, config 4 through ring
+    attention (strong, with an in-run parity check), config 5 batch shards (strong)."""
+    from densecore_b200 import _native
+    from densecore_b200.ring import RingAttention, zigzag_shard
+    extras = {}
+
+    # Config 3: the 96 independent (batch, head) units of [8, 12, 1024, 64] split evenly over the
+    # ranks (12 per GPU at 8), as DenseCore's par_chunks splits them over threads
+    # (torch_attention.rs:108-128). Each rank's units are a (1, 96/N, 1024, 64) slice; e2e
+    # copies exactly that slice up from and its results back into pinned host buffers.
+    w3 = WORKLOADS["gpt2_causal_fwd_bwd"]
+    units = w3["q"][0] * w3["q"][1]
+    if units % world == 0:
+        per = units // world
+        wr = dict(w3, q=(1, per, 1024, 64), kv=(1, per, 1024, 64))
+        r = measure("gpt2_causal_fwd_bwd", wr, device, dist, steps, 3, agg_amount=work(w3)[0], e2e=True,
+                    e2e_args=e2e_args, seed=4321 + rank)
+        r.update(units_per_rank=per, scaling="strong",
+                 scatter_gather="each rank copies its units' q, k, v, dO from pinned host memory and its "
+                                "out, dq, dk, dv back (inside e2e's timed region)")
+        extras["cfg3_strong"] = r
+        torch.cuda.empty_cache()
+
+    # Config 4 through ring attention (strong scaling), next to the same forward on one GPU per
+    # rank (all ranks at once) for the fraction of N x one GPU, and a parity check of every
+    # rank's ring rows against single-GPU forwards of two heads over the whole sequence.
+    w4 = WORKLOADS["long_causal_fwd"]
+    S = w4["q"][2]
+    if S % (2 * world) == 0:
+        full = make_inputs(w4, device, seed=1234)
+        q, k, v = (zigzag_shard(t, rank, world) for t in full[:3])
+        ringa = RingAttention(q.shape, k.shape, device, causal=True)
+        r = measure("long_causal_fwd", w4, device, dist, steps, 3, agg_amount=work(w4)[0], inputs=(q, k, v, None, None),
+                    ring=ringa)
+        one = measure("long_causal_fwd", w4, device, dist, max(3, steps // 4), 3, agg_amount=work(w4)[0],
+                      inputs=full)
+        out, lse = ringa(q, k, v)
+        heads = [0, 9]
+        so, sl = _native._flash_attention(*(t[:, heads].contiguous() for t in full[:3]), True)
+        ref_o, ref_l = zigzag_shard(so, rank, world), zigzag_shard(sl.unsqueeze(-1), rank, world).squeeze(-1)
+        err_o = float((out[:, heads] - ref_o).abs().max() / ref_o.abs().max())
+        err_l = float((lse[:, heads] - ref_l).abs().max() / ref_l.abs().max())
+        err = _max_over_ranks(max(err_o, err_l), dist, device)
+        r.update(scaling="strong", one_gpu_ms=one["ms_per_step"], one_gpu_value=one["value"],
+                 frac_of_n_x_one_gpu=r["value"] / (world * one["value"]),
+                 parity={"max_rel_err": err, "tol": 1e-5, "ok": err <= 1e-5,
+                         "what": "every rank's ring out and lse, heads 0 and 9, against a single-GPU forward "
+                                 "of those heads over the whole sequence (max |delta| / max |ref|)"})
+        extras["ring_cfg4"] = r
+        del full, q, k, v, ringa, out, lse, so, sl
+        torch.cuda.empty_cache()
+
+    # Config 5: the batch of 64 decode rows split over the ranks (8 per GPU at 8); each rank
+    # streams its K/V shard (17.18 GB / N).
+    w5 = WORKLOADS["decode_splitkv"]
+    if w5["q"][0] % world == 0:
+        bpr = w5["q"][0] // world
+        wr = dict(w5, q=(bpr,) + w5["q"][1:], kv=(bpr,) + w5["kv"][1:])
+        r = measure("decode_splitkv", wr, device, dist, steps, 3, agg_amount=work(w5)[0], seed=999 + rank)
+        r.update(batch_per_rank=bpr, scaling="strong",
+                 frac_of_n_x_hbm=r["value"] / (world * peaks()["hbm"]))
+        extras["decode_shard"] = r
+        torch.cuda.empty_cache()
+    return extras
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="gpt2_causal_fwd_bwd", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="3xtf32", choices=["3xtf32", "tf32", "fp32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="only the headline workload")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    name = args.workload
+    w = WORKLOADS[name]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args, w, name, rank, world)
+        return
+
+    import densecore_b200 as dc
+    from densecore_b200 import _lib
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    dc.set_sdpa_precision(args.precision)
+    _lib.load()
+
+    # Config 4 on several GPUs is sequence-parallel (ring attention over zig-zag shards of one
+    # sequence: strong scaling); every other headline gives each rank a whole workload (weak
+    # scaling).
+    ring = None
+    inputs = None
+    agg = None
+    if w["cfg"] == 4 and world > 1:
+        from densecore_b200.ring import RingAttention, zigzag_shard
+        full = make_inputs(w, device, seed=1234)
+        q, k, v = (zigzag_shard(t, rank, world) for t in full[:3])
+        del full
+        inputs = (q, k, v, None, None)
+        ring = RingAttention(q.shape, k.shape, device, causal=True)
+        agg = work(w)[0]
+    head = measure(name, w, device, dist, args.steps, args.warmup, agg_amount=agg, inputs=inputs, ring=ring,
+                   e2e=not args.no_e2e, e2e_args=args, clocks=True, seed=1234 + rank,
+                   cpu=rank == 0 and world == 1 and not args.no_cpu_baseline)
+    del inputs, ring
+    torch.cuda.empty_cache()
+
+    extras = {}
+    if not args.no_extras and name == "gpt2_causal_fwd_bwd" and args.precision == "3xtf32":
+        if world == 1:
+            extras["configs"] = single_gpu_extras(device, min(args.steps, 10))
         else:
-            achieved = per_launch / (avg_ms / 1e3) / 1e12
-            # Dense TF32 on sm_100 issues at half the bf16 rate: half the measured bf16 burst.
-            peak, ru, bound = pk["bf16"] / 2.0, "TFLOP/s", "tensor"
-        traffic = None
-        tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
-        if os.path.exists(tpath):
-            with open(tpath) as f:
-                per = json.load(f).get(name, {})
-            traffic = per.get(kname)
-            if kname == "bwd_tc" and traffic is None and "bwd_dkdv_tc" in per and "bwd_dq_tc" in per:
-                traffic = per["bwd_dkdv_tc"] + per["bwd_dq_tc"]
-        roofline = {"kernel": kname, "slowest_kernel": slowest, "bound": bound, "achieved": achieved, "peak": peak,
-                    "unit": ru,
-                    "frac": achieved / peak, "traffic": traffic, "avg_launch_ms": avg_ms,
-                    "peak_source": (f"{pk['src']} hbm_gbs" if bound == "hbm"
-                                    else f"{pk['src']} bf16_tflops / 2 (dense TF32 rate)")}
-    launches = sum(v[0] for k_, v in kernels.items() if k_ != "bwd_tc")  # bwd_tc spans two launches
-
-    # End to end through the public API with pinned host buffers; copies in the timed region.
-    e2e = None
-    if not args.no_e2e:
-        e2e = run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring)
-
-    cb = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline(w, name)
+            extras.update(multi_gpu_extras(device, dist, rank, world, min(args.steps, 10), args))
+    dc.set_sdpa_precision(args.precision)
 
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-                "scaling": "strong" if ring is not None else "weak",
+        line = {"metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+                "higher_is_better": True, "scaling": "strong" if w["cfg"] == 4 and world > 1 else "weak",
                 "vs_baseline": None, "dtype": "f32" if args.precision == "fp32" else args.precision,
                 "data": "synthetic (seeded N(0,1) of the config's shape)",
-                "config": {"workload": name, "baseline_cfg": w["cfg"], "shape_q": list(w["q"]),
-                           "shape_kv": list(w["kv"]), "causal": causal, "mask": w["mask"],
-                           "dropout_p": w.get("dropout", 0.0),
-                           "per_rank": ("zig-zag sequence shard (ring attention, NCCL send/recv)"
-                                        if ring is not None else "full workload (weak scaling)"),
-                           "parallelism": f"ring{world}" if ring is not None else f"dp{world}",
-                           "precision": args.precision, "l2": "flushed (256 MB write) before every timed step",
-                           "launch": launch,
+                "config": config_of(name, w, world, w["cfg"] == 4 and world > 1),
+                "timing": {"launch": head["launch"], "precision": args.precision,
                            "kernel_breakdown": "a second, untimed pass of the same steps with per-launch tracing"},
-                "roofline": roofline, "kernels": {k_: {"launches": v_[0], "total_ms": v_[1]}
-                                                  for k_, v_ in kernels.items()},
-                "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cb, "clocks": clocks.summary()}
+                "roofline": head["roofline"], "kernels": head["kernels"], "gpu_launches": head["gpu_launches"],
+                "e2e": head.get("e2e"), "cpu_baseline": head.get("cpu_baseline"), "clocks": head.get("clocks")}
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -553,6 +704,7 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
     ev_used = [torch.cuda.Event() for _ in range(nslot)]  # the slot's compute finished
     ev_out = [torch.cuda.Event() for _ in range(nslot)]   # the slot's results are on the host
     used = [False] * nslot
+    last_res = [None] * nslot  # each slot's latest results (device tensors), reused by copy_ceiling
 
     def compute(d):
         if ring is not None:
@@ -598,6 +750,7 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
                 h.copy_(r, non_blocking=True)
             ev_out[sl].record(s_d2h)
         used[sl] = True
+        last_res[sl] = res
 
     # Results freed on the compute stream stay reserved until their copy stream is done with
     # them, so the caching allocator grows over the first pipelined steps; a cudaMalloc inside
@@ -623,19 +776,61 @@ def run_e2e(w, q, k, v, g, mask, args, device, scale, amount, dist, ring=None):
     torch.cuda.synchronize()
     allocs = torch.cuda.memory_stats(device).get("num_device_alloc", 0) - allocs0
     ms = s.elapsed_time(e) / args.steps
-    world = 1
-    if dist is not None:
-        world = dist.get_world_size()
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    if ring is not None:
-        world = 1  # the ranks share one sequence
-    return {"value": world * amount / (ms / 1e3) / scale, "unit": "GB/s" if scale == 1e9 else "TFLOP/s",
-            "ms_per_step": ms, "h2d_bytes_per_step": sum(t.numel() * 4 for t in host_in[0]),
+    copy_ms = copy_ceiling(host_in, dev_in, host_out, [[r for r in row] for row in last_res], args.steps, device,
+                           dist)
+    ms = _max_over_ranks(ms, dist, device)
+    unit = "GB/s" if scale == 1e9 else "TFLOP/s"
+    value = amount / (ms / 1e3) / scale
+    ceiling = amount / (copy_ms / 1e3) / scale
+    return {"value": value, "unit": unit, "ms_per_step": ms, "h2d_bytes_per_step": sum(t.numel() * 4 for t in host_in[0]),
             "d2h_bytes_per_step": sum(t.numel() * 4 for t in host_out[0]), "pipelined": True,
-            "warmup_steps": warm, "device_allocs_in_timed_steps": allocs}
+            "warmup_steps": warm, "device_allocs_in_timed_steps": allocs,
+            "copy_ceiling": {"ms_per_step": copy_ms, "value": ceiling, "frac": value / ceiling,
+                             "what": "the same per-step H2D and D2H copies through the same pinned buffers, "
+                                     "streams and slots with no compute (max over ranks): the host link's "
+                                     "bound on e2e"}}
 
+
+def copy_ceiling(host_in, dev_in, host_out, dev_out, steps, device, dist):
+    """ms per step of the e2e loop's copies alone: each step's inputs up on one stream and the
+    previous step's results down on another, three slots, no compute; max over ranks."""
+    nslot = len(host_in)
+    s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(nslot)]
+    ev_out = [torch.cuda.Event() for _ in range(nslot)]
+    used = [False] * nslot
+
+    def step(i):
+        sl = i % nslot
+        if used[sl]:
+            ev_out[sl].synchronize()
+        with torch.cuda.stream(s_h2d):
+            for h, d in zip(host_in[sl], dev_in[sl]):
+                d.copy_(h, non_blocking=True)
+            ev_in[sl].record(s_h2d)
+        with torch.cuda.stream(s_d2h):
+            s_d2h.wait_event(ev_in[sl])
+            for h, r in zip(host_out[sl], dev_out[sl]):
+                h.copy_(r, non_blocking=True)
+            ev_out[sl].record(s_d2h)
+        used[sl] = True
+
+    for i in range(2 * nslot):
+        step(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    cur = torch.cuda.current_stream(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(cur)
+    s_h2d.wait_event(s)
+    for i in range(steps):
+        step(2 * nslot + i)
+    for sl in range(nslot):
+        cur.wait_event(ev_out[sl])
+    e.record(cur)
+    torch.cuda.synchronize()
+    return _max_over_ranks(s.elapsed_time(e) / steps, dist, device)
 
 if __name__ == "__main__":
     main()

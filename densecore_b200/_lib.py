@@ -23,7 +23,8 @@ DC_PREC_3XTF32, DC_PREC_TF32, DC_PREC_FP32 = 0, 1, 2
 EXPORTS = ("dc_sdpa_fwd", "dc_sdpa_bwd_workspace_size", "dc_sdpa_bwd", "dc_sdpa_decode_workspace_size",
            "dc_sdpa_decode_default_splits", "dc_sdpa_decode", "dc_sdpa_decode_noalloc", "dc_attn_merge", "dc_attn_probs",
            "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report", "dc_device_status",
-           "dc_dropout_keep_bits", "dc_rng_skip", "dc_sdpa_fwd_dropout", "dc_sdpa_bwd_dropout", "dc_attn_probs_dropout")
+           "dc_dropout_keep_bits", "dc_rng_skip", "dc_sdpa_fwd_dropout", "dc_sdpa_bwd_dropout", "dc_attn_probs_dropout",
+           "dc_debug_wait_probe")
 
 
 class DcTensor(ctypes.Structure):
@@ -88,6 +89,8 @@ def load():
         L.dc_sdpa_fwd_path.restype = i
         L.dc_device_status.argtypes = [i]
         L.dc_device_status.restype = i
+        L.dc_debug_wait_probe.argtypes = [ctypes.c_uint64, i, vp]
+        L.dc_debug_wait_probe.restype = i
         L.dc_kernel_timing.argtypes = [i]
         L.dc_kernel_timing.restype = i
         L.dc_kernel_timing_report.argtypes = [ctypes.c_char_p, sz, i]

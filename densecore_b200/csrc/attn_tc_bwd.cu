@@ -1058,41 +1058,12 @@ struct PoolScratch {
     ~PoolScratch() { pool_free(ptr, stream); }
 };
 
-// The dQ kernel does not depend on the dK / dV kernel: it runs on a second stream of the
-// library's (one per device, created on first use), forked from the caller's stream after the
-// pre-pass and joined back before the call returns, so that the two kernels share the GPU (the
-// CTAs of one fill the SMs that the other's last, shorter tiles leave idle). Both events are
-// created per call, so concurrent calls from several host threads do not share them.
-constexpr int kSideDevices = 64;
-std::mutex g_side_mu;
-cudaStream_t g_side[kSideDevices];
-
-int side_stream(cudaStream_t *out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "backward: current device");
-    if (dev < 0 || dev >= kSideDevices) return fail(DC_ERR_UNSUPPORTED, "backward: device ordinal above 63");
-    std::lock_guard<std::mutex> lock(g_side_mu);
-    if (!g_side[dev]) {
-        e = cudaStreamCreateWithFlags(&g_side[dev], cudaStreamNonBlocking);
-        if (e != cudaSuccess) {
-            g_side[dev] = nullptr;
-            return cuda_fail(e, "backward: create the dQ stream");
-        }
-    }
-    *out = g_side[dev];
-    return DC_OK;
-}
-
-// Records an event on `from` and makes `to` wait for it.
-int stream_edge(cudaStream_t from, cudaStream_t to) {
-    cudaEvent_t ev = nullptr;
-    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventRecord(ev, from);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(to, ev, 0);
-    if (ev) cudaEventDestroy(ev);  // released once the recorded work completes
-    return e == cudaSuccess ? DC_OK : cuda_fail(e, "backward: stream fork / join");
-}
+// The dQ kernel does not depend on the dK / dV kernel: it runs on a side stream of the
+// library's that belongs to the caller's stream (streams.cu), forked from the caller's stream
+// after the pre-pass and joined back before the call returns -- on error paths too -- so that
+// the two kernels share the GPU (the CTAs of one fill the SMs that the other's last, shorter
+// tiles leave idle). The fork and join events are created per call.
+constexpr int kSideRoleDq = 0;
 
 }  // namespace
 
@@ -1163,9 +1134,10 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     // Fork the dQ stream here, after the pre-pass and before the dK / dV launch.
     cudaStream_t side = nullptr;
     if (p.L > 0) {
-        if ((st = side_stream(&side))) return st;
+        if ((st = side_stream(stream, kSideRoleDq, &side))) return st;
         if ((st = stream_edge(stream, side))) return st;
     }
+    StreamJoin join(stream, side);  // joins side back into stream on every return below
     if (p.S > 0) {
         CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
         st = make_tmap(&tk, pa.khl, DD, p.S, p.Hkv, nb, kst, TILE);
@@ -1214,7 +1186,7 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
             kernel<<<grid, THREADS, QC::SMEM, side>>>(tq, tdo, tkk, tkmn, tvk, a);
         }
         const int launched = check_launch("attn_bwd_dq_tc");
-        if ((st = stream_edge(side, stream))) return st;
+        if ((st = join.join())) return st;
         if (launched) return launched;
     }
     return DC_OK;

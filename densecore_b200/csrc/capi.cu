@@ -25,6 +25,8 @@ thread_local std::string g_last_error;
 
 void set_error(const std::string &msg) { g_last_error = msg; }
 
+std::string last_error() { return g_last_error; }
+
 int fail(int status, const std::string &msg) {
     g_last_error = msg;
     return status;

@@ -154,6 +154,7 @@ __device__ __forceinline__ bool causal_visible(int causal, int64_t i, int64_t j)
 
 // Host side: the thread's last error message and a setter that returns the status.
 void set_error(const std::string &msg);
+std::string last_error();
 int fail(int status, const std::string &msg);
 int cuda_fail(cudaError_t err, const char *what);
 

@@ -46,6 +46,27 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
               cudaStream_t stream);
 int rng_skip(const uint32_t *st_in, uint64_t outputs, uint32_t *st_out);
 
+// Side streams (streams.cu): the library's stream for `role` (0 = the backward's dQ kernel,
+// 1 = ring attention's transfers) beside caller stream `caller` on the current device, and an
+// event edge that makes `to` wait for the work enqueued on `from` so far.
+int side_stream(cudaStream_t caller, int role, cudaStream_t *out);
+int stream_edge(cudaStream_t from, cudaStream_t to);
+
+// A fork of `side` from `caller` that is joined back exactly once: by join(), or, on an error
+// path that returns early, by the destructor (which keeps the call's error message).
+class StreamJoin {
+   public:
+    StreamJoin(cudaStream_t caller, cudaStream_t side) : caller_(caller), side_(side) {}
+    ~StreamJoin();
+    int join();
+    StreamJoin(const StreamJoin &) = delete;
+    StreamJoin &operator=(const StreamJoin &) = delete;
+
+   private:
+    cudaStream_t caller_, side_;
+    bool joined_ = false;
+};
+
 // The library's stream-ordered scratch pool (pool.cu): memory for `bytes` on `stream`'s
 // order of the current device, and its release on the same stream.
 int pool_alloc(void **ptr, size_t bytes, cudaStream_t stream);

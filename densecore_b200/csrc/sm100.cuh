@@ -53,17 +53,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase of `bar` with the given parity. Gives up (returns false) when *abort
-// is set by another thread or after WAIT_TIMEOUT_NS, in which case it sets *abort and
+// is set by another thread or after timeout_ns (WAIT_TIMEOUT_NS in every kernel; only the
+// wait probe of selftest.cu passes a shorter bound), in which case it sets *abort and
 // records DEV_WAIT_TIMEOUT in *err_flag.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
-                                          int *err_flag) {
+                                          int *err_flag, uint64_t timeout_ns = WAIT_TIMEOUT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0) {
             if (*abort) return false;
-            if (globaltimer() - t0 > WAIT_TIMEOUT_NS) {
+            if (globaltimer() - t0 > timeout_ns) {
                 *abort = 1;
                 if (err_flag) atomicExch(err_flag, DEV_WAIT_TIMEOUT);
                 return false;

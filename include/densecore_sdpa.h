@@ -39,6 +39,9 @@
  *  - Launches are asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream).
  *    No call synchronises the host. There is no CPU fallback: with no usable device the call
  *    fails with DC_ERR_CUDA.
+ *  - The library keeps per-device state for the life of the process (side streams, the device
+ *    status word's and the no-alloc scratch's addresses, the dropout jump tables): calling
+ *    cudaDeviceReset while the library is loaded and then using it again is not supported.
  *  - Return value: DC_OK, or an error code; dc_last_error() then holds the message.
  *    DC_ERR_VALUE corresponds to the reference's ValueError (shape errors, lib.rs:562-570,
  *    :601-605, :658-662); DC_ERR_RUNTIME / DC_ERR_CUDA to its RuntimeError (lib.rs:633, :677).
@@ -119,7 +122,9 @@ DC_API int dc_sdpa_decode(const dc_tensor_t *q, const dc_tensor_t *k, const dc_t
                    void *stream);
 
 /* Fixed size of the device scratch dc_sdpa_decode_noalloc holds per device: 8 MiB, enough for
- * the default split count (148 SMs) of up to 16131 (batch, head) rows at head dim 128. */
+ * the default split count (148 SMs) of up to 16131 (batch, head) rows at head dim 128 -- the
+ * default split count falls to 1 at 3552 rows and more, so that at 16131 rows one split's
+ * partials (130 floats per row) still fit. */
 #define DC_DECODE_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 /* dc_sdpa_decode that allocates no device memory: the split partials go to a static device
@@ -229,6 +234,16 @@ DC_API int dc_kernel_timing_report(char *buf, size_t len, int reset);
  * 1..624 -- it then wrote neither mask nor state. Synchronises with the device. reset != 0
  * clears the status. -1 on a CUDA error. */
 DC_API int dc_device_status(int reset);
+
+/* Failure-detection hook for tests: launches `blocks` (1..1024) CTAs of a probe kernel that
+ * takes 32 columns of tensor memory and then waits on an mbarrier that nothing arrives at,
+ * through the same bounded wait the tensor-core kernels use, with the bound shortened to
+ * timeout_ns (1000 ns .. 1 s). Each wait gives up after the bound, sets dc_device_status() to
+ * 1, and its CTA frees its tensor memory and returns: the call ends, the device stays usable
+ * and the next call runs normally. Nothing faults or hangs. No counterpart in the reference,
+ * whose CPU kernels report failure through their Result slots (torch_attention.rs:163,
+ * :274-276; raised as RuntimeError at lib.rs:633, :677). */
+DC_API int dc_debug_wait_probe(uint64_t timeout_ns, int blocks, void *stream);
 
 /* Message of the last failing call on this host thread ("" if none). */
 DC_API const char *dc_last_error(void);

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_library_exports_nothing_undeclared():
-    """Every exported dc_* symbol is part of the header: no debugging or probe entry points."""
+    """Every exported dc_* symbol is declared in the header: nothing is exported that the header does not document."""
     import subprocess
     try:
         out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,

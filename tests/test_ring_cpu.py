@@ -87,3 +87,58 @@ def test_zigzag_round_trip_and_balance():
     assert len(set(work)) == 1
     with pytest.raises(ValueError):
         zigzag_indices(50, 0, 4)
+
+
+def _peer_worker(rank, world, port, mode, timeout_s, result_dir):
+    """Rank 1 either joins the ring late (inside the process group's timeout) or never joins
+    (it sleeps past the timeout and leaves). Rank 0 records how its ring call ended."""
+    import datetime
+    import json
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    try:
+        from densecore_b200.ring import RingAttention, zigzag_shard
+        shape = (1, 2, 64 * world, 64)
+        q, k, v = (zigzag_shard(t, rank, world) for t in _inputs(shape, 6))
+        ring = RingAttention(q.shape, k.shape, "cpu", causal=True, attn_fn=_oracle_attn, merge_fn=_torch_merge)
+        if rank == 1:
+            time.sleep(timeout_s * (0.3 if mode == "late" else 2.0))
+            if mode == "absent":
+                return  # leaves without taking part; rank 0's receive can never complete
+        t0 = time.monotonic()
+        try:
+            out, lse = ring(q, k, v)
+            res = {"ok": True, "s": time.monotonic() - t0}
+            torch.save({"out": out, "lse": lse}, os.path.join(result_dir, f"r{rank}.pt"))
+        except Exception as e:  # the outcome under test: the host-side timeout raises
+            res = {"ok": False, "type": type(e).__name__, "msg": str(e)[:300], "s": time.monotonic() - t0}
+        with open(os.path.join(result_dir, f"r{rank}.json"), "w") as f:
+            json.dump(res, f)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["late", "absent"])
+def test_ring_peer_late_or_absent(mode, tmp_path):
+    """A ring peer that arrives late (within the process group's timeout) only delays the
+    result; a peer that never takes part makes the waiting rank's ring call raise once the
+    timeout runs out, instead of hanging."""
+    import json
+    import oracle
+    from densecore_b200.ring import zigzag_unshard
+    world, timeout_s = 2, 3
+    mp.start_processes(_peer_worker, args=(world, _free_port(), mode, timeout_s, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    r0 = json.loads((tmp_path / "r0.json").read_text())
+    if mode == "absent":
+        assert not r0["ok"], "rank 0's ring call should fail when its peer never takes part"
+        assert r0["type"] in ("RuntimeError", "DistBackendError"), r0
+        assert r0["s"] < 10 * timeout_s, r0
+        return
+    assert r0["ok"], r0
+    parts = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
+    out = zigzag_unshard([p["out"] for p in parts]).numpy()
+    q, k, v = (t.numpy() for t in _inputs((1, 2, 64 * world, 64), 6))
+    ref_out, _ = oracle.flash_forward(q, k, v, causal=True)
+    assert rel_err(out, ref_out) <= 1e-5
