@@ -550,33 +550,48 @@ def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
         extras["cfg3_strong"] = r
         torch.cuda.empty_cache()
 
-    # Config 4 through ring attention (strong scaling), next to the same forward on one GPU per
-    # rank (all ranks at once) for the fraction of N x one GPU, and a parity check of every
+    # Config 4 through ring attention (strong scaling): the C-ABI entry dc_ring_sdpa_fwd over an
+    # NCCL communicator made through libnccl's C API (what a C or Rust host hands it), beside the
+    # same ring driven from Python over torch.distributed, and the same forward on one GPU per
+    # rank (all ranks at once) for the fraction of N x one GPU; then a parity check of every
     # rank's ring rows against single-GPU forwards of two heads over the whole sequence.
     w4 = WORKLOADS["long_causal_fwd"]
     S = w4["q"][2]
     if S % (2 * world) == 0:
+        from densecore_b200.ring import NativeRingAttention, NcclCommunicator
         full = make_inputs(w4, device, seed=1234)
         q, k, v = (zigzag_shard(t, rank, world) for t in full[:3])
-        ringa = RingAttention(q.shape, k.shape, device, causal=True)
-        r = measure("long_causal_fwd", w4, device, dist, steps, 3, agg_amount=work(w4)[0], inputs=(q, k, v, None, None),
-                    ring=ringa)
+        comm = NcclCommunicator(device=device)
+        try:
+            ringn = NativeRingAttention(q.shape, k.shape, device, comm, causal=True)
+            r = measure("long_causal_fwd", w4, device, dist, steps, 3, agg_amount=work(w4)[0],
+                        inputs=(q, k, v, None, None), ring=ringn)
+            out, lse = ringn(q, k, v)
+            torch.cuda.synchronize()
+        finally:
+            dist.barrier()
+            comm.destroy()
+        ringt = RingAttention(q.shape, k.shape, device, causal=True)
+        rt = measure("long_causal_fwd", w4, device, dist, steps, 3, agg_amount=work(w4)[0],
+                     inputs=(q, k, v, None, None), ring=ringt)
         one = measure("long_causal_fwd", w4, device, dist, max(3, steps // 4), 3, agg_amount=work(w4)[0],
                       inputs=full)
-        out, lse = ringa(q, k, v)
         heads = [0, 9]
         so, sl = _native._flash_attention(*(t[:, heads].contiguous() for t in full[:3]), True)
         ref_o, ref_l = zigzag_shard(so, rank, world), zigzag_shard(sl.unsqueeze(-1), rank, world).squeeze(-1)
         err_o = float((out[:, heads] - ref_o).abs().max() / ref_o.abs().max())
         err_l = float((lse[:, heads] - ref_l).abs().max() / ref_l.abs().max())
         err = _max_over_ranks(max(err_o, err_l), dist, device)
-        r.update(scaling="strong", one_gpu_ms=one["ms_per_step"], one_gpu_value=one["value"],
+        r.update(impl="dc_ring_sdpa_fwd (C ABI; NCCL send/recv on a side stream, merges in the library)",
+                 scaling="strong", one_gpu_ms=one["ms_per_step"], one_gpu_value=one["value"],
                  frac_of_n_x_one_gpu=r["value"] / (world * one["value"]),
+                 torch_ring={"ms_per_step": rt["ms_per_step"], "value": rt["value"],
+                             "impl": "densecore_b200.ring.RingAttention (batch_isend_irecv over the NCCL process group)"},
                  parity={"max_rel_err": err, "tol": 1e-5, "ok": err <= 1e-5,
                          "what": "every rank's ring out and lse, heads 0 and 9, against a single-GPU forward "
                                  "of those heads over the whole sequence (max |delta| / max |ref|)"})
         extras["ring_cfg4"] = r
-        del full, q, k, v, ringa, out, lse, so, sl
+        del full, q, k, v, ringn, ringt, out, lse, so, sl
         torch.cuda.empty_cache()
 
     # Config 5: the batch of 64 decode rows split over the ranks (8 per GPU at 8); each rank

@@ -24,7 +24,7 @@ EXPORTS = ("dc_sdpa_fwd", "dc_sdpa_bwd_workspace_size", "dc_sdpa_bwd", "dc_sdpa_
            "dc_sdpa_decode_default_splits", "dc_sdpa_decode", "dc_sdpa_decode_noalloc", "dc_attn_merge", "dc_attn_probs",
            "dc_last_error", "dc_abi_version", "dc_sdpa_fwd_path", "dc_kernel_timing", "dc_kernel_timing_report", "dc_device_status",
            "dc_dropout_keep_bits", "dc_rng_skip", "dc_sdpa_fwd_dropout", "dc_sdpa_bwd_dropout", "dc_attn_probs_dropout",
-           "dc_debug_wait_probe")
+           "dc_debug_wait_probe", "dc_ring_sdpa_fwd_workspace_size", "dc_ring_sdpa_fwd")
 
 
 class DcTensor(ctypes.Structure):
@@ -89,6 +89,10 @@ def load():
         L.dc_sdpa_fwd_path.restype = i
         L.dc_device_status.argtypes = [i]
         L.dc_device_status.restype = i
+        L.dc_ring_sdpa_fwd_workspace_size.argtypes = [i64, i64, i64, i64, i64]
+        L.dc_ring_sdpa_fwd_workspace_size.restype = sz
+        L.dc_ring_sdpa_fwd.argtypes = [_P, _P, _P, i, i, d, i, vp, _P, _P, vp, sz, vp]
+        L.dc_ring_sdpa_fwd.restype = i
         L.dc_debug_wait_probe.argtypes = [ctypes.c_uint64, i, vp]
         L.dc_debug_wait_probe.restype = i
         L.dc_kernel_timing.argtypes = [i]

@@ -156,6 +156,26 @@ def _attn_merge(out_acc, lse_acc, out_part, lse_part):
     return out_acc, lse_acc
 
 
+def _ring_attention(q, k, v, comm_ptr, causal=True, scale=None, precision=None, workspace=None):
+    """Ring attention forward of this rank's zig-zag shards over an NCCL communicator
+    (dc_ring_sdpa_fwd): (out, lse) of the local query rows against the whole sequence."""
+    L = _lib.load()
+    dev = _require_cuda(q, k, v)
+    B, H, Lq = q.shape[:3]
+    out = torch.empty((B, H, Lq, v.shape[3]), device=dev, dtype=torch.float32)
+    lse = torch.empty((B, H, Lq), device=dev, dtype=torch.float32)
+    prec = precision_code() if precision is None else precision
+    has, sc = _scale_args(scale)
+    with torch.cuda.device(dev):
+        need = L.dc_ring_sdpa_fwd_workspace_size(B, H, k.shape[1], Lq, q.shape[3])
+        ws = workspace if workspace is not None else torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+        vs = [_lib.view(t) for t in (q, k, v, out, lse)]
+        st = L.dc_ring_sdpa_fwd(*[_lib.ref(x) for x in vs[:3]], int(bool(causal)), has, sc, prec, comm_ptr,
+                                _lib.ref(vs[3]), _lib.ref(vs[4]), ws.data_ptr(), ws.numel(), _lib.stream_of(q))
+    _lib.check(st, "ring attention failed")
+    return out, lse
+
+
 def _attn_probs(q, k, lse, causal, scale=None, mask=None, average_heads=True, keep=None, keep_scale=0.0):
     """softmax(scale q k^T + mask) from the forward's lse; (B,L,S) head mean or (B,H,L,S).
     With ``keep`` (packed dropout keep bits) each probability is times its dropout factor."""

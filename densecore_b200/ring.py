@@ -170,3 +170,78 @@ def ring_attention_forward(q, k, v, group=None, causal=True, scale=None, precisi
     if v.shape != k.shape:
         raise ValueError("ring attention needs k and v of the same shape")
     return ring(q, k, v)
+
+
+class NcclCommunicator:
+    """An NCCL communicator over the ranks of a torch.distributed group, made through
+    libnccl's own C API (ncclGetUniqueId on the group's first rank, broadcast over the group,
+    ncclCommInitRank on every rank) -- the communicator a C or Rust host would hand to
+    ``dc_ring_sdpa_fwd``. ``ptr`` is the ncclComm_t. Every rank of the group must construct it
+    together, with its CUDA device current."""
+
+    _nccl = None
+
+    @classmethod
+    def _lib(cls):
+        import ctypes
+        if cls._nccl is None:
+            import torch.cuda.nccl  # noqa: F401  (makes torch load its libnccl first)
+            cls._nccl = ctypes.CDLL("libnccl.so.2")
+        return cls._nccl
+
+    def __init__(self, group=None, device=None):
+        import ctypes
+
+        class UniqueId(ctypes.Structure):
+            _fields_ = [("internal", ctypes.c_char * 128)]
+
+        lib = self._lib()
+        lib.ncclGetUniqueId.argtypes = [ctypes.POINTER(UniqueId)]
+        lib.ncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, UniqueId, ctypes.c_int]
+        lib.ncclCommDestroy.argtypes = [ctypes.c_void_p]
+        lib.ncclGetErrorString.restype = ctypes.c_char_p
+        single = group is None and not dist.is_initialized()  # a one-rank communicator needs no group
+        world, rank = (1, 0) if single else (dist.get_world_size(group), dist.get_rank(group))
+        uid = UniqueId()
+        if rank == 0:
+            r = lib.ncclGetUniqueId(ctypes.byref(uid))
+            if r:
+                raise RuntimeError("ncclGetUniqueId: " + lib.ncclGetErrorString(r).decode())
+        if not single:
+            box = [bytes(uid.internal) if rank == 0 else None]
+            src = dist.get_global_rank(group, 0) if group is not None else 0
+            dist.broadcast_object_list(box, src=src, group=group)
+            uid = UniqueId()
+            ctypes.memmove(ctypes.addressof(uid), box[0], 128)
+        comm = ctypes.c_void_p()
+        with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+            r = lib.ncclCommInitRank(ctypes.byref(comm), world, uid, rank)
+        if r:
+            raise RuntimeError("ncclCommInitRank: " + lib.ncclGetErrorString(r).decode())
+        self.ptr = comm.value
+        self.world, self.rank = world, rank
+
+    def destroy(self):
+        if self.ptr:
+            self._lib().ncclCommDestroy(self.ptr)
+            self.ptr = None
+
+
+class NativeRingAttention:
+    """Ring attention through the library's C entry point ``dc_ring_sdpa_fwd``: the same zig-zag
+    ring as :class:`RingAttention`, with the ring loop, the NCCL send/recv of K/V blocks and the
+    merges inside the library (NCCL on a side stream, overlapped with each step's attention).
+    ``comm`` is an :class:`NcclCommunicator` (or anything with an ncclComm_t in ``.ptr``)."""
+
+    def __init__(self, shape_q, shape_kv, device, comm, causal=True, scale=None, precision=None):
+        from . import _lib
+        B, H, L2, D = shape_q
+        _, Hk, S2, _ = shape_kv
+        self.comm, self.causal, self.scale, self.precision = comm, causal, scale, precision
+        n = _lib.load().dc_ring_sdpa_fwd_workspace_size(B, H, Hk, L2, D)
+        self.ws = torch.empty(max(n, 1), dtype=torch.uint8, device=device)
+        self.shape_q = tuple(shape_q)
+
+    def __call__(self, q, k, v):
+        from ._native import _ring_attention
+        return _ring_attention(q, k, v, self.comm.ptr, self.causal, self.scale, self.precision, self.ws)

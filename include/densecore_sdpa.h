@@ -11,6 +11,8 @@
  *   dc_sdpa_decode   q_len == 1 case of _flash_attention (torch_attention.rs:157, q_split -> 1)
  *   dc_sdpa_decode_noalloc  the same with a static scratch array (no reference counterpart)
  *   dc_attn_merge    logsumexp merge of partial results (ring attention; no CPU counterpart)
+ *   dc_ring_sdpa_fwd  _flash_attention sharded by sequence over an NCCL communicator (ring
+ *                    attention; the reference has no sequence parallelism)
  *   dc_attn_probs    softmax(scale*QK^T + mask) averaged over heads: the need_weights output of
  *                    multi_head_attention_forward (python/densecore/functional.py:456-461)
  *   dc_dropout_keep_bits  the bernoulli draw of _dropout_noise (functional.py:638-641,
@@ -152,6 +154,34 @@ DC_API int dc_sdpa_decode_noalloc(const dc_tensor_t *q, const dc_tensor_t *k, co
  * reference has no sequence parallelism). */
 DC_API int dc_attn_merge(dc_tensor_t *out_acc, dc_tensor_t *lse_acc, const dc_tensor_t *out_part,
                   const dc_tensor_t *lse_part, void *stream);
+
+/* ---- Ring attention (sequence parallelism over an NCCL communicator) ----
+ * NCCL's communicator type: ncclComm_t in nccl.h is `struct ncclComm *`. */
+struct ncclComm;
+
+/* Bytes of device workspace dc_ring_sdpa_fwd needs for local shards q (B, H, 2C, E) and
+ * k, v (B, Hkv, 2C, E): two packed K/V blocks and one partial result. */
+DC_API size_t dc_ring_sdpa_fwd_workspace_size(int64_t batch, int64_t heads, int64_t kv_heads,
+                                              int64_t local_len, int64_t head_dim);
+
+/* Ring attention forward over the P ranks of `comm` (rank and P are the communicator's own).
+ * Each rank passes its zig-zag shard of one sequence: chunks r and 2P-1-r of 2P equal chunks,
+ * back to back, as q (B, H, 2C, E) and contiguous k, v (B, Hkv, 2C, E); out (B, H, 2C, E) and
+ * lse (B, H, 2C) receive what dc_sdpa_fwd over the whole sequence gives for those query rows
+ * (top-left causal when causal != 0). K/V blocks go round the ring with ncclSend / ncclRecv on
+ * a side stream of the library's, overlapped with each step's attention on `stream`; partial
+ * results are merged by logsumexp (dc_attn_merge). Every rank must make the same call (same
+ * shapes, causal flag and order of calls on `comm`). workspace: device memory of
+ * dc_ring_sdpa_fwd_workspace_size() bytes, 256-byte aligned. No user mask (a row fully masked
+ * inside one block would give the reference's out = 0, lse = 0 for that block, which a merge
+ * cannot tell from a real contribution). If a call fails after its first transfer was issued,
+ * the peers' matching transfers are left pending: abort the communicator (ncclCommAbort).
+ * The reference has no sequence parallelism: this shards torch_attention.rs:146-284 by
+ * sequence, and its result contract is that of dc_sdpa_fwd / _flash_attention (lib.rs:609-638). */
+DC_API int dc_ring_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor_t *v,
+                            int causal, int has_scale, double scale, int precision,
+                            struct ncclComm *comm, dc_tensor_t *out, dc_tensor_t *lse,
+                            void *workspace, size_t workspace_bytes, void *stream);
 
 /* Head-averaged attention probabilities (B, L, S): mean over H of
  * exp(scale*q.k + mask - lse) with lse from dc_sdpa_fwd, zero where masked or causal-hidden.

@@ -103,3 +103,26 @@ def test_cpu_tensors_are_refused_loudly():
     q = torch.zeros(1, 2, 4, 8)
     with pytest.raises(RuntimeError, match="CUDA"):
         dc.scaled_dot_product_attention(q, q, q)
+
+
+def test_ring_entry_validates_before_any_device_work():
+    L = _lib.load()
+    q, k, v = _fake((1, 2, 64, 64)), _fake((1, 2, 64, 64)), _fake((1, 2, 64, 64))
+    out, lse = _fake((1, 2, 64, 64)), _fake((1, 2, 64))
+    need = L.dc_ring_sdpa_fwd_workspace_size(1, 2, 2, 64, 64)
+    assert need == ((2 * 2 * 2 * 64 * 64 + 2 * 64 * 65) * 4 + 255) // 256 * 256
+    ws = 0x100000
+
+    def call(q_=q, k_=k, comm=0x2000, nbytes=need, wsp=ws):
+        return L.dc_ring_sdpa_fwd(ctypes.byref(q_), ctypes.byref(k_), ctypes.byref(v), 1, 0, 0.0, 0, comm,
+                                  ctypes.byref(out), ctypes.byref(lse), wsp, nbytes, None)
+
+    assert call(comm=None) == _lib.DC_ERR_VALUE                # no communicator
+    assert call(nbytes=need - 1) == _lib.DC_ERR_VALUE          # workspace too small
+    assert call(wsp=ws + 16) == _lib.DC_ERR_VALUE              # workspace not 256-byte aligned
+    odd = _fake((1, 2, 63, 64))
+    assert call(q_=odd, k_=odd) == _lib.DC_ERR_VALUE           # local length must be even
+    strided = _fake((1, 2, 64, 64))
+    strided.strides[2] = 128                                    # k not contiguous
+    assert call(k_=strided) == _lib.DC_ERR_VALUE
+    assert b"contiguous" in L.dc_last_error()
