@@ -90,7 +90,7 @@ def kernel_work(w, name):
     gemm = 2.0 * D * pairs
     if name.startswith("fwd"):
         return 2 * gemm
-    if name == "bwd_tc":  # dK/dV and dQ, run concurrently: one record spans both
+    if name == "bwd_tc":  # dK/dV and dQ (beside it, or after it from the stored dS): one record spans both
         return 5 * gemm
     if "dkdv" in name:
         return 4 * gemm
@@ -463,7 +463,7 @@ def roofline_of(name, w, kernels, steps, ring, world, rank_amount):
     pk = peaks()
     # Kernels without a roofline of their own (the dropout mask draw: integer generator work,
     # neither HBM- nor tensor-bound) are named in "slowest_kernel" but are not the unit.
-    concurrent = ("bwd_dkdv_tc", "bwd_dq_tc") if "bwd_tc" in kernels else ()
+    concurrent = ("bwd_dkdv_tc", "bwd_dq_tc", "bwd_dq_gemm") if "bwd_tc" in kernels else ()
     candidates = {k_: v_ for k_, v_ in kernels.items() if k_ not in concurrent}
     slowest = max(candidates.items(), key=lambda kv: kv[1][1])[0] if candidates else None
     candidates = {k_: v_ for k_, v_ in candidates.items() if kernel_work(w, k_) > 0 or ring is not None}
@@ -526,13 +526,27 @@ def single_gpu_extras(device, steps):
     return out
 
 
+def _guarded(extras, key, fn):
+    """Runs one extra; an exception is recorded in its place instead of ending the run. (All
+    ranks run the same code on the same shapes, so a failure is normally on every rank.)"""
+    try:
+        fn()
+    except Exception as e:  # noqa: BLE001 -- reported in the JSON line
+        extras[key] = {"error": f"{type(e).__name__}: {e}"[:500]}
+        torch.cuda.empty_cache()
+
+
 def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
     """At N > 1: config 3 strong-scaled over its 96 (batch, head) units, config 4 through ring
     attention (strong, with an in-run parity check), config 5 batch shards (strong)."""
-    from densecore_b200 import _native
-    from densecore_b200.ring import RingAttention, zigzag_shard
     extras = {}
+    _guarded(extras, "cfg3_strong", lambda: _cfg3_strong(extras, device, dist, rank, world, steps, e2e_args))
+    _guarded(extras, "ring_cfg4", lambda: _ring_cfg4(extras, device, dist, rank, world, steps))
+    _guarded(extras, "decode_shard", lambda: _decode_shard(extras, device, dist, rank, world, steps))
+    return extras
 
+
+def _cfg3_strong(extras, device, dist, rank, world, steps, e2e_args):
     # Config 3: the 96 independent (batch, head) units of [8, 12, 1024, 64] split evenly over the
     # ranks (12 per GPU at 8), as DenseCore's par_chunks splits them over threads
     # (torch_attention.rs:108-128). Each rank's units are a (1, 96/N, 1024, 64) slice; e2e
@@ -550,6 +564,10 @@ def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
         extras["cfg3_strong"] = r
         torch.cuda.empty_cache()
 
+
+def _ring_cfg4(extras, device, dist, rank, world, steps):
+    from densecore_b200 import _native
+    from densecore_b200.ring import NativeRingAttention, NcclCommunicator, RingAttention, zigzag_shard
     # Config 4 through ring attention (strong scaling): the C-ABI entry dc_ring_sdpa_fwd over an
     # NCCL communicator made through libnccl's C API (what a C or Rust host hands it), beside the
     # same ring driven from Python over torch.distributed, and the same forward on one GPU per
@@ -558,7 +576,6 @@ def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
     w4 = WORKLOADS["long_causal_fwd"]
     S = w4["q"][2]
     if S % (2 * world) == 0:
-        from densecore_b200.ring import NativeRingAttention, NcclCommunicator
         full = make_inputs(w4, device, seed=1234)
         q, k, v = (zigzag_shard(t, rank, world) for t in full[:3])
         comm = NcclCommunicator(device=device)
@@ -594,6 +611,8 @@ def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
         del full, q, k, v, ringn, ringt, out, lse, so, sl
         torch.cuda.empty_cache()
 
+
+def _decode_shard(extras, device, dist, rank, world, steps):
     # Config 5: the batch of 64 decode rows split over the ranks (8 per GPU at 8); each rank
     # streams its K/V shard (17.18 GB / N).
     w5 = WORKLOADS["decode_splitkv"]
@@ -605,7 +624,6 @@ def multi_gpu_extras(device, dist, rank, world, steps, e2e_args):
                  frac_of_n_x_hbm=r["value"] / (world * peaks()["hbm"]))
         extras["decode_shard"] = r
         torch.cuda.empty_cache()
-    return extras
 
 
 def main():

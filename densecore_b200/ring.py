@@ -208,10 +208,13 @@ class NcclCommunicator:
             if r:
                 raise RuntimeError("ncclGetUniqueId: " + lib.ncclGetErrorString(r).decode())
         if not single:
-            box = [bytes(uid.internal) if rank == 0 else None]
+            # The id's raw 128 bytes (reading the c_char array field would stop at its first NUL).
+            box = [ctypes.string_at(ctypes.addressof(uid), 128) if rank == 0 else None]
             src = dist.get_global_rank(group, 0) if group is not None else 0
             dist.broadcast_object_list(box, src=src, group=group)
             uid = UniqueId()
+            if len(box[0]) != 128:
+                raise RuntimeError("NCCL unique id broadcast returned a wrong size")
             ctypes.memmove(ctypes.addressof(uid), box[0], 128)
         comm = ctypes.c_void_p()
         with torch.cuda.device(device if device is not None else torch.cuda.current_device()):

@@ -33,7 +33,7 @@ def _train(T, F, model, steps, batches, device, dtype):
         opt.zero_grad()
         loss.backward()
         opt.step()
-        losses.append(float(loss))
+        losses.append(loss.item())
     return losses, {k: p.detach().double().cpu() for k, p in model.named_parameters()}
 
 
@@ -91,10 +91,11 @@ def test_run_module_drives_a_script(tmp_path):
         "m = make_gpt(torch, F, 65, 128, 2, 64).cuda()\n"
         "opt = torch.optim.SGD(m.parameters(), lr=0.1)\n"
         "x = torch.randint(0, 65, (2, 64), device='cuda')\n"
+        "y = torch.randint(0, 65, (2, 64), device='cuda')\n"
         "losses = []\n"
         "for _ in range(3):\n"
-        "    loss = m(x, x)\n"
-        "    opt.zero_grad(); loss.backward(); opt.step(); losses.append(float(loss))\n"
+        "    loss = m(x, y)\n"
+        "    opt.zero_grad(); loss.backward(); opt.step(); losses.append(loss.item())\n"
         "assert losses[-1] < losses[0], losses\n"
         "print('trained', sys.argv[1:], losses)\n")
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "tests")]))
