@@ -90,7 +90,7 @@ def kernel_work(w, name):
     gemm = 2.0 * D * pairs
     if name.startswith("fwd"):
         return 2 * gemm
-    if name == "bwd_tc":  # dK/dV and dQ (beside it, or after it from the stored dS): one record spans both
+    if name == "bwd_tc":  # dK/dV and dQ, run concurrently: one record spans both
         return 5 * gemm
     if "dkdv" in name:
         return 4 * gemm
@@ -463,7 +463,7 @@ def roofline_of(name, w, kernels, steps, ring, world, rank_amount):
     pk = peaks()
     # Kernels without a roofline of their own (the dropout mask draw: integer generator work,
     # neither HBM- nor tensor-bound) are named in "slowest_kernel" but are not the unit.
-    concurrent = ("bwd_dkdv_tc", "bwd_dq_tc", "bwd_dq_gemm") if "bwd_tc" in kernels else ()
+    concurrent = ("bwd_dkdv_tc", "bwd_dq_tc") if "bwd_tc" in kernels else ()
     candidates = {k_: v_ for k_, v_ in kernels.items() if k_ not in concurrent}
     slowest = max(candidates.items(), key=lambda kv: kv[1][1])[0] if candidates else None
     candidates = {k_: v_ for k_, v_ in candidates.items() if kernel_work(w, k_) > 0 or ring is not None}

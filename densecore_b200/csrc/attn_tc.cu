@@ -416,10 +416,11 @@ __global__ void __maxnreg__(128)
 #pragma unroll
                 for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(r[x]);
             }
-            if (!edge) {
-#pragma unroll
-                for (int c = 0; c < C::HB; c++) s[c] *= a.scale_log2;
-            } else {
+            // Interior blocks keep the raw scores and fold the scale into the exponent's FFMA
+            // (the max commutes with a positive scale); edge blocks scale, mask and fill first.
+            const bool raw = !edge && a.scale_log2 > 0.0f;
+            const float smul = raw ? a.scale_log2 : 1.0f;
+            if (!raw) {
 #pragma unroll
                 for (int c = 0; c < C::HB; c++) {
                     float x = s[c] * a.scale_log2;
@@ -427,7 +428,7 @@ __global__ void __maxnreg__(128)
                     s[c] = ((vbits >> c) & 1u) ? x : -INFINITY;
                 }
             }
-            float bmax = max_tree<C::HB>(s);
+            float bmax = max_tree<C::HB>(s) * smul;
             // The block's row max, shared with the partner thread (the other half) through
             // shared memory and an mbarrier (a bounded wait, unlike bar.sync).
             xmax[(bb * 2 + half) * C::BM + row] = bmax;
@@ -451,12 +452,16 @@ __global__ void __maxnreg__(128)
                 uint32_t phi[16], plo[16];
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
-                    const float pc = dead ? 0.0f : ex2_approx(s[r0 + c] - m);
+                    const float pc = dead ? 0.0f : ex2_approx(fmaf(s[r0 + c], smul, -m));
                     part[c & 3] += pc;
                     float pw = pc;
                     if constexpr (DROP) pw = ((kbits >> (r0 + c)) & 1u) ? pc * p.keep_scale : 0.0f;
-                    phi[c] = tf32_rna(pw);
-                    if (SPLIT) plo[c] = tf32_lo(pw, phi[c]);
+                    if (SPLIT) {
+                        phi[c] = __float_as_uint(pw);
+                        plo[c] = tf32_lo_trunc(pw);
+                    } else {
+                        phi[c] = tf32_rna(pw);
+                    }
                 }
                 tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
                 if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);

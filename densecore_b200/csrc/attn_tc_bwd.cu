@@ -215,10 +215,6 @@ struct TcBwdArgs {
     const float *lse2;  // (B*H, L) lse * log2(e), written by the pre-pass
     float scale_log2;
     int *err;
-    // When set (head dim 64, L % 4 == 0), the dK / dV kernel also stores dS^T, the TF32 hi and
-    // (with the 3xTF32 split) lo parts it hands the dK MMAs, as [B][H][S][L] (key rows of query
-    // columns) for the dQ GEMM; ds_lo follows ds_hi by B*H*S*L floats.
-    float *ds_hi;
 };
 
 // ================================================================= pre-pass ==========
@@ -602,10 +598,11 @@ __global__ void __maxnreg__(168)
                 tmem_wait_ld();
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
-                    float x = __uint_as_float(sr[c]) * a.scale_log2;
-                    if (MASKED) x += mk[MASKED ? r0 + c : 0] * LOG2E;
                     const float lse2 = __shfl_sync(FULL, cur_l, r0 + c);
-                    pv[r0 + c] = ((vbits >> (r0 + c)) & 1u) ? ex2_approx(x - lse2) : 0.0f;
+                    float x;
+                    if (MASKED) x = fmaf(mk[MASKED ? r0 + c : 0], LOG2E, __uint_as_float(sr[c]) * a.scale_log2) - lse2;
+                    else x = fmaf(__uint_as_float(sr[c]), a.scale_log2, -lse2);
+                    pv[r0 + c] = ((vbits >> (r0 + c)) & 1u) ? ex2_approx(x) : 0.0f;
                 }
             }
 #pragma unroll
@@ -615,8 +612,12 @@ __global__ void __maxnreg__(168)
                 for (int c = 0; c < 16; c++) {
                     float pw = pv[r0 + c];
                     if constexpr (DROP) pw = ((zb >> (r0 + c)) & 1u) ? pw * p.keep_scale : 0.0f;
-                    xh[c] = tf32_rna(pw);
-                    if (SPLIT) xl[c] = tf32_lo(pw, xh[c]);
+                    if (SPLIT) {
+                        xh[c] = __float_as_uint(pw);
+                        xl[c] = tf32_lo_trunc(pw);
+                    } else {
+                        xh[c] = tf32_rna(pw);
+                    }
                 }
                 tmem_st16(tl + C::C_S + cb + r0, xh);
                 if (SPLIT) tmem_st16(tl + C::C_PLO + cb + r0, xl);
@@ -640,28 +641,15 @@ __global__ void __maxnreg__(168)
                     float dpv = __uint_as_float(dr[c]);
                     if constexpr (DROP) dpv = ((zb >> (r0 + c)) & 1u) ? dpv * p.keep_scale : 0.0f;
                     const float ds = pv[r0 + c] * (dpv - del);
-                    xh[c] = tf32_rna(ds);
-                    if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
+                    if (SPLIT) {
+                        xh[c] = __float_as_uint(ds);
+                        xl[c] = tf32_lo_trunc(ds);
+                    } else {
+                        xh[c] = tf32_rna(ds);
+                    }
                 }
                 tmem_st16(tl + C::C_DP + cb + r0, xh);
                 if (SPLIT) tmem_st16(tl + C::C_DSLO + cb + r0, xl);
-                if (a.ds_hi != nullptr && key_ok) {
-                    // This key's 16 query columns of dS^T for the dQ GEMM: four 16-byte pieces per
-                    // part, each wholly below L or wholly past it (L % 4 == 0).
-                    const int64_t q = base + r0;
-                    float *dh = a.ds_hi + ((b * p.H + h) * p.S + key) * p.L + q;
-                    const int64_t lo_off = p.B * p.H * p.S * p.L;
-#pragma unroll
-                    for (int g4 = 0; g4 < 4; g4++) {
-                        if (q + 4 * g4 < p.L) {
-                            *reinterpret_cast<uint4 *>(dh + 4 * g4) =
-                                make_uint4(xh[4 * g4], xh[4 * g4 + 1], xh[4 * g4 + 2], xh[4 * g4 + 3]);
-                            if (SPLIT)
-                                *reinterpret_cast<uint4 *>(dh + lo_off + 4 * g4) =
-                                    make_uint4(xl[4 * g4], xl[4 * g4 + 1], xl[4 * g4 + 2], xl[4 * g4 + 3]);
-                        }
-                    }
-                }
             }
             tmem_wait_st();
             tc_fence_before();
@@ -1004,9 +992,10 @@ __global__ void __maxnreg__(168)
             mbar_arrive(bar(C::S_READ));
 #pragma unroll
             for (int c = 0; c < CPT; c++) {
-                float x = __uint_as_float(sr[c]) * a.scale_log2;
-                if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
-                pv[c] = ((vbits >> c) & 1u) ? ex2_approx(x - lse2) : 0.0f;
+                float x;
+                if (MASKED) x = fmaf(mk[MASKED ? c : 0], LOG2E, __uint_as_float(sr[c]) * a.scale_log2) - lse2;
+                else x = fmaf(__uint_as_float(sr[c]), a.scale_log2, -lse2);
+                pv[c] = ((vbits >> c) & 1u) ? ex2_approx(x) : 0.0f;
             }
             return true;
         };
@@ -1028,8 +1017,12 @@ __global__ void __maxnreg__(168)
                     float dpv = __uint_as_float(dr[c]);
                     if constexpr (DROP) dpv = ((zcur >> (r0 + c)) & 1u) ? dpv * p.keep_scale : 0.0f;
                     const float ds = pv[r0 + c] * (dpv - del);
-                    xh[c] = tf32_rna(ds);
-                    if (SPLIT) xl[c] = tf32_lo(ds, xh[c]);
+                    if (SPLIT) {
+                        xh[c] = __float_as_uint(ds);
+                        xl[c] = tf32_lo_trunc(ds);
+                    } else {
+                        xh[c] = tf32_rna(ds);
+                    }
                 }
                 tmem_st16(tl + C::C_DP + cb + r0, xh);
                 if (SPLIT) tmem_st16(tl + C::C_DSLO + cb + r0, xl);
@@ -1063,190 +1056,6 @@ __global__ void __maxnreg__(168)
     tc_fence_before();
     __syncthreads();
     if (warp == W_MMA) {
-        tc_fence_after();
-        tmem_dealloc(tmem, C::TCOLS);
-    }
-}
-
-// ================================================================ dQ from dS ========
-// Head dim 64: dQ = scale * dS K as a tensor-core GEMM over the dS^T tiles the dK / dV kernel
-// stored ([B][H][S][L], TF32 hi and lo), instead of a kernel that recomputes S and dP (two
-// GEMM-equivalents of the reference's five) to rebuild dS. A CTA owns 128 query rows of one
-// (batch, head); 64-key blocks stream through a two-stage ring: the dS^T tile as the A operand
-// (MN-major, query columns contiguous: the layout the dK / dV kernel writes) and the K tile as
-// the B operand (MN-major), hi and lo of each. Per block the MMA warp issues the three split
-// passes into one of two TMEM accumulators while four fold warps (one thread per query row)
-// add the other into fp32 registers. Under causal masking a query tile reads the keys below its
-// end only: every dS^T entry it reads was stored (as 0 where masked) by the dK / dV kernel.
-struct DqGemmCfg {
-    static constexpr int KB = 64;                       // keys per block
-    static constexpr uint32_t A_BYTES = TILE * KB * 4;  // dS^T tile: 128 queries x 64 keys
-    static constexpr uint32_t A_CHUNK = KB * 128;       // one 32-query chunk: 64 key rows of 128 bytes
-    static constexpr uint32_t B_BYTES = KB * 64 * 4;    // K tile: 64 keys x 64 dims
-    static constexpr uint32_t B_CHUNK = KB * 128;       // one 32-dim chunk
-    static constexpr int NST = 2;
-    static constexpr uint32_t OFF_ALO = A_BYTES, OFF_BHI = 2 * A_BYTES, OFF_BLO = 2 * A_BYTES + B_BYTES;
-    static constexpr uint32_t STAGE = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr uint32_t OFF_BAR = NST * STAGE;
-    enum { FULL = 0, EMPTY = NST, ACC_FULL = 2 * NST, ACC_FREE = ACC_FULL + 2, DRAIN = ACC_FREE + 2, NBAR };
-    static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-    static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
-    static constexpr uint32_t TCOLS = 128;  // two 64-column accumulators
-    static constexpr int THREADS = 192;     // warps 0-3 fold, 4 TMA producer, 5 MMA issuer
-    static constexpr int W_PROD = 4, W_MMA = 5;
-    static constexpr uint32_t IDESC = idesc_tf32(128, 64, 1, 1);
-    static_assert(SMEM <= 232448, "smem");
-};
-
-// tm_ds: (L, S, H, S2*B) over the stored dS^T (lo at batch B + b), box 32 queries x 64 keys,
-// 32-byte-atom swizzle; tm_kmn: (64, S, Hkv, S2*B) over the K hi / lo copies, box 64 keys,
-// 32-byte-atom swizzle.
-template <bool SPLIT>
-__global__ void __launch_bounds__(192)
-    attn_bwd_dq_gemm_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid_constant__ CUtensorMap tm_kmn,
-                            const TcBwdArgs a) {
-    using C = DqGemmCfg;
-    constexpr int KB = C::KB, NST = C::NST;
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw = smem_addr(smem_raw);
-    const uint32_t sb = (raw + 1023u) & ~1023u;
-    uint8_t *sg = smem_raw + (sb - raw);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const AttnProblem &p = a.p;
-    const int64_t ntiles = (p.L + TILE - 1) / TILE;
-    int64_t qt, bh;
-    grouped_tile(blockIdx.x, ntiles, p.B * p.H, qt, bh);
-    qt = ntiles - 1 - qt;  // under causal masking the last tiles read the most keys: first
-    const int64_t h = bh % p.H, b = bh / p.H, hk = h / p.group;
-    const int lo_b = (int)(p.B + b);
-    const int64_t q0 = qt * TILE;
-    const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
-    const int nblk = (int)((kv_end + KB - 1) / KB);
-    auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
-    volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
-    int *err = a.err;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < NST; s++) {
-            mbar_init(bar(C::FULL + s), 1);
-            mbar_init(bar(C::EMPTY + s), 1);
-        }
-        for (int s = 0; s < 2; s++) {
-            mbar_init(bar(C::ACC_FULL + s), 1);
-            mbar_init(bar(C::ACC_FREE + s), 128);
-        }
-        mbar_init(bar(C::DRAIN), 1);
-        *abort = 0;
-        fence_mbar_init();
-    }
-    if (warp == C::W_MMA) {
-        tmem_alloc(smem_addr(tmem_slot), C::TCOLS);
-        tmem_relinquish();
-    }
-    if (warp == C::W_PROD && lane == 0) {
-        prefetch_tmap(&tm_ds);
-        prefetch_tmap(&tm_kmn);
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == C::W_PROD) {
-        // ----------------------------------------------- producer: dS^T and K, hi and lo ----
-        if (lane == 0) {
-            int issued = -1;
-            for (int j = 0; j < nblk; j++) {
-                const int st = j % NST;
-                if (j >= NST && !mbar_wait(bar(C::EMPTY + st), ((j / NST) - 1) & 1, abort, err)) break;
-                const uint32_t base = sb + st * C::STAGE;
-                mbar_expect_tx(bar(C::FULL + st), (SPLIT ? 2 : 1) * (C::A_BYTES + C::B_BYTES));
-                for (int c = 0; c < 4; c++) {
-                    tma_load_4d(&tm_ds, base + c * C::A_CHUNK, bar(C::FULL + st), (int)q0 + 32 * c, j * KB, (int)h, (int)b);
-                    if (SPLIT)
-                        tma_load_4d(&tm_ds, base + C::OFF_ALO + c * C::A_CHUNK, bar(C::FULL + st), (int)q0 + 32 * c, j * KB,
-                                    (int)h, lo_b);
-                }
-                for (int c = 0; c < 2; c++) {
-                    tma_load_4d(&tm_kmn, base + C::OFF_BHI + c * C::B_CHUNK, bar(C::FULL + st), 32 * c, j * KB, (int)hk, (int)b);
-                    if (SPLIT)
-                        tma_load_4d(&tm_kmn, base + C::OFF_BLO + c * C::B_CHUNK, bar(C::FULL + st), 32 * c, j * KB, (int)hk,
-                                    lo_b);
-                }
-                issued = j;
-                if (*abort) break;
-            }
-            if (*abort) {  // let the copies in flight land before the CTA exits
-                volatile int never = 0;
-                for (int j = max(0, issued - NST + 1); j <= issued; j++)
-                    mbar_wait(bar(C::FULL + j % NST), (j / NST) & 1, &never, nullptr);
-            }
-        }
-    } else if (warp == C::W_MMA) {
-        // ---------------------------------------------------- MMA: dQ_blk = dS_blk K_blk ----
-        {
-            bool ok = true;
-            for (int j = 0; ok && j < nblk; j++) {
-                const int st = j % NST, ab = j & 1;
-                if (!warp_wait(bar(C::FULL + st), (j / NST) & 1, abort, err)) break;
-                if (j >= 2 && !warp_wait(bar(C::ACC_FREE + ab), ((j >> 1) - 1) & 1, abort, err)) break;
-                tc_fence_after();
-                const uint32_t base = sb + st * C::STAGE;
-                const uint64_t ahi = sdesc_mn_sw128_32b(base, C::A_CHUNK, 512);
-                const uint64_t alo = sdesc_mn_sw128_32b(base + C::OFF_ALO, C::A_CHUNK, 512);
-                const uint64_t bhi = sdesc_mn_sw128_32b(base + C::OFF_BHI, C::B_CHUNK, 512);
-                const uint64_t blo = sdesc_mn_sw128_32b(base + C::OFF_BLO, C::B_CHUNK, 512);
-                const uint32_t d = tmem + 64 * ab;
-                if (SPLIT) {  // the small cross terms first
-#pragma unroll
-                    for (int kk = 0; kk < KB / 8; kk++) {
-                        mma_tf32_ss_w(d, ahi + mnoff(kk), blo + mnoff(kk), C::IDESC, kk > 0 ? 1u : 0u);
-                        mma_tf32_ss_w(d, alo + mnoff(kk), bhi + mnoff(kk), C::IDESC, 1u);
-                    }
-                }
-#pragma unroll
-                for (int kk = 0; kk < KB / 8; kk++)
-                    mma_tf32_ss_w(d, ahi + mnoff(kk), bhi + mnoff(kk), C::IDESC, (SPLIT || kk > 0) ? 1u : 0u);
-                tc_commit_w(bar(C::ACC_FULL + ab));
-                tc_commit_w(bar(C::EMPTY + st));
-            }
-            // Every MMA this warp issued completes before TMEM is released.
-            tc_commit_w(bar(C::DRAIN));
-            volatile int never = 0;
-            warp_wait(bar(C::DRAIN), 0, &never, nullptr);
-        }
-    } else if (warp < C::W_PROD) {
-        // -------------------------------------------- fold: fp32 dQ row in registers ----
-        const int row = warp * 32 + lane;
-        const int64_t q = q0 + row;
-        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-        float acc[64];
-#pragma unroll
-        for (int x = 0; x < 64; x++) acc[x] = 0.0f;
-        bool ok = true;
-        for (int j = 0; j < nblk; j++) {
-            const int ab = j & 1;
-            if (!warp_wait(bar(C::ACC_FULL + ab), (j >> 1) & 1, abort, err)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; c++) fold16(tl + 64 * ab + 16 * c, acc + 16 * c);
-            tc_fence_before();
-            mbar_arrive(bar(C::ACC_FREE + ab));
-        }
-        const bool aborted = __any_sync(FULL, *abort != 0);
-        if (ok && !aborted && q < p.L) {
-            float *dqr = a.g.dq + b * a.g.dqs[0] + h * a.g.dqs[1] + q * a.g.dqs[2];
-            store_row<64>(dqr, a.g.dqs[3], acc, p.scale);
-        }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == C::W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TCOLS);
     }
@@ -1290,69 +1099,6 @@ F pick_kernel(bool split, bool masked, bool drop, F ttt, F ttf, F tft, F tff, F 
     return masked ? (drop ? ftt : ftf) : (drop ? fft : fff);
 }
 
-// Limit of the dS^T scratch the dQ GEMM path takes from the pool (hi and lo together).
-constexpr uint64_t kDsScratchBytes = 4ull << 30;
-
-// The head-dim-64 backward with dQ from stored dS^T: the dK / dV kernel (which also writes
-// dS^T hi / lo) and then the dQ GEMM, both on the caller's stream. `a` and `pa` come from the
-// pre-pass (pa's hi / lo copies stay alive in the caller's scratch until both kernels ran).
-int dkdv_then_dq_gemm(const AttnProblem &p, TcBwdArgs a, const PrepArgs &pa, bool split, bool masked, bool drop,
-                      cudaStream_t stream) {
-    constexpr int DD = 64;
-    using KC = KvCfg<DD>;
-    using GC = DqGemmCfg;
-    const int64_t S2 = split ? 2 : 1;
-    const int64_t ds_elems = p.B * p.H * p.S * p.L;
-    PoolScratch ds;
-    ds.stream = stream;
-    int st = pool_alloc(&ds.ptr, sizeof(float) * (size_t)(S2 * ds_elems), stream);
-    if (st) return st;
-    a.ds_hi = static_cast<float *>(ds.ptr);
-    const int64_t qst[3] = {p.H * p.L * DD, p.L * DD, DD}, kst[3] = {p.Hkv * p.S * DD, p.S * DD, DD};
-    const int64_t dst[3] = {p.H * p.S * p.L, p.S * p.L, p.L};  // (batch, head, key) strides of dS^T
-    const int64_t nb = S2 * p.B;
-    constexpr CUtensorMapSwizzle MN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    KernelTrace pair("bwd_tc", stream);
-    {
-        CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
-        st = make_tmap(&tk, pa.khl, DD, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tv, pa.vhl, DD, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tqk, pa.qhl, DD, p.L, p.H, nb, qst, KC::QB);
-        if (!st) st = make_tmap(&tqmn, pa.qhl, DD, p.L, p.H, nb, qst, KC::QB, MN);
-        if (!st) st = make_tmap(&tdok, pa.dohl, DD, p.L, p.H, nb, qst, KC::QB);
-        if (!st) st = make_tmap(&tdomn, pa.dohl, DD, p.L, p.H, nb, qst, KC::QB, MN);
-        if (st) return st;
-        auto kernel = pick_kernel(split, masked, drop, attn_bwd_dkdv_tc_kernel<DD, true, true, true>,
-                                  attn_bwd_dkdv_tc_kernel<DD, true, true, false>,
-                                  attn_bwd_dkdv_tc_kernel<DD, true, false, true>,
-                                  attn_bwd_dkdv_tc_kernel<DD, true, false, false>,
-                                  attn_bwd_dkdv_tc_kernel<DD, false, true, true>,
-                                  attn_bwd_dkdv_tc_kernel<DD, false, true, false>,
-                                  attn_bwd_dkdv_tc_kernel<DD, false, false, true>,
-                                  attn_bwd_dkdv_tc_kernel<DD, false, false, false>);
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)KC::SMEM);
-        if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
-        const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B * KC::NH);
-        KernelTrace tr("bwd_dkdv_tc", stream);
-        kernel<<<grid, THREADS, KC::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
-        if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
-    }
-    {
-        CUtensorMap tds, tkmn;
-        st = make_tmap(&tds, a.ds_hi, p.L, p.S, p.H, nb, dst, GC::KB, MN);
-        if (!st) st = make_tmap(&tkmn, pa.khl, DD, p.S, p.Hkv, nb, kst, GC::KB, MN);
-        if (st) return st;
-        auto kernel = split ? attn_bwd_dq_gemm_kernel<true> : attn_bwd_dq_gemm_kernel<false>;
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GC::SMEM);
-        if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_gemm smem attribute");
-        const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B);
-        KernelTrace tr("bwd_dq_gemm", stream);
-        kernel<<<grid, GC::THREADS, GC::SMEM, stream>>>(tds, tkmn, a);
-        if ((st = check_launch("attn_bwd_dq_gemm"))) return st;
-    }
-    return DC_OK;
-}
-
 template <int DD>
 int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
     using KC = KvCfg<DD>;
@@ -1389,7 +1135,6 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     a.lse2 = pa.lse2;
     a.scale_log2 = p.scale * LOG2E;
     a.err = device_error_word();
-    a.ds_hi = nullptr;
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
     // Strides (batch, head, row) of the contiguous hi / lo copies.
     const int64_t qst[3] = {p.H * p.L * DD, p.L * DD, DD}, kst[3] = {p.Hkv * p.S * DD, p.S * DD, DD};
@@ -1397,13 +1142,6 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     const bool masked = p.mask_kind != MASK_NONE;
     const bool drop = p.keep != nullptr;
     constexpr CUtensorMapSwizzle MN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    // Head dim 64: dQ from the stored dS^T by a GEMM after the dK / dV kernel, when the dS^T
-    // scratch (hi and lo, B*H*S*L floats each) stays within kDsScratchBytes; otherwise the dQ
-    // kernel that recomputes S and dP runs beside dK / dV.
-    const int64_t ds_elems = p.B * p.H * p.S * p.L;
-    const bool dq_gemm = DD == 64 && p.L > 0 && p.S > 0 && p.L % 4 == 0 &&
-                         (uint64_t)ds_elems * S2 * sizeof(float) <= kDsScratchBytes;
-    if (dq_gemm) return dkdv_then_dq_gemm(p, a, pa, split, masked, drop, stream);
     // The two tensor-core kernels run concurrently; with tracing on, this record spans both
     // (from before the fork to after the join, on the caller's stream).
     KernelTrace pair("bwd_tc", stream);

@@ -293,5 +293,15 @@ __device__ __forceinline__ uint32_t tf32_lo(float x, uint32_t hi) {
     return __float_as_uint(x - __uint_as_float(hi));
 }
 
+// The 3xTF32 split with the high part truncated instead of rounded: hi = x itself (the
+// tensor core reads only its top 19 bits, i.e. x with the 13 low mantissa bits cleared), lo =
+// x minus that truncation, exact in fp32 and of x's sign, below one TF32 ulp of x. The tensor
+// core truncates lo in turn, which errs by less than 2^-11 of lo (2^-21 of x) toward zero.
+// One LOP and one FADD instead of the two integer ops of the rounding plus the FADD; used for
+// the softmax warps' P and dS splits, where those ops sit on the critical path.
+__device__ __forceinline__ uint32_t tf32_lo_trunc(float x) {
+    return __float_as_uint(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+}
+
 }  // namespace sm100
 }  // namespace dc

@@ -47,7 +47,6 @@ def test_kernel_attribution_sums_to_the_step(name):
     pair = bench.kernel_work(w, "bwd_tc")
     assert fwd + pair == pytest.approx(total)
     assert bench.kernel_work(w, "bwd_dkdv_tc") + bench.kernel_work(w, "bwd_dq_tc") == pytest.approx(pair)
-    assert bench.kernel_work(w, "bwd_dq_gemm") == bench.kernel_work(w, "bwd_dq_tc")  # the two dQ variants
     # the pre-pass and the mask draw carry no algorithmic flops of their own
     assert bench.kernel_work(w, "bwd_prep") == 0.0
     assert bench.kernel_work(w, "dropout_keep_bits") == 0.0
