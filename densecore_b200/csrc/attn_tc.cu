@@ -10,9 +10,10 @@
 //               B operand); V uses the 32-byte-atom 128-byte swizzle, the only layout tf32
 //               accepts for an MN-major operand.
 //   warps 10-13 converters: Q goes into TMEM as tf32 hi / lo (the A operand of S = Q K^T, so
-//               the S MMAs read only K from shared memory); each landed K / V tile x is split
-//               in place into hi = tf32(x) and lo = tf32(x - hi) (3xTF32: a*b ~ ah*bh + ah*bl
-//               + al*bh keeps fp32-class accuracy on the TF32 tensor cores).
+//               the S MMAs read only K from shared memory); each landed K / V tile x stays as
+//               the hi operand (the tensor core reads x truncated to TF32) and its lo part
+//               x - trunc(x) is written beside it (3xTF32: a*b ~ ah*bh + ah*bl + al*bh keeps
+//               fp32-class accuracy on the TF32 tensor cores).
 //   warps 9, 14 MMA issuers (whole warps, one elected lane issuing; descriptors precomputed): warp 9 issues
 //               S_j = Q K_j^T into one of two TMEM buffers, warp 14 O_blk = P_j V_j with P read
 //               from TMEM. With two issuers one warp's barrier waits overlap the other's
@@ -117,27 +118,25 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) 
     else tmem_st16(taddr, r);
 }
 
-// hi = tf32(x) in place and, with SPLIT, lo = x - hi (tf32_lo) `lo_off` bytes further.
-// Single-pass TF32 rounds to nearest here rather than letting the tensor core drop the low
-// mantissa bits (which would bias every operand toward zero).
+// 3xTF32 (SPLIT): the landed tile x stays in place as the hi operand (the tensor core reads
+// x truncated to TF32) and lo = x - trunc(x), exact, goes `lo_off` bytes further. Single-pass
+// TF32 rounds x to nearest in place instead of letting the tensor core drop the low mantissa
+// bits (which would bias every operand toward zero).
 template <bool SPLIT>
 __device__ __forceinline__ void split_tile(uint8_t *hi, uint32_t lo_off, uint32_t bytes, int t) {
     for (uint32_t i = t; i < bytes / 16; i += 128) {
         float4 *ph = reinterpret_cast<float4 *>(hi) + i;
         const float4 x = *ph;
-        float4 hv;
-        hv.x = __uint_as_float(tf32_rna(x.x));
-        hv.y = __uint_as_float(tf32_rna(x.y));
-        hv.z = __uint_as_float(tf32_rna(x.z));
-        hv.w = __uint_as_float(tf32_rna(x.w));
-        *ph = hv;
         if (SPLIT) {
-            float4 lv;
-            lv.x = __uint_as_float(tf32_lo(x.x, __float_as_uint(hv.x)));
-            lv.y = __uint_as_float(tf32_lo(x.y, __float_as_uint(hv.y)));
-            lv.z = __uint_as_float(tf32_lo(x.z, __float_as_uint(hv.z)));
-            lv.w = __uint_as_float(tf32_lo(x.w, __float_as_uint(hv.w)));
-            *(reinterpret_cast<float4 *>(hi + lo_off) + i) = lv;
+            *(reinterpret_cast<uint4 *>(hi + lo_off) + i) =
+                make_uint4(tf32_lo_trunc(x.x), tf32_lo_trunc(x.y), tf32_lo_trunc(x.z), tf32_lo_trunc(x.w));
+        } else {
+            float4 hv;
+            hv.x = __uint_as_float(tf32_rna(x.x));
+            hv.y = __uint_as_float(tf32_rna(x.y));
+            hv.z = __uint_as_float(tf32_rna(x.z));
+            hv.w = __uint_as_float(tf32_rna(x.w));
+            *ph = hv;
         }
     }
 }
@@ -156,7 +155,8 @@ __device__ __forceinline__ float max_tree(const float (&v)[N]) {
 }
 
 // Row `row` of a raw 128-byte-swizzled tile (rows of 128-byte chunks, chunk stride
-// `chunk_bytes`) into TMEM: tf32 hi at col_hi and, with SPLIT, lo at col_lo.
+// `chunk_bytes`) into TMEM: with SPLIT the raw values as hi at col_hi and the exact remainder of
+// their TF32 truncation as lo at col_lo; without, the rounded TF32 values at col_hi.
 template <int CHUNKS, bool SPLIT>
 __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_bytes, int row, uint32_t tlane,
                                             uint32_t col_hi, uint32_t col_lo) {
@@ -170,8 +170,12 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_b
             const float v[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                hi[4 * g + e] = tf32_rna(v[e]);
-                if (SPLIT) lo[4 * g + e] = tf32_rna(v[e] - __uint_as_float(hi[4 * g + e]));
+                if (SPLIT) {
+                    hi[4 * g + e] = __float_as_uint(v[e]);
+                    lo[4 * g + e] = tf32_lo_trunc(v[e]);
+                } else {
+                    hi[4 * g + e] = tf32_rna(v[e]);
+                }
             }
         }
         tmem_st32(tlane + col_hi + 32 * c, hi);

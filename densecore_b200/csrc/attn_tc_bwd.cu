@@ -221,10 +221,14 @@ struct TcBwdArgs {
 struct PrepArgs {
     AttnProblem p;
     AttnGrads g;
-    float *qhl, *dohl, *khl, *vhl;  // [S2][B][heads][rows][64] contiguous: hi, then lo
-    float *lse2;                    // [B*H][L]
+    // [S2][B][heads][rows][DD] contiguous: hi, then lo; with lo_only, [B][heads][rows][DD] of lo
+    float *qhl, *dohl, *khl, *vhl;
+    float *lse2;  // [B*H][L]
     int split;
-    int vec;  // every input row is 16-byte aligned with unit inner stride
+    int vec;      // every input row is 16-byte aligned with unit inner stride
+    // The kernels read the hi operand from the inputs themselves (the tensor core reads their
+    // top 19 bits: x truncated to TF32); write only lo = x - trunc(x), exact in fp32.
+    int lo_only;
 };
 
 __device__ __forceinline__ float4 load4(const float *row, int64_t inner, int j, int vec) {
@@ -233,7 +237,12 @@ __device__ __forceinline__ float4 load4(const float *row, int64_t inner, int j, 
                        row[(4 * j + 3) * inner]);
 }
 
-__device__ __forceinline__ void split_store(float *hl, int64_t at, int64_t lo_off, float4 x, int split) {
+__device__ __forceinline__ void split_store(float *hl, int64_t at, int64_t lo_off, float4 x, int split, int lo_only) {
+    if (lo_only) {
+        *reinterpret_cast<uint4 *>(hl + at) =
+            make_uint4(tf32_lo_trunc(x.x), tf32_lo_trunc(x.y), tf32_lo_trunc(x.z), tf32_lo_trunc(x.w));
+        return;
+    }
     float4 h;
     h.x = __uint_as_float(tf32_rna(x.x));
     h.y = __uint_as_float(tf32_rna(x.y));
@@ -268,8 +277,8 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
         float s = fmaf(d4.w, o4.w, fmaf(d4.z, o4.z, fmaf(d4.y, o4.y, d4.x * o4.x)));
 #pragma unroll
         for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(group_mask, s, o);
-        split_store(a.qhl, r * DD + 4 * j, rows_a * DD, q4, a.split);
-        split_store(a.dohl, r * DD + 4 * j, rows_a * DD, d4, a.split);
+        split_store(a.qhl, r * DD + 4 * j, rows_a * DD, q4, a.split, a.lo_only);
+        split_store(a.dohl, r * DD + 4 * j, rows_a * DD, d4, a.split, a.lo_only);
         if (j == 0) {
             a.g.delta[r] = s;
             a.lse2[r] = p.lse[b * p.ls[0] + h * p.ls[1] + l * p.ls[2]] * LOG2E;
@@ -279,8 +288,8 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
         const int64_t sidx = rr % p.S, bh = rr / p.S, hk = bh % p.Hkv, b = bh / p.Hkv;
         const float4 k4 = load4(p.k + b * p.ks[0] + hk * p.ks[1] + sidx * p.ks[2], p.ks[3], j, a.vec);
         const float4 v4 = load4(p.v + b * p.vs[0] + hk * p.vs[1] + sidx * p.vs[2], p.vs[3], j, a.vec);
-        split_store(a.khl, rr * DD + 4 * j, rows_b * DD, k4, a.split);
-        split_store(a.vhl, rr * DD + 4 * j, rows_b * DD, v4, a.split);
+        split_store(a.khl, rr * DD + 4 * j, rows_b * DD, k4, a.split, a.lo_only);
+        split_store(a.vhl, rr * DD + 4 * j, rows_b * DD, v4, a.split, a.lo_only);
     }
 }
 
@@ -337,6 +346,9 @@ __global__ void __maxnreg__(168)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_qmn,
                             const __grid_constant__ CUtensorMap tm_dok, const __grid_constant__ CUtensorMap tm_domn,
+                            const __grid_constant__ CUtensorMap tm_k_lo, const __grid_constant__ CUtensorMap tm_v_lo,
+                            const __grid_constant__ CUtensorMap tm_qk_lo, const __grid_constant__ CUtensorMap tm_qmn_lo,
+                            const __grid_constant__ CUtensorMap tm_dok_lo, const __grid_constant__ CUtensorMap tm_domn_lo,
                             const TcBwdArgs a) {
     using C = KvCfg<DD>;
     constexpr int QB = C::QB, CPT = C::CPT;
@@ -352,7 +364,6 @@ __global__ void __maxnreg__(168)
     const int dh = (int)(bhd % C::NH);  // gradient column half
     const int64_t bh = bhd / C::NH;
     const int64_t hk = bh % p.Hkv, b = bh / p.Hkv, k0 = kt * TILE;
-    const int lo_b = (int)(p.B + b);  // batch coordinate of the lo copies
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
     const int64_t r_begin = p.causal ? min(k0, p.L) : 0;
     const int qb_first = (int)(r_begin / QB);
@@ -396,7 +407,7 @@ __global__ void __maxnreg__(168)
 
     // One streamed tile (hi and, with SPLIT, lo) of query block i into a stage: all DD columns
     // (K-major) or this CTA's 64-column half (MN-major).
-    auto load_tile = [&](const CUtensorMap *tm, uint32_t stage, uint32_t full, int i, bool mn) {
+    auto load_tile = [&](const CUtensorMap *tm, const CUtensorMap *tm_lo, uint32_t stage, uint32_t full, int i, bool mn) {
         int64_t h, q0;
         blk_coords(i, h, q0);
         const int nch = mn ? 2 : DD / 32;
@@ -405,7 +416,7 @@ __global__ void __maxnreg__(168)
         mbar_expect_tx(full, (SPLIT ? 2 : 1) * bytes);
         for (int c = 0; c < nch; c++) {
             tma_load_4d(tm, stage + c * chunk, full, col0 + 32 * c, (int)q0, (int)h, (int)b);
-            if (SPLIT) tma_load_4d(tm, stage + bytes + c * chunk, full, col0 + 32 * c, (int)q0, (int)h, lo_b);
+            if (SPLIT) tma_load_4d(tm_lo, stage + bytes + c * chunk, full, col0 + 32 * c, (int)q0, (int)h, (int)b);
         }
     };
 
@@ -419,8 +430,8 @@ __global__ void __maxnreg__(168)
                 tma_load_4d(&tm_k, sb + C::OFF_KHI_STAGE + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 tma_load_4d(&tm_v, sb + C::OFF_VHI_STAGE + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 if (SPLIT && !lo_later) {
-                    tma_load_4d(&tm_k, sb + C::OFF_KLO + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
-                    tma_load_4d(&tm_v, sb + C::OFF_VLO + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                    tma_load_4d(&tm_k_lo, sb + C::OFF_KLO + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                    tma_load_4d(&tm_v_lo, sb + C::OFF_VLO + c * RES_CHUNK, bar(C::KV_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 }
             }
             if (!SPLIT || !lo_later) mbar_arrive(bar(C::KVLO_FULL));
@@ -428,16 +439,16 @@ __global__ void __maxnreg__(168)
             if (ok && SPLIT && lo_later) {
                 mbar_expect_tx(bar(C::KVLO_FULL), 2 * C::RESB);
                 for (int c = 0; c < DD / 32; c++) {
-                    tma_load_4d(&tm_k, sb + C::OFF_KLO + c * RES_CHUNK, bar(C::KVLO_FULL), 32 * c, (int)k0, (int)hk, lo_b);
-                    tma_load_4d(&tm_v, sb + C::OFF_VLO + c * RES_CHUNK, bar(C::KVLO_FULL), 32 * c, (int)k0, (int)hk, lo_b);
+                    tma_load_4d(&tm_k_lo, sb + C::OFF_KLO + c * RES_CHUNK, bar(C::KVLO_FULL), 32 * c, (int)k0, (int)hk, (int)b);
+                    tma_load_4d(&tm_v_lo, sb + C::OFF_VLO + c * RES_CHUNK, bar(C::KVLO_FULL), 32 * c, (int)k0, (int)hk, (int)b);
                 }
             }
             for (int i = 0; ok && i < nblk; i++) {
                 if (i >= 1 && !mbar_wait(bar(C::QK_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_qk, sb + C::OFF_QK, bar(C::QK_FULL), i, false);
+                load_tile(&tm_qk, &tm_qk_lo, sb + C::OFF_QK, bar(C::QK_FULL), i, false);
                 qk_issued = i;
                 if (i >= 1 && !mbar_wait(bar(C::DOK_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_dok, sb + C::OFF_DOK, bar(C::DOK_FULL), i, false);
+                load_tile(&tm_dok, &tm_dok_lo, sb + C::OFF_DOK, bar(C::DOK_FULL), i, false);
                 dok_issued = i;
             }
             if (*abort) {  // let the copies in flight land before the CTA exits
@@ -454,10 +465,10 @@ __global__ void __maxnreg__(168)
             int domn_issued = -1, qmn_issued = -1;
             for (int i = 0; i < nblk; i++) {
                 if (i >= 1 && !mbar_wait(bar(C::DOMN_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_domn, sb + C::OFF_DOMN, bar(C::DOMN_FULL), i, true);
+                load_tile(&tm_domn, &tm_domn_lo, sb + C::OFF_DOMN, bar(C::DOMN_FULL), i, true);
                 domn_issued = i;
                 if (i >= 1 && !mbar_wait(bar(C::QMN_EMPTY), (i - 1) & 1, abort, err)) break;
-                load_tile(&tm_qmn, sb + C::OFF_QMN, bar(C::QMN_FULL), i, true);
+                load_tile(&tm_qmn, &tm_qmn_lo, sb + C::OFF_QMN, bar(C::QMN_FULL), i, true);
                 qmn_issued = i;
                 if (*abort) break;
             }
@@ -736,7 +747,10 @@ template <int DD, bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(168)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_kk, const __grid_constant__ CUtensorMap tm_kmn,
-                          const __grid_constant__ CUtensorMap tm_vk, const TcBwdArgs a) {
+                          const __grid_constant__ CUtensorMap tm_vk, const __grid_constant__ CUtensorMap tm_q_lo,
+                          const __grid_constant__ CUtensorMap tm_do_lo, const __grid_constant__ CUtensorMap tm_kk_lo,
+                          const __grid_constant__ CUtensorMap tm_kmn_lo, const __grid_constant__ CUtensorMap tm_vk_lo,
+                          const TcBwdArgs a) {
     using C = QqCfg<DD>;
     constexpr int NB = C::NB, CPT = C::CPT, NST_K = C::NST_K, NST_G = C::NST_G;
     extern __shared__ uint8_t smem_raw[];
@@ -753,7 +767,6 @@ __global__ void __maxnreg__(168)
     const int dh = (int)(bhd % C::NH);  // dQ column half
     const int64_t bh = bhd / C::NH;
     const int64_t h = bh % p.H, b = bh / p.H, hk = h / p.group;
-    const int lo_b = (int)(p.B + b);
     const int64_t q0 = qt * TILE;
     const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
     const int nblk = (int)((kv_end + NB - 1) / NB);
@@ -806,8 +819,8 @@ __global__ void __maxnreg__(168)
                 tma_load_4d(&tm_q, sb + C::OFF_QHI_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 tma_load_4d(&tm_do, sb + C::OFF_DOHI_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 if (lo_now) {
-                    tma_load_4d(&tm_q, sb + C::OFF_QLO_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
-                    tma_load_4d(&tm_do, sb + C::OFF_DOLO_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                    tma_load_4d(&tm_q_lo, sb + C::OFF_QLO_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_do_lo, sb + C::OFF_DOLO_STAGE + c * RES_CHUNK, bar(C::QD_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 }
             }
             if (!(SPLIT && !C::LO_TMEM)) mbar_arrive(bar(C::QDLO_FULL));
@@ -816,8 +829,8 @@ __global__ void __maxnreg__(168)
             if (lo_later) {
                 mbar_expect_tx(bar(C::QDLO_FULL), 2 * C::RESB);
                 for (int c = 0; c < DD / 32; c++) {
-                    tma_load_4d(&tm_q, sb + C::OFF_QLO + c * RES_CHUNK, bar(C::QDLO_FULL), 32 * c, (int)q0, (int)h, lo_b);
-                    tma_load_4d(&tm_do, sb + C::OFF_DOLO + c * RES_CHUNK, bar(C::QDLO_FULL), 32 * c, (int)q0, (int)h, lo_b);
+                    tma_load_4d(&tm_q_lo, sb + C::OFF_QLO + c * RES_CHUNK, bar(C::QDLO_FULL), 32 * c, (int)q0, (int)h, (int)b);
+                    tma_load_4d(&tm_do_lo, sb + C::OFF_DOLO + c * RES_CHUNK, bar(C::QDLO_FULL), 32 * c, (int)q0, (int)h, (int)b);
                 }
             }
             for (int j = 0; ok && j < nblk; j++) {
@@ -827,7 +840,7 @@ __global__ void __maxnreg__(168)
                 for (int c = 0; c < DD / 32; c++) {
                     const uint32_t o = C::OFF_KK + st * C::KSTAGE + c * C::TK_CHUNK;
                     tma_load_4d(&tm_kk, sb + o, bar(C::KK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_kk, sb + o + C::TK_BYTES, bar(C::KK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
+                    if (SPLIT) tma_load_4d(&tm_kk_lo, sb + o + C::TK_BYTES, bar(C::KK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
                 }
                 k_issued = j;
                 if (j >= NST_K && !mbar_wait(bar(C::VK_EMPTY + st), ((j / NST_K) - 1) & 1, abort, err)) break;
@@ -835,7 +848,7 @@ __global__ void __maxnreg__(168)
                 for (int c = 0; c < DD / 32; c++) {
                     const uint32_t o = C::OFF_VK + st * C::KSTAGE + c * C::TK_CHUNK;
                     tma_load_4d(&tm_vk, sb + o, bar(C::VK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_vk, sb + o + C::TK_BYTES, bar(C::VK_FULL + st), 32 * c, j * NB, (int)hk, lo_b);
+                    if (SPLIT) tma_load_4d(&tm_vk_lo, sb + o + C::TK_BYTES, bar(C::VK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
                 }
                 v_issued = j;
             }
@@ -862,7 +875,7 @@ __global__ void __maxnreg__(168)
                     const uint32_t o = C::OFF_KMN + st * C::GSTAGE + c * C::TM_CHUNK;
                     const int col = 64 * dh + 32 * c;
                     tma_load_4d(&tm_kmn, sb + o, bar(C::SG_FULL + st), col, j * NB, (int)hk, (int)b);
-                    if (SPLIT) tma_load_4d(&tm_kmn, sb + o + C::TM_BYTES, bar(C::SG_FULL + st), col, j * NB, (int)hk, lo_b);
+                    if (SPLIT) tma_load_4d(&tm_kmn_lo, sb + o + C::TM_BYTES, bar(C::SG_FULL + st), col, j * NB, (int)hk, (int)b);
                 }
                 issued = j;
                 if (*abort) break;
@@ -1099,14 +1112,42 @@ F pick_kernel(bool split, bool masked, bool drop, F ttt, F ttf, F tft, F tff, F 
     return masked ? (drop ? ftt : ftf) : (drop ? fft : fff);
 }
 
+// Whether the tensor-core kernels can read a (B, heads, rows, DD) input's rows themselves
+// through a TMA map: unit inner stride, 16-byte multiples for the other strides, 16-byte base.
+bool tma_readable(const float *ptr, int64_t B, int64_t heads, int64_t rows, const int64_t *st) {
+    return st[3] == 1 && tma_stride_ok(rows, st[2]) && tma_stride_ok(heads, st[1]) && tma_stride_ok(B, st[0]) &&
+           (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0;
+}
+
+// The hi and lo TMA maps of one operand. Copy mode: hi and lo in the pre-pass's contiguous
+// scratch (lo after hi). Raw mode: hi is the input itself (strides `ust`), lo the pre-pass's
+// lo-only scratch.
+struct HiLoMaps {
+    CUtensorMap hi, lo;
+};
+int make_hilo(HiLoMaps &m, bool raw, const float *input, const int64_t *ust, const float *scratch, int64_t DD,
+              int64_t rows, int64_t heads, int64_t B, int box, CUtensorMapSwizzle sw) {
+    const int64_t cst[3] = {heads * rows * DD, rows * DD, DD};
+    int st = raw ? make_tmap(&m.hi, input, DD, rows, heads, B, ust, box, sw)
+                 : make_tmap(&m.hi, scratch, DD, rows, heads, B, cst, box, sw);
+    if (st) return st;
+    const float *lo = raw ? scratch : scratch + B * heads * rows * DD;
+    return make_tmap(&m.lo, lo, DD, rows, heads, B, cst, box, sw);
+}
+
 template <int DD>
 int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cudaStream_t stream) {
     using KC = KvCfg<DD>;
     using QC = QqCfg<DD>;
     const bool split = precision != DC_PREC_TF32;
-    const int64_t S2 = split ? 2 : 1;
     const int64_t rows_a = p.B * p.H * p.L, rows_b = p.B * p.Hkv * p.S;
-    const size_t bytes = sizeof(float) * (size_t)(S2 * 2 * (rows_a + rows_b) * DD + rows_a);
+    // Raw mode (3xTF32 with TMA-readable q, k, v and grad_out): the kernels read the hi
+    // operands from the inputs and the pre-pass writes only the lo parts (half the scratch
+    // and the pre-pass's writes). Otherwise the pre-pass copies hi (rounded) and lo.
+    const bool raw = split && tma_readable(p.q, p.B, p.H, p.L, p.qs) && tma_readable(p.k, p.B, p.Hkv, p.S, p.ks) &&
+                     tma_readable(p.v, p.B, p.Hkv, p.S, p.vs) && tma_readable(g.dout, p.B, p.H, p.L, g.dos);
+    const int64_t NC = raw ? 1 : (split ? 2 : 1);  // copies per operand in the scratch
+    const size_t bytes = sizeof(float) * (size_t)(NC * 2 * (rows_a + rows_b) * DD + rows_a);
     PoolScratch ws;
     ws.stream = stream;
     int st = pool_alloc(&ws.ptr, bytes, stream);
@@ -1115,11 +1156,12 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     pa.p = p;
     pa.g = g;
     pa.qhl = static_cast<float *>(ws.ptr);
-    pa.dohl = pa.qhl + S2 * rows_a * DD;
-    pa.khl = pa.dohl + S2 * rows_a * DD;
-    pa.vhl = pa.khl + S2 * rows_b * DD;
-    pa.lse2 = pa.vhl + S2 * rows_b * DD;
+    pa.dohl = pa.qhl + NC * rows_a * DD;
+    pa.khl = pa.dohl + NC * rows_a * DD;
+    pa.vhl = pa.khl + NC * rows_b * DD;
+    pa.lse2 = pa.vhl + NC * rows_b * DD;
     pa.split = split ? 1 : 0;
+    pa.lo_only = raw ? 1 : 0;
     pa.vec = rows_vec(p.q, p.qs) && rows_vec(p.k, p.ks) && rows_vec(p.v, p.vs) && rows_vec(g.dout, g.dos) &&
              rows_vec(p.out, p.os);
     if (rows_a + rows_b > 0) {
@@ -1136,12 +1178,21 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     a.scale_log2 = p.scale * LOG2E;
     a.err = device_error_word();
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
-    // Strides (batch, head, row) of the contiguous hi / lo copies.
-    const int64_t qst[3] = {p.H * p.L * DD, p.L * DD, DD}, kst[3] = {p.Hkv * p.S * DD, p.S * DD, DD};
-    const int64_t nb = S2 * p.B;
     const bool masked = p.mask_kind != MASK_NONE;
     const bool drop = p.keep != nullptr;
-    constexpr CUtensorMapSwizzle MN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    constexpr CUtensorMapSwizzle KM = CU_TENSOR_MAP_SWIZZLE_128B, MN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    auto q_maps = [&](HiLoMaps &m, int box, CUtensorMapSwizzle sw) {
+        return make_hilo(m, raw, p.q, p.qs, pa.qhl, DD, p.L, p.H, p.B, box, sw);
+    };
+    auto do_maps = [&](HiLoMaps &m, int box, CUtensorMapSwizzle sw) {
+        return make_hilo(m, raw, g.dout, g.dos, pa.dohl, DD, p.L, p.H, p.B, box, sw);
+    };
+    auto k_maps = [&](HiLoMaps &m, int box, CUtensorMapSwizzle sw) {
+        return make_hilo(m, raw, p.k, p.ks, pa.khl, DD, p.S, p.Hkv, p.B, box, sw);
+    };
+    auto v_maps = [&](HiLoMaps &m, int box, CUtensorMapSwizzle sw) {
+        return make_hilo(m, raw, p.v, p.vs, pa.vhl, DD, p.S, p.Hkv, p.B, box, sw);
+    };
     // The two tensor-core kernels run concurrently; with tracing on, this record spans both
     // (from before the fork to after the join, on the caller's stream).
     KernelTrace pair("bwd_tc", stream);
@@ -1153,13 +1204,13 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     }
     StreamJoin join(stream, side);  // joins side back into stream on every return below
     if (p.S > 0) {
-        CUtensorMap tk, tv, tqk, tqmn, tdok, tdomn;
-        st = make_tmap(&tk, pa.khl, DD, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tv, pa.vhl, DD, p.S, p.Hkv, nb, kst, TILE);
-        if (!st) st = make_tmap(&tqk, pa.qhl, DD, p.L, p.H, nb, qst, KC::QB);
-        if (!st) st = make_tmap(&tqmn, pa.qhl, DD, p.L, p.H, nb, qst, KC::QB, MN);
-        if (!st) st = make_tmap(&tdok, pa.dohl, DD, p.L, p.H, nb, qst, KC::QB);
-        if (!st) st = make_tmap(&tdomn, pa.dohl, DD, p.L, p.H, nb, qst, KC::QB, MN);
+        HiLoMaps tk, tv, tqk, tqmn, tdok, tdomn;
+        st = k_maps(tk, TILE, KM);
+        if (!st) st = v_maps(tv, TILE, KM);
+        if (!st) st = q_maps(tqk, KC::QB, KM);
+        if (!st) st = q_maps(tqmn, KC::QB, MN);
+        if (!st) st = do_maps(tdok, KC::QB, KM);
+        if (!st) st = do_maps(tdomn, KC::QB, MN);
         if (st) return st;
         auto kernel = pick_kernel(split, masked, drop, attn_bwd_dkdv_tc_kernel<DD, true, true, true>,
                                   attn_bwd_dkdv_tc_kernel<DD, true, true, false>,
@@ -1173,16 +1224,17 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
         const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B * KC::NH);
         KernelTrace tr("bwd_dkdv_tc", stream);
-        kernel<<<grid, THREADS, KC::SMEM, stream>>>(tk, tv, tqk, tqmn, tdok, tdomn, a);
+        kernel<<<grid, THREADS, KC::SMEM, stream>>>(tk.hi, tv.hi, tqk.hi, tqmn.hi, tdok.hi, tdomn.hi, tk.lo, tv.lo,
+                                                     tqk.lo, tqmn.lo, tdok.lo, tdomn.lo, a);
         if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
     }
     if (p.L > 0) {
-        CUtensorMap tq, tdo, tkk, tkmn, tvk;
-        st = make_tmap(&tq, pa.qhl, DD, p.L, p.H, nb, qst, TILE);
-        if (!st) st = make_tmap(&tdo, pa.dohl, DD, p.L, p.H, nb, qst, TILE);
-        if (!st) st = make_tmap(&tkk, pa.khl, DD, p.S, p.Hkv, nb, kst, QC::NB);
-        if (!st) st = make_tmap(&tkmn, pa.khl, DD, p.S, p.Hkv, nb, kst, QC::NB, MN);
-        if (!st) st = make_tmap(&tvk, pa.vhl, DD, p.S, p.Hkv, nb, kst, QC::NB);
+        HiLoMaps tq, tdo, tkk, tkmn, tvk;
+        st = q_maps(tq, TILE, KM);
+        if (!st) st = do_maps(tdo, TILE, KM);
+        if (!st) st = k_maps(tkk, QC::NB, KM);
+        if (!st) st = k_maps(tkmn, QC::NB, MN);
+        if (!st) st = v_maps(tvk, QC::NB, KM);
         if (st) return st;
         auto kernel = pick_kernel(split, masked, drop, attn_bwd_dq_tc_kernel<DD, true, true, true>,
                                   attn_bwd_dq_tc_kernel<DD, true, true, false>,
@@ -1197,7 +1249,8 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
         const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B * QC::NH);
         {
             KernelTrace tr("bwd_dq_tc", side);
-            kernel<<<grid, THREADS, QC::SMEM, side>>>(tq, tdo, tkk, tkmn, tvk, a);
+            kernel<<<grid, THREADS, QC::SMEM, side>>>(tq.hi, tdo.hi, tkk.hi, tkmn.hi, tvk.hi, tq.lo, tdo.lo, tkk.lo,
+                                                      tkmn.lo, tvk.lo, a);
         }
         const int launched = check_launch("attn_bwd_dq_tc");
         if ((st = join.join())) return st;

@@ -311,3 +311,25 @@ def test_full_size_decode_sampled_rows():
         _assert_close(f"out {b},{h}", out[b:b + 1, h:h + 1].cpu().numpy(), ro, 1e-5)
     del k, v
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_with_inputs_tma_cannot_read(precision, D):
+    # Rows of D floats inside rows of D + 1: strides that are not 16-byte multiples and bases off
+    # 16-byte boundaries. The tensor-core backward then copies its hi and lo operands (in the
+    # 3xTF32 mode it otherwise reads hi from the inputs and copies lo only); both must agree with
+    # the oracle.
+    rng = np.random.default_rng(23)
+    B, H, L = 2, 3, 300
+    bases = [rng.normal(size=(B, H, L, D + 1)).astype(np.float32) for _ in range(4)]
+    ts = [_cuda(a)[..., 1:] for a in bases]
+    assert ts[0].stride(2) == D + 1
+    q, k, v = (t.clone().requires_grad_(True) for t in ts[:3])  # contiguous leaves for the forward
+    out, lse = dc._flash_attention(q.detach(), k.detach(), v.detach(), True)
+    dq, dk, dv = dc._flash_attention_backward(ts[3], ts[0], ts[1], ts[2], out, lse, True)
+    qn, kn, vn, gn = (np.ascontiguousarray(a[..., 1:]) for a in bases)
+    ro, rl = oracle.flash_forward(qn, kn, vn, causal=True)
+    ref = oracle.flash_backward(gn, qn, kn, vn, ro, rl, causal=True)
+    for nm, a, r in zip(("dq", "dk", "dv"), (dq, dk, dv), ref):
+        _assert_close(nm, a.cpu().numpy(), r, TOL[precision])
+    assert dc._lib.load().dc_device_status(0) == 0
