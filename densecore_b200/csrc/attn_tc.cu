@@ -4,7 +4,8 @@
 // 64 and 128 with a warp-specialised kernel; one CTA computes a 128-row query tile of one
 // (batch, head):
 //
-//   warp 8      TMA producer: the Q tile once, then K and V tiles of BN keys into 3-stage
+//   warp 8      TMA producer: the Q tile once (staged in the V ring, so that the K ring fills
+//               while the converters move Q into TMEM), then K and V tiles of BN keys into 3-stage
 //               shared-memory rings (4-D tensor maps over the caller's strided (B, H, L, E)
 //               views, zero fill past the sequence end). K uses the 128-byte swizzle (K-major
 //               B operand); V uses the 32-byte-atom 128-byte swizzle, the only layout tf32
@@ -95,7 +96,7 @@ struct FwdCfg {
     __host__ __device__ static constexpr uint32_t col_plo(int b) { return 2 * D + b * 2 * BN + BN; }
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(COLS_USED <= 512, "tensor memory budget");
-    static_assert(Q_BYTES <= KST * KV_STAGE, "the raw Q tile is staged in the K ring");
+    static_assert(Q_BYTES <= VST * KV_STAGE, "the raw Q tile is staged in the V ring");
     static_assert(HB == 16 || HB == 32, "softmax half-block width");
 };
 
@@ -250,11 +251,13 @@ __global__ void __maxnreg__(128)
         // ------------------------------------------------------------ TMA producer ----
         if (lane == 0) {
             int k_issued = -1, v_issued = -1;
-            // The raw Q tile lands in the K ring; the converters move it into TMEM.
+            // The raw Q tile lands in the V ring and the converters move it into TMEM; the K
+            // ring fills meanwhile (S_0 needs Q and K_0), and the first V load waits until Q has
+            // left the V ring.
             mbar_expect_tx(bar(C::Q_FULL), C::Q_BYTES);
             for (int c = 0; c < C::CHUNKS; c++)
-                tma_load_4d(&tmq, sb + C::OFF_K + c * C::Q_CHUNK, bar(C::Q_FULL), 32 * c, (int)q0, (int)h, (int)b);
-            bool ok = mbar_wait(bar(C::Q_READY), 0, abort, err);
+                tma_load_4d(&tmq, sb + C::OFF_V + c * C::Q_CHUNK, bar(C::Q_FULL), 32 * c, (int)q0, (int)h, (int)b);
+            bool ok = true;
             for (int j = 0; ok && j < nblk; j++) {
                 const int ks = j % C::KST, vs = j % C::VST;
                 if (j >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, err)) break;
@@ -263,6 +266,7 @@ __global__ void __maxnreg__(128)
                 for (int c = 0; c < C::CHUNKS; c++)
                     tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
                 k_issued = j;
+                if (j == 0 && !(ok = mbar_wait(bar(C::Q_READY), 0, abort, err))) break;
                 if (j >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, err)) break;
                 mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
                 const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
@@ -356,7 +360,7 @@ __global__ void __maxnreg__(128)
         const int ct = threadIdx.x - 32 * C::W_CVT;
         const int quad = warp & 3;
         if (mbar_wait(bar(C::Q_FULL), 0, abort, err)) {
-            row_to_tmem<C::CHUNKS, SPLIT>(sg + C::OFF_K, C::Q_CHUNK, quad * 32 + lane,
+            row_to_tmem<C::CHUNKS, SPLIT>(sg + C::OFF_V, C::Q_CHUNK, quad * 32 + lane,
                                           tmem + ((uint32_t)(quad * 32) << 16), C::COL_QHI, C::COL_QLO);
             tmem_wait_st();
             tc_fence_before();
