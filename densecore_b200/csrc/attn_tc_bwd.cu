@@ -310,13 +310,14 @@ struct KvCfg {
     static constexpr uint32_t TM_CHUNK = QB * 128;
     // Shared memory: K lo | V lo | Q_K | dO_K | dO_MN | Q_MN (hi + lo each), one stage per
     // streamed tile, each freed by its own reader. K hi and V hi wait for the softmax warps to
-    // move them into TMEM: DD = 64 in the Q_K and dO_K stages, DD = 128 in the K lo / V lo
-    // areas (whose lo copies are loaded after).
+    // move them into TMEM: DD = 64 in the Q_MN and dO_MN stages (the gradient MMAs need those
+    // tiles last, so the Q_K and dO_K tiles of the first S^T / dP^T load meanwhile), DD = 128
+    // in the K lo / V lo areas (whose lo copies are loaded after).
     static constexpr uint32_t OFF_KLO = 0, OFF_VLO = RESB, OFF_QK = 2 * RESB, OFF_DOK = OFF_QK + 2 * TK_BYTES,
                               OFF_DOMN = OFF_DOK + 2 * TK_BYTES, OFF_QMN = OFF_DOMN + 2 * TM_BYTES,
                               OFF_BAR = OFF_QMN + 2 * TM_BYTES;
-    static constexpr uint32_t OFF_KHI_STAGE = DD == 64 ? OFF_QK : OFF_KLO;
-    static constexpr uint32_t OFF_VHI_STAGE = DD == 64 ? OFF_DOK : OFF_VLO;
+    static constexpr uint32_t OFF_KHI_STAGE = DD == 64 ? OFF_QMN : OFF_KLO;
+    static constexpr uint32_t OFF_VHI_STAGE = DD == 64 ? OFF_DOMN : OFF_VLO;
     // Per block i: S^T (S_FULL) turned into P^T (P_READY); dP^T (DP_FULL) into dS^T (DS_READY);
     // dV (DV_DONE: P^T read, S^T_{i+1} may overwrite it) and dK (DK_DONE: dS^T read, dP^T_{i+1}
     // may overwrite it); DV_FREE / DK_FREE: the fold has read that accumulator. KVLO_FULL: the
@@ -330,7 +331,7 @@ struct KvCfg {
     static constexpr uint32_t C_KHI = 0, C_VHI = DD, C_S = 2 * DD, C_PLO = C_S + QB, C_DP = C_S + 2 * QB,
                               C_DSLO = C_S + 3 * QB, C_DV = C_S + 4 * QB, C_DK = C_DV + 64, TCOLS = 512;
     static_assert(C_DK + 64 <= TCOLS, "tensor memory budget");
-    static_assert(RESB <= 2 * TK_BYTES || DD != 64, "K / V hi are staged in the Q_K and dO_K stages");
+    static_assert(RESB <= 2 * TM_BYTES || DD != 64, "K / V hi are staged in the Q_MN and dO_MN stages");
     static_assert(SMEM <= 232448, "smem");
 };
 
@@ -435,7 +436,8 @@ __global__ void __maxnreg__(168)
                 }
             }
             if (!SPLIT || !lo_later) mbar_arrive(bar(C::KVLO_FULL));
-            bool ok = mbar_wait(bar(C::KV_READY), 0, abort, err);
+            // DD = 128 loads the lo copies where the hi tiles wait: after they left for TMEM.
+            bool ok = !lo_later || mbar_wait(bar(C::KV_READY), 0, abort, err);
             if (ok && SPLIT && lo_later) {
                 mbar_expect_tx(bar(C::KVLO_FULL), 2 * C::RESB);
                 for (int c = 0; c < DD / 32; c++) {
@@ -463,7 +465,9 @@ __global__ void __maxnreg__(168)
         // ------------------------------------------ producer: the dO_MN and Q_MN tiles ----
         if (lane == 0) {
             int domn_issued = -1, qmn_issued = -1;
-            for (int i = 0; i < nblk; i++) {
+            // DD = 64: K hi and V hi wait in these stages until the softmax warps moved them.
+            const bool staged = DD != 64 || mbar_wait(bar(C::KV_READY), 0, abort, err);
+            for (int i = 0; staged && i < nblk; i++) {
                 if (i >= 1 && !mbar_wait(bar(C::DOMN_EMPTY), (i - 1) & 1, abort, err)) break;
                 load_tile(&tm_domn, &tm_domn_lo, sb + C::OFF_DOMN, bar(C::DOMN_FULL), i, true);
                 domn_issued = i;
@@ -713,11 +717,12 @@ struct QqCfg {
     static constexpr uint32_t OFF_QLO = 0, OFF_DOLO = RESB, OFF_KK = LO_TMEM ? 0 : 2 * RESB,
                               OFF_VK = OFF_KK + NST_K * KSTAGE, OFF_KMN = OFF_VK + NST_K * KSTAGE,
                               OFF_BAR = OFF_KMN + NST_G * GSTAGE;
-    // Where Q / dO wait until the softmax warps move them into TMEM: DD = 64, hi in the K ring
-    // and lo in the V ring; DD = 128, hi in the lo areas (the lo copies are loaded after).
-    static constexpr uint32_t OFF_QHI_STAGE = LO_TMEM ? OFF_KK : OFF_QLO,
-                              OFF_DOHI_STAGE = LO_TMEM ? OFF_KK + RESB : OFF_DOLO,
-                              OFF_QLO_STAGE = OFF_VK, OFF_DOLO_STAGE = OFF_VK + RESB;
+    // Where Q / dO wait until the softmax warps move them into TMEM: DD = 64, Q in the MN-major
+    // ring and dO in the V ring (the K ring, which the first S MMA needs, fills meanwhile);
+    // DD = 128, hi in the lo areas (the lo copies are loaded after).
+    static constexpr uint32_t OFF_QHI_STAGE = LO_TMEM ? OFF_KMN : OFF_QLO,
+                              OFF_DOHI_STAGE = LO_TMEM ? OFF_VK : OFF_DOLO,
+                              OFF_QLO_STAGE = OFF_KMN + RESB, OFF_DOLO_STAGE = OFF_VK + RESB;
     // Per block j: S (S_FULL) read out by the softmax warps (S_READ: S_{j+1} may overwrite it);
     // dP (DP_FULL) turned into dS hi / lo (DS_READY); dQ_blk = dS K (DQ_DONE: dS read, dP_{j+1}
     // may overwrite it) folded into registers (DQ_FREE: the accumulator may restart).
@@ -732,7 +737,8 @@ struct QqCfg {
                               C_S = LO_TMEM ? 4 * DD : 2 * DD, C_DP = C_S + NB, C_DSLO = C_S + 2 * NB,
                               C_DQB = C_S + 3 * NB, TCOLS = 512;
     static_assert(C_DQB + 64 <= TCOLS, "tensor memory budget");
-    static_assert(!LO_TMEM || 2 * RESB <= NST_K * KSTAGE, "Q / dO tiles are staged in the K and V rings");
+    static_assert(!LO_TMEM || (2 * RESB <= NST_K * KSTAGE && 2 * RESB <= NST_G * GSTAGE),
+                  "Q / dO tiles are staged in the MN-major and V rings");
     static_assert(SMEM <= 232448, "smem");
 };
 
@@ -824,7 +830,9 @@ __global__ void __maxnreg__(168)
                 }
             }
             if (!(SPLIT && !C::LO_TMEM)) mbar_arrive(bar(C::QDLO_FULL));
-            bool ok = mbar_wait(bar(C::QD_READY), 0, abort, err);
+            // DD = 64 stages dO in the V ring: the K ring fills at once and the first V load
+            // waits below. DD = 128 loads the lo copies where the hi tiles wait, after they left.
+            bool ok = C::LO_TMEM || mbar_wait(bar(C::QD_READY), 0, abort, err);
             const bool lo_later = ok && SPLIT && !C::LO_TMEM;
             if (lo_later) {
                 mbar_expect_tx(bar(C::QDLO_FULL), 2 * C::RESB);
@@ -843,6 +851,7 @@ __global__ void __maxnreg__(168)
                     if (SPLIT) tma_load_4d(&tm_kk_lo, sb + o + C::TK_BYTES, bar(C::KK_FULL + st), 32 * c, j * NB, (int)hk, (int)b);
                 }
                 k_issued = j;
+                if (C::LO_TMEM && j == 0 && !(ok = mbar_wait(bar(C::QD_READY), 0, abort, err))) break;
                 if (j >= NST_K && !mbar_wait(bar(C::VK_EMPTY + st), ((j / NST_K) - 1) & 1, abort, err)) break;
                 mbar_expect_tx(bar(C::VK_FULL + st), (SPLIT ? 2 : 1) * C::TK_BYTES);
                 for (int c = 0; c < DD / 32; c++) {
@@ -866,8 +875,9 @@ __global__ void __maxnreg__(168)
         // ------------------------------------------------ producer: the MN-major ring ----
         if (lane == 0) {
             int issued = -1;
-            // DD = 64 stages Q / dO in the K and V rings only, so this ring may start at once.
-            for (int j = 0; j < nblk; j++) {
+            // DD = 64 stages Q in this ring: its first load waits until Q has left for TMEM.
+            const bool staged = !C::LO_TMEM || mbar_wait(bar(C::QD_READY), 0, abort, err);
+            for (int j = 0; staged && j < nblk; j++) {
                 const int st = j % NST_G;
                 if (j >= NST_G && !mbar_wait(bar(C::SG_EMPTY + st), ((j / NST_G) - 1) & 1, abort, err)) break;
                 mbar_expect_tx(bar(C::SG_FULL + st), (SPLIT ? 2 : 1) * C::TM_BYTES);
