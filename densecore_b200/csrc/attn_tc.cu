@@ -72,7 +72,7 @@ struct FwdCfg {
     static constexpr uint32_t OFF_XMAX = OFF_V + VST * KV_STAGE;     // float [2][2][BM]
     static constexpr uint32_t OFF_XSUM = OFF_XMAX + 2 * 2 * BM * 4;  // float [2][BM]
     static constexpr uint32_t OFF_BAR = OFF_XSUM + 2 * BM * 4;
-    static constexpr int Q_FULL = 0, Q_READY = 1, K_FULL = 2, K_READY = K_FULL + KST,
+    static constexpr int K_FULL = 0, K_READY = K_FULL + KST,
                          K_EMPTY = K_READY + KST, V_FULL = K_EMPTY + KST, V_READY = V_FULL + VST,
                          V_EMPTY = V_READY + VST, S_FULL = V_EMPTY + VST, P_FULL = S_FULL + 2,
                          PV_DONE_B = P_FULL + 2, OB_FREE = PV_DONE_B + 2,
@@ -96,13 +96,19 @@ struct FwdCfg {
     __host__ __device__ static constexpr uint32_t col_plo(int b) { return 2 * D + b * 2 * BN + BN; }
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(COLS_USED <= 512, "tensor memory budget");
-    static_assert(Q_BYTES <= VST * KV_STAGE, "the raw Q tile is staged in the V ring");
+    // The raw Q tile takes QS consecutive items of the V ring (Q_CHUNKS_PER_SLOT 128-byte
+    // column chunks each).
+    static constexpr int QS = (int)(Q_BYTES / KV_STAGE), Q_CHUNKS_PER_SLOT = (int)(KV_STAGE / Q_CHUNK);
+    static_assert(QS * KV_STAGE == Q_BYTES && Q_CHUNKS_PER_SLOT * Q_CHUNK == KV_STAGE && QS < VST,
+                  "the raw Q tile is staged in whole V-ring slots");
     static_assert(HB == 16 || HB == 32, "softmax half-block width");
 };
 
 struct TcFwdArgs {
     AttnProblem p;
     int num_q_tiles;
+    int64_t num_tiles;    // num_q_tiles * H * B
+    int64_t group_heads;  // (batch, head) pairs whose tiles are ordered together (their K / V fit in L2)
     float scale_log2;
     int *err;
 };
@@ -184,6 +190,33 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_b
     }
 }
 
+// Tile t of the schedule: groups of group_heads (batch, head) pairs, and within a group the
+// tiles with the most causal work first (q-tile major, pair minor). Tiles handed out together
+// then share their heads' K / V in L2.
+__device__ __forceinline__ void fwd_tile(const TcFwdArgs &a, int64_t t, int64_t &q0, int64_t &h, int64_t &b) {
+    const int64_t nq = a.num_q_tiles, g = a.group_heads, hb = a.p.H * a.p.B;
+    const int64_t grp = t / (g * nq), base = grp * g, gs = min(g, hb - base), r = t - grp * g * nq;
+    const int64_t qt = nq - 1 - r / gs, bh = base + r % gs;
+    h = bh % a.p.H;
+    b = bh / a.p.H;
+    q0 = qt * 128;
+}
+
+// Tile of round r of CTA c among G persistent CTAs: rounds alternate direction (a snake), which
+// evens out the causal tiles' unequal lengths across CTAs. -1 when the tiles have run out.
+__device__ __forceinline__ int64_t fwd_tile_of(int64_t r, int c, int G, int64_t T) {
+    const int64_t t = r * G + ((r & 1) ? G - 1 - c : c);
+    return t < T ? t : -1;
+}
+
+// Persistent: gridDim.x CTAs (at most one per SM) walk the tiles in fwd_tile_of order. Every
+// role keeps running counters across tiles: K items (one per key block) in the K ring; V-ring
+// items, which are each tile's Q (QS slots) followed by its V blocks, so that the barriers of a
+// V-ring slot count Q and V uses alike; and blocks (the S / P buffers, the O blocks). The next
+// tile's Q lands and its first K / V tiles load while the tensor core and the softmax warps
+// still work on the current tile; the converters move Q into TMEM once the current tile's last
+// S MMA has read the old Q, and the softmax warps' epilogue (last fold, normalisation, stores)
+// overlaps the next tile's first S MMAs.
 template <class C, bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(128)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
@@ -194,19 +227,22 @@ __global__ void __maxnreg__(128)
     uint8_t *sg = smem_raw + (sb - raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnProblem &p = a.p;
-    const int qt = a.num_q_tiles - 1 - (int)blockIdx.x;  // longest (causal) tiles first
-    const int64_t h = blockIdx.y, b = blockIdx.z, hk = h / p.group;
-    const int64_t q0 = (int64_t)qt * C::BM;
-    const int64_t kv_end = p.causal ? min(p.S, q0 + C::BM) : p.S;
-    const int nblk = (int)((kv_end + C::BN - 1) / C::BN);
+    const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+    const int64_t T = a.num_tiles;
+    constexpr int QS = C::QS, CPS = C::Q_CHUNKS_PER_SLOT;
+    // Key blocks of the tile at q0 (causal tiles stop at their last row).
+    auto tile_blocks = [&](int64_t q0) {
+        const int64_t kv_end = p.causal ? min(p.S, q0 + C::BM) : p.S;
+        return (int)((kv_end + C::BN - 1) / C::BN);
+    };
     auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
+    auto vslot = [&](int64_t x) { return (int)(x % C::VST); };
+    auto vpar = [&](int64_t x) { return (uint32_t)((x / C::VST) & 1); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
     volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
     int *err = a.err;
 
     if (threadIdx.x == 0) {
-        mbar_init(bar(C::Q_FULL), 1);
-        mbar_init(bar(C::Q_READY), 128);
         for (int s = 0; s < C::KST; s++) {
             mbar_init(bar(C::K_FULL + s), 1);
             mbar_init(bar(C::K_READY + s), 128);
@@ -250,38 +286,55 @@ __global__ void __maxnreg__(128)
     if (warp == C::W_PROD) {
         // ------------------------------------------------------------ TMA producer ----
         if (lane == 0) {
-            int k_issued = -1, v_issued = -1;
-            // The raw Q tile lands in the V ring and the converters move it into TMEM; the K
-            // ring fills meanwhile (S_0 needs Q and K_0), and the first V load waits until Q has
-            // left the V ring.
-            mbar_expect_tx(bar(C::Q_FULL), C::Q_BYTES);
-            for (int c = 0; c < C::CHUNKS; c++)
-                tma_load_4d(&tmq, sb + C::OFF_V + c * C::Q_CHUNK, bar(C::Q_FULL), 32 * c, (int)q0, (int)h, (int)b);
+            int64_t x = 0, kk = 0, x_last = -1, k_last = -1;
             bool ok = true;
-            for (int j = 0; ok && j < nblk; j++) {
-                const int ks = j % C::KST, vs = j % C::VST;
-                if (j >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, err)) break;
-                mbar_expect_tx(bar(C::K_FULL + ks), C::KV_BYTES);
-                const uint32_t kd = sb + C::OFF_K + ks * C::KV_STAGE;
-                for (int c = 0; c < C::CHUNKS; c++)
-                    tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
-                k_issued = j;
-                if (j == 0 && !(ok = mbar_wait(bar(C::Q_READY), 0, abort, err))) break;
-                if (j >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, err)) break;
-                mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
-                const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
-                for (int c = 0; c < C::CHUNKS; c++)
-                    tma_load_4d(&tmv, vd + c * C::KV_CHUNK, bar(C::V_FULL + vs), 32 * c, j * C::BN, (int)hk, (int)b);
-                v_issued = j;
+            for (int64_t r = 0; ok; r++) {
+                const int64_t t = fwd_tile_of(r, cta, G, T);
+                if (t < 0) break;
+                int64_t q0, h, b;
+                fwd_tile(a, t, q0, h, b);
+                const int64_t hk = h / p.group;
+                const int nblk = tile_blocks(q0);
+                // The raw Q tile into the next QS V-ring slots; the converters move it to TMEM.
+                for (int s = 0; s < QS; s++, x++) {
+                    const int vs = vslot(x);
+                    if (x >= C::VST && !(ok = mbar_wait(bar(C::V_EMPTY + vs), vpar(x - C::VST), abort, err))) break;
+                    mbar_expect_tx(bar(C::V_FULL + vs), C::KV_STAGE);
+                    for (int c = 0; c < CPS; c++)
+                        tma_load_4d(&tmq, sb + C::OFF_V + vs * C::KV_STAGE + c * C::Q_CHUNK, bar(C::V_FULL + vs),
+                                    32 * (s * CPS + c), (int)q0, (int)h, (int)b);
+                    x_last = x;
+                }
+                for (int j = 0; ok && j < nblk; j++) {
+                    const int ks = (int)(kk % C::KST);
+                    if (kk >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), (uint32_t)(((kk / C::KST) - 1) & 1), abort, err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(bar(C::K_FULL + ks), C::KV_BYTES);
+                    const uint32_t kd = sb + C::OFF_K + ks * C::KV_STAGE;
+                    for (int c = 0; c < C::CHUNKS; c++)
+                        tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
+                    k_last = kk++;
+                    const int vs = vslot(x);
+                    if (x >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), vpar(x - C::VST), abort, err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
+                    const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
+                    for (int c = 0; c < C::CHUNKS; c++)
+                        tma_load_4d(&tmv, vd + c * C::KV_CHUNK, bar(C::V_FULL + vs), 32 * c, j * C::BN, (int)hk, (int)b);
+                    x_last = x++;
+                }
             }
             if (*abort) {
                 // Let the copies already in flight land before the CTA's memory goes away.
                 volatile int never = 0;
-                mbar_wait(bar(C::Q_FULL), 0, &never, nullptr);
-                for (int j = max(0, k_issued - C::KST + 1); j <= k_issued; j++)
-                    mbar_wait(bar(C::K_FULL + j % C::KST), (j / C::KST) & 1, &never, nullptr);
-                for (int j = max(0, v_issued - C::VST + 1); j <= v_issued; j++)
-                    mbar_wait(bar(C::V_FULL + j % C::VST), (j / C::VST) & 1, &never, nullptr);
+                for (int64_t i = max((int64_t)0, k_last - C::KST + 1); i <= k_last; i++)
+                    mbar_wait(bar(C::K_FULL + (int)(i % C::KST)), (uint32_t)((i / C::KST) & 1), &never, nullptr);
+                for (int64_t i = max((int64_t)0, x_last - C::VST + 1); i <= x_last; i++)
+                    mbar_wait(bar(C::V_FULL + vslot(i)), vpar(i), &never, nullptr);
             }
         }
     } else if (warp == C::W_MMA) {
@@ -291,31 +344,47 @@ __global__ void __maxnreg__(128)
             // Descriptor of K stage 0; stage and k-step offsets go into the address field.
             const uint64_t kdesc0 = sdesc_sw128(sb + C::OFF_K, 16, 1024);
             const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO;
-            bool ok = mbar_wait_warp(bar(C::Q_READY), 0, abort, err);
-            tc_fence_after();
-            for (int j = 0; ok && j < nblk; j++) {
-                const int bb = j & 1, ks = j % C::KST;
-                // S buffer bb held P_{j-2}, read by PV_{j-2}.
-                if (j >= 2 && !mbar_wait_warp(bar(C::PV_DONE_B + bb), ((j - 2) >> 1) & 1, abort, err)) break;
-                if (!mbar_wait_warp(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
+            int64_t x = 0, kk = 0, jg = 0;
+            bool ok = true;
+            for (int64_t r = 0; ok; r++) {
+                const int64_t t = fwd_tile_of(r, cta, G, T);
+                if (t < 0) break;
+                int64_t q0, h, b;
+                fwd_tile(a, t, q0, h, b);
+                const int nblk = tile_blocks(q0);
+                // This tile's Q is in TMEM once its V-ring slots are READY; those slots are then free.
+                for (int s = 0; s < QS; s++)
+                    if (!(ok = mbar_wait_warp(bar(C::V_READY + vslot(x + s)), vpar(x + s), abort, err))) break;
+                if (!ok) break;
+                if (lane == 0)
+                    for (int s = 0; s < QS; s++) mbar_arrive(bar(C::V_EMPTY + vslot(x + s)));
+                x += QS + nblk;
                 tc_fence_after();
-                const uint64_t kd = kdesc0 + ((ks * C::KV_STAGE) >> 4);
-                const uint32_t d_s = tmem + C::col_s(bb);
-                if (SPLIT) {  // Qhi Klo + Qlo Khi first, then Qhi Khi
+                for (int j = 0; j < nblk; j++, jg++, kk++) {
+                    const int bb = (int)(jg & 1), ks = (int)(kk % C::KST);
+                    // S buffer bb held P of block jg - 2, read by its PV.
+                    if (jg >= 2 && !(ok = mbar_wait_warp(bar(C::PV_DONE_B + bb), (uint32_t)(((jg - 2) >> 1) & 1), abort, err)))
+                        break;
+                    if (!(ok = mbar_wait_warp(bar(C::K_READY + ks), (uint32_t)((kk / C::KST) & 1), abort, err))) break;
+                    tc_fence_after();
+                    const uint64_t kd = kdesc0 + ((ks * C::KV_STAGE) >> 4);
+                    const uint32_t d_s = tmem + C::col_s(bb);
+                    if (SPLIT) {  // Qhi Klo + Qlo Khi first, then Qhi Khi
 #pragma unroll
-                    for (int kk = 0; kk < C::D / 8; kk++) {
-                        const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
-                        mma_tf32_ts_w(d_s, q_hi + kk * 8, kd + ((C::KV_BYTES >> 4) + off), C::IDESC_S, kk > 0 ? 1u : 0u);
-                        mma_tf32_ts_w(d_s, q_lo + kk * 8, kd + off, C::IDESC_S, 1u);
+                        for (int k8 = 0; k8 < C::D / 8; k8++) {
+                            const uint32_t off = ((k8 >> 2) * C::KV_CHUNK + (k8 & 3) * 32) >> 4;
+                            mma_tf32_ts_w(d_s, q_hi + k8 * 8, kd + ((C::KV_BYTES >> 4) + off), C::IDESC_S, k8 > 0 ? 1u : 0u);
+                            mma_tf32_ts_w(d_s, q_lo + k8 * 8, kd + off, C::IDESC_S, 1u);
+                        }
                     }
-                }
 #pragma unroll
-                for (int kk = 0; kk < C::D / 8; kk++) {
-                    const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
-                    mma_tf32_ts_w(d_s, q_hi + kk * 8, kd + off, C::IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+                    for (int k8 = 0; k8 < C::D / 8; k8++) {
+                        const uint32_t off = ((k8 >> 2) * C::KV_CHUNK + (k8 & 3) * 32) >> 4;
+                        mma_tf32_ts_w(d_s, q_hi + k8 * 8, kd + off, C::IDESC_S, (SPLIT || k8 > 0) ? 1u : 0u);
+                    }
+                    tc_commit_w(bar(C::S_FULL + bb));
+                    tc_commit_w(bar(C::K_EMPTY + ks));
                 }
-                tc_commit_w(bar(C::S_FULL + bb));
-                tc_commit_w(bar(C::K_EMPTY + ks));
             }
             // Every MMA this warp issued completes before TMEM is released.
             tc_commit_w(bar(C::DRAIN));
@@ -326,30 +395,41 @@ __global__ void __maxnreg__(128)
         // ----------------------------------------------------- MMA issuer: O_blk = P V ----
         {
             const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
-            for (int i = 0; i < nblk; i++) {
-                const int bi = i & 1, vs = i % C::VST;
-                if (!mbar_wait_warp(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) break;
-                if (!mbar_wait_warp(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) break;
-                // O_blk buffer i % NOB held block i - NOB until the softmax threads folded it.
-                if (i >= C::NOB && !mbar_wait_warp(bar(C::OB_FREE + i % C::NOB), ((i / C::NOB) - 1) & 1, abort, err))
-                    break;
-                const uint32_t d_ob = tmem + C::col_ob(i);
-                tc_fence_after();
-                const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
-                const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
-                if (SPLIT) {  // the small cross terms first, then the main products
+            int64_t x = 0, jg = 0;
+            bool ok = true;
+            for (int64_t r = 0; ok; r++) {
+                const int64_t t = fwd_tile_of(r, cta, G, T);
+                if (t < 0) break;
+                int64_t q0, h, b;
+                fwd_tile(a, t, q0, h, b);
+                const int nblk = tile_blocks(q0);
+                x += QS;
+                for (int j = 0; j < nblk; j++, jg++, x++) {
+                    const int bi = (int)(jg & 1), vs = vslot(x);
+                    if (!(ok = mbar_wait_warp(bar(C::P_FULL + bi), (uint32_t)((jg >> 1) & 1), abort, err))) break;
+                    if (!(ok = mbar_wait_warp(bar(C::V_READY + vs), vpar(x), abort, err))) break;
+                    // O_blk buffer jg % NOB held block jg - NOB until the softmax threads folded it.
+                    if (jg >= C::NOB &&
+                        !(ok = mbar_wait_warp(bar(C::OB_FREE + (int)(jg % C::NOB)), (uint32_t)(((jg / C::NOB) - 1) & 1), abort, err)))
+                        break;
+                    const uint32_t d_ob = tmem + C::col_ob((int)(jg % C::NOB));
+                    tc_fence_after();
+                    const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
+                    const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
+                    if (SPLIT) {  // the small cross terms first, then the main products
 #pragma unroll
-                    for (int kk = 0; kk < C::BN / 8; kk++) {
-                        mma_tf32_ts_w(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
-                                      kk > 0 ? 1u : 0u);
-                        mma_tf32_ts_w(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
+                        for (int k8 = 0; k8 < C::BN / 8; k8++) {
+                            mma_tf32_ts_w(d_ob, a_hi + k8 * 8, vd + ((C::KV_BYTES + k8 * 1024) >> 4), C::IDESC_O,
+                                          k8 > 0 ? 1u : 0u);
+                            mma_tf32_ts_w(d_ob, a_lo + k8 * 8, vd + ((k8 * 1024) >> 4), C::IDESC_O, 1u);
+                        }
                     }
-                }
 #pragma unroll
-                for (int kk = 0; kk < C::BN / 8; kk++)
-                    mma_tf32_ts_w(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
-                tc_commit_w(bar(C::PV_DONE_B + bi));
-                tc_commit_w(bar(C::V_EMPTY + vs));
+                    for (int k8 = 0; k8 < C::BN / 8; k8++)
+                        mma_tf32_ts_w(d_ob, a_hi + k8 * 8, vd + ((k8 * 1024) >> 4), C::IDESC_O, (SPLIT || k8 > 0) ? 1u : 0u);
+                    tc_commit_w(bar(C::PV_DONE_B + bi));
+                    tc_commit_w(bar(C::V_EMPTY + vs));
+                }
             }
             tc_commit_w(bar(C::DRAIN_PV));
             volatile int never = 0;
@@ -359,190 +439,218 @@ __global__ void __maxnreg__(128)
         // --------------------------------------------------------------- converters ----
         const int ct = threadIdx.x - 32 * C::W_CVT;
         const int quad = warp & 3;
-        if (mbar_wait(bar(C::Q_FULL), 0, abort, err)) {
-            row_to_tmem<C::CHUNKS, SPLIT>(sg + C::OFF_V, C::Q_CHUNK, quad * 32 + lane,
-                                          tmem + ((uint32_t)(quad * 32) << 16), C::COL_QHI, C::COL_QLO);
+        const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+        int64_t x = 0, kk = 0, jg = 0;
+        bool ok = true;
+        for (int64_t r = 0; ok; r++) {
+            const int64_t t = fwd_tile_of(r, cta, G, T);
+            if (t < 0) break;
+            int64_t q0, h, b;
+            fwd_tile(a, t, q0, h, b);
+            const int nblk = tile_blocks(q0);
+            // The previous tile's last S MMA (block jg - 1) has read the old Q before the new one
+            // overwrites it in TMEM. (S_FULL of that buffer cannot move on before this Q is in.)
+            if (jg > 0 && !(ok = mbar_wait(bar(C::S_FULL + (int)((jg - 1) & 1)), (uint32_t)(((jg - 1) >> 1) & 1), abort, err)))
+                break;
+            tc_fence_after();
+            for (int s = 0; s < QS; s++, x++) {
+                const int vs = vslot(x);
+                if (!(ok = mbar_wait(bar(C::V_FULL + vs), vpar(x), abort, err))) break;
+                row_to_tmem<CPS, SPLIT>(sg + C::OFF_V + vs * C::KV_STAGE, C::Q_CHUNK, quad * 32 + lane, tl,
+                                        C::COL_QHI + 32 * CPS * s, C::COL_QLO + 32 * CPS * s);
+            }
+            if (!ok) break;
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(C::Q_READY));
-            for (int j = 0; j < nblk; j++) {
-                const int ks = j % C::KST, vs = j % C::VST;
-                if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, err)) break;
+            for (int s = 0; s < QS; s++) mbar_arrive(bar(C::V_READY + vslot(x - QS + s)));
+            for (int j = 0; j < nblk; j++, kk++, x++) {
+                const int ks = (int)(kk % C::KST), vs = vslot(x);
+                if (!(ok = mbar_wait(bar(C::K_FULL + ks), (uint32_t)((kk / C::KST) & 1), abort, err))) break;
                 split_tile<SPLIT>(sg + C::OFF_K + ks * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
                 mbar_arrive(bar(C::K_READY + ks));
-                if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, err)) break;
+                if (!(ok = mbar_wait(bar(C::V_FULL + vs), vpar(x), abort, err))) break;
                 split_tile<SPLIT>(sg + C::OFF_V + vs * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
                 mbar_arrive(bar(C::V_READY + vs));
             }
+            jg += nblk;
         }
     } else {
         // ------------------------------------------------------------------ softmax ----
         const int row = threadIdx.x & 127, half = threadIdx.x >> 7;
-        const int64_t qrow = q0 + row;
-        const bool row_ok = qrow < p.L;
         const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         float *xmax = reinterpret_cast<float *>(sg + C::OFF_XMAX);  // [2][2][BM]
         float *xsum = reinterpret_cast<float *>(sg + C::OFF_XSUM);  // [2][BM]
-        float m = -INFINITY, l = 0.0f;
-        float o[C::HD];
-#pragma unroll
-        for (int x = 0; x < C::HD; x++) o[x] = 0.0f;
+        int64_t jg = 0;
         bool ok = true;
-        for (int j = 0; j < nblk; j++) {
-            const int bb = j & 1;
-            const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
-            // Rows past L (zero-filled by TMA) are computed but never stored. Column c is key
-            // k0 + c: valid below S and, under causal masking, up to qrow (one bit per column
-            // keeps the edge path as short as the fast one).
-            const bool edge = MASKED || (k0 + C::HB > p.S) || (p.causal && k0 + C::HB - 1 > q0);
-            uint32_t vbits = 0xFFFFFFFFu;
-            if (edge) {
-                const int64_t lim = (p.causal ? min(p.S, qrow + 1) : p.S) - k0;
-                const int n = !row_ok || lim <= 0 ? 0 : (lim >= C::HB ? C::HB : (int)lim);
-                vbits = n == 0 ? 0u : (0xFFFFFFFFu >> (32 - n));
-            }
-            // The user mask's values for these columns, loaded before the wait for S so that
-            // the wait hides their latency.
-            float mk[MASKED ? C::HB : 1];
-            if constexpr (MASKED) mask_run<C::HB>(p, b, h, qrow, k0, p.ms[3], vbits, mk);
-            // Dropout: this row's keep bits for these columns (the weights that meet V are
-            // P * keep_scale where kept, 0 where dropped; the row sum and lse stay undropped).
-            uint32_t kbits = 0;
-            if constexpr (DROP) kbits = row_ok ? keep_run32(p, b, h, qrow, k0) : 0u;
-            if (!mbar_wait(bar(C::S_FULL + bb), (j >> 1) & 1, abort, err)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            float s[C::HB];
-            {
-                uint32_t r[C::HB];
-                tmem_ld<C::HB>(tl + C::col_s(bb) + half * C::HB, r);
-                tmem_wait_ld();
+        for (int64_t r = 0; ok; r++) {
+            const int64_t t = fwd_tile_of(r, cta, G, T);
+            if (t < 0) break;
+            int64_t q0, h, b;
+            fwd_tile(a, t, q0, h, b);
+            const int nblk = tile_blocks(q0);
+            const int64_t qrow = q0 + row;
+            const bool row_ok = qrow < p.L;
+            float m = -INFINITY, l = 0.0f;
+            float o[C::HD];
 #pragma unroll
-                for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(r[x]);
-            }
-            // Interior blocks keep the raw scores and fold the scale into the exponent's FFMA
-            // (the max commutes with a positive scale); edge blocks scale, mask and fill first.
-            const bool raw = !edge && a.scale_log2 > 0.0f;
-            const float smul = raw ? a.scale_log2 : 1.0f;
-            if (!raw) {
-#pragma unroll
-                for (int c = 0; c < C::HB; c++) {
-                    float x = s[c] * a.scale_log2;
-                    if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
-                    s[c] = ((vbits >> c) & 1u) ? x : -INFINITY;
+            for (int x = 0; x < C::HD; x++) o[x] = 0.0f;
+            for (int j = 0; j < nblk; j++, jg++) {
+                const int bb = (int)(jg & 1);
+                const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
+                // Rows past L (zero-filled by TMA) are computed but never stored. Column c is key
+                // k0 + c: valid below S and, under causal masking, up to qrow (one bit per column
+                // keeps the edge path as short as the fast one).
+                const bool edge = MASKED || (k0 + C::HB > p.S) || (p.causal && k0 + C::HB - 1 > q0);
+                uint32_t vbits = 0xFFFFFFFFu;
+                if (edge) {
+                    const int64_t lim = (p.causal ? min(p.S, qrow + 1) : p.S) - k0;
+                    const int n = !row_ok || lim <= 0 ? 0 : (lim >= C::HB ? C::HB : (int)lim);
+                    vbits = n == 0 ? 0u : (0xFFFFFFFFu >> (32 - n));
                 }
-            }
-            float bmax = max_tree<C::HB>(s) * smul;
-            // The block's row max, shared with the partner thread (the other half) through
-            // shared memory and an mbarrier (a bounded wait, unlike bar.sync).
-            xmax[(bb * 2 + half) * C::BM + row] = bmax;
-            mbar_arrive(bar(C::XCH + bb));
-            if (!mbar_wait(bar(C::XCH + bb), (j >> 1) & 1, abort, err)) {
-                ok = false;
-                break;
-            }
-            bmax = fmaxf(bmax, xmax[(bb * 2 + (half ^ 1)) * C::BM + row]);
-            const float m_new = fmaxf(m, bmax);
-            const bool rescale = m_new > m + 8.0f;
-            float corr = 1.0f;
-            if (rescale) {
-                corr = ex2_approx(m - m_new);
-                m = m_new;
-            }
-            const bool dead = (m == -INFINITY);
-            float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four partial row sums: shorter chains
-#pragma unroll
-            for (int r0 = 0; r0 < C::HB; r0 += 16) {  // P in 16-column pieces
-                uint32_t phi[16], plo[16];
-#pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    const float pc = dead ? 0.0f : ex2_approx(fmaf(s[r0 + c], smul, -m));
-                    part[c & 3] += pc;
-                    float pw = pc;
-                    if constexpr (DROP) pw = ((kbits >> (r0 + c)) & 1u) ? pc * p.keep_scale : 0.0f;
-                    if (SPLIT) {
-                        phi[c] = __float_as_uint(pw);
-                        plo[c] = tf32_lo_trunc(pw);
-                    } else {
-                        phi[c] = tf32_rna(pw);
-                    }
-                }
-                tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
-                if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);
-            }
-            const float rs = (part[0] + part[1]) + (part[2] + part[3]);
-            l = fmaf(l, corr, rs);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bar(C::P_FULL + bb));
-            // Fold the previous block: o = (o + O_blk(j-1)) * corr (both relative to the
-            // previous max; corr moves them to m).
-            if (j >= 1) {
-                // Per-buffer barrier: with two O_blk buffers PV_j may finish before this wait,
-                // so a single barrier could be two phases ahead of it.
-                if (!mbar_wait(bar(C::PV_DONE_B + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort, err)) {
-                    ok = false;
-                    break;
-                }
+                // The user mask's values for these columns, loaded before the wait for S so that
+                // the wait hides their latency.
+                float mk[MASKED ? C::HB : 1];
+                if constexpr (MASKED) mask_run<C::HB>(p, b, h, qrow, k0, p.ms[3], vbits, mk);
+                // Dropout: this row's keep bits for these columns (the weights that meet V are
+                // P * keep_scale where kept, 0 where dropped; the row sum and lse stay undropped).
+                uint32_t kbits = 0;
+                if constexpr (DROP) kbits = row_ok ? keep_run32(p, b, h, qrow, k0) : 0u;
+                if (!(ok = mbar_wait(bar(C::S_FULL + bb), (uint32_t)((jg >> 1) & 1), abort, err))) break;
                 tc_fence_after();
-                const bool scaled = __any_sync(0xffffffffu, corr != 1.0f);
-#pragma unroll
-                for (int c = 0; c < C::HD / 16; c++) {
-                    uint32_t r[16];
-                    tmem_ld16(tl + C::col_ob(j - 1) + half * C::HD + 16 * c, r);
+                float s[C::HB];
+                {
+                    uint32_t rr[C::HB];
+                    tmem_ld<C::HB>(tl + C::col_s(bb) + half * C::HB, rr);
                     tmem_wait_ld();
-                    if (scaled) {
 #pragma unroll
-                        for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(r[x])) * corr;
-                    } else {
+                    for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(rr[x]);
+                }
+                // Interior blocks keep the raw scores and fold the scale into the exponent's FFMA
+                // (the max commutes with a positive scale); edge blocks scale, mask and fill first.
+                const bool rawp = !edge && a.scale_log2 > 0.0f;
+                const float smul = rawp ? a.scale_log2 : 1.0f;
+                if (!rawp) {
 #pragma unroll
-                        for (int x = 0; x < 16; x++) o[16 * c + x] += __uint_as_float(r[x]);
+                    for (int c = 0; c < C::HB; c++) {
+                        float x = s[c] * a.scale_log2;
+                        if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                        s[c] = ((vbits >> c) & 1u) ? x : -INFINITY;
                     }
+                }
+                float bmax = max_tree<C::HB>(s) * smul;
+                // The block's row max, shared with the partner thread (the other half) through
+                // shared memory and an mbarrier (a bounded wait, unlike bar.sync).
+                xmax[(bb * 2 + half) * C::BM + row] = bmax;
+                mbar_arrive(bar(C::XCH + bb));
+                if (!(ok = mbar_wait(bar(C::XCH + bb), (uint32_t)((jg >> 1) & 1), abort, err))) break;
+                bmax = fmaxf(bmax, xmax[(bb * 2 + (half ^ 1)) * C::BM + row]);
+                const float m_new = fmaxf(m, bmax);
+                const bool rescale = m_new > m + 8.0f;
+                float corr = 1.0f;
+                if (rescale) {
+                    corr = ex2_approx(m - m_new);
+                    m = m_new;
+                }
+                const bool dead = (m == -INFINITY);
+                float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four partial row sums: shorter chains
+#pragma unroll
+                for (int r0 = 0; r0 < C::HB; r0 += 16) {  // P in 16-column pieces
+                    uint32_t phi[16], plo[16];
+#pragma unroll
+                    for (int c = 0; c < 16; c++) {
+                        const float pc = dead ? 0.0f : ex2_approx(fmaf(s[r0 + c], smul, -m));
+                        part[c & 3] += pc;
+                        float pw = pc;
+                        if constexpr (DROP) pw = ((kbits >> (r0 + c)) & 1u) ? pc * p.keep_scale : 0.0f;
+                        if (SPLIT) {
+                            phi[c] = __float_as_uint(pw);
+                            plo[c] = tf32_lo_trunc(pw);
+                        } else {
+                            phi[c] = tf32_rna(pw);
+                        }
+                    }
+                    tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
+                    if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);
+                }
+                const float rs = (part[0] + part[1]) + (part[2] + part[3]);
+                l = fmaf(l, corr, rs);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar(C::P_FULL + bb));
+                // Fold the previous block: o = (o + O_blk(jg-1)) * corr (both relative to the
+                // previous max; corr moves them to m).
+                if (j >= 1) {
+                    // Per-buffer barrier: with two O_blk buffers PV_jg may finish before this wait,
+                    // so a single barrier could be two phases ahead of it.
+                    if (!(ok = mbar_wait(bar(C::PV_DONE_B + (int)((jg - 1) & 1)), (uint32_t)(((jg - 1) >> 1) & 1), abort, err)))
+                        break;
+                    tc_fence_after();
+                    const bool scaled = __any_sync(0xffffffffu, corr != 1.0f);
+#pragma unroll
+                    for (int c = 0; c < C::HD / 16; c++) {
+                        uint32_t rr[16];
+                        tmem_ld16(tl + C::col_ob((int)((jg - 1) % C::NOB)) + half * C::HD + 16 * c, rr);
+                        tmem_wait_ld();
+                        if (scaled) {
+#pragma unroll
+                            for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(rr[x])) * corr;
+                        } else {
+#pragma unroll
+                            for (int x = 0; x < 16; x++) o[16 * c + x] += __uint_as_float(rr[x]);
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(bar(C::OB_FREE + (int)((jg - 1) % C::NOB)));
+                }
+            }
+            // The tile's last block: its O_blk into the registers, its buffer freed for the next
+            // tile's PV MMAs.
+            const int64_t jl = jg - 1;
+            if (ok) {
+                ok = mbar_wait(bar(C::PV_DONE_B + (int)(jl & 1)), (uint32_t)((jl >> 1) & 1), abort, err);
+                tc_fence_after();
+            }
+            const bool read_o = __all_sync(0xffffffffu, ok);
+            if (read_o) {
+#pragma unroll
+                for (int c = 0; c < C::HD / 32; c++) {
+                    uint32_t rr[32];
+                    tmem_ld32(tl + C::col_ob((int)(jl % C::NOB)) + half * C::HD + 32 * c, rr);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int x = 0; x < 32; x++) o[32 * c + x] += __uint_as_float(rr[x]);
                 }
                 tc_fence_before();
-                mbar_arrive(bar(C::OB_FREE + (j - 1) % C::NOB));
+                mbar_arrive(bar(C::OB_FREE + (int)(jl % C::NOB)));
             }
-        }
-        if (ok && nblk > 0) {
-            ok = mbar_wait(bar(C::PV_DONE_B + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort, err);
-            tc_fence_after();
-        }
-        const bool read_o = __all_sync(0xffffffffu, ok) && nblk > 0;
-        const bool aborted = __any_sync(0xffffffffu, *abort != 0);
-        if (read_o) {
+            if (!read_o) ok = false;
+            const bool aborted = __any_sync(0xffffffffu, *abort != 0);
+            // The row sum: this half's part plus the partner's. (A thread can only write the next
+            // tile's sum after its partner passed the next tile's first max exchange, so after it
+            // read this one.)
+            xsum[half * C::BM + row] = l;
+            mbar_arrive(bar(C::XSUM));
+            const bool have_sum = mbar_wait(bar(C::XSUM), (uint32_t)(r & 1), abort, err);
+            l += xsum[(half ^ 1) * C::BM + row];
+            if (!have_sum) ok = false;
+            if (ok && !aborted && row_ok) {
+                const float lfin = l == 0.0f ? 1.0f : l;
+                const float mnat = m == -INFINITY ? 0.0f : m * LN2;
+                const float inv = 1.0f / lfin;
+                float *orow = p.out + b * p.os[0] + h * p.os[1] + qrow * p.os[2] + (int64_t)half * C::HD * p.os[3];
+                if (p.os[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15u) == 0) {
 #pragma unroll
-            for (int c = 0; c < C::HD / 32; c++) {
-                uint32_t r[32];
-                tmem_ld32(tl + C::col_ob(nblk - 1) + half * C::HD + 32 * c, r);
-                tmem_wait_ld();
+                    for (int x = 0; x < C::HD; x += 4)
+                        *reinterpret_cast<float4 *>(orow + x) =
+                            make_float4(o[x] * inv, o[x + 1] * inv, o[x + 2] * inv, o[x + 3] * inv);
+                } else {
 #pragma unroll
-                for (int x = 0; x < 32; x++) o[32 * c + x] += __uint_as_float(r[x]);
+                    for (int x = 0; x < C::HD; x++) orow[x * p.os[3]] = o[x] * inv;
+                }
+                if (half == 0) p.lse[b * p.ls[0] + h * p.ls[1] + qrow * p.ls[2]] = mnat + logf(lfin);
             }
-        }
-        // The row sum: this half's part plus the partner's.
-        xsum[half * C::BM + row] = l;
-        mbar_arrive(bar(C::XSUM));
-        const bool have_sum = mbar_wait(bar(C::XSUM), 0, abort, err);
-        l += xsum[(half ^ 1) * C::BM + row];
-        if (!aborted && have_sum && row_ok) {
-            const float lfin = l == 0.0f ? 1.0f : l;
-            const float mnat = m == -INFINITY ? 0.0f : m * LN2;
-            const float inv = 1.0f / lfin;
-            float *orow = p.out + b * p.os[0] + h * p.os[1] + qrow * p.os[2] + (int64_t)half * C::HD * p.os[3];
-            if (p.os[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15u) == 0) {
-#pragma unroll
-                for (int x = 0; x < C::HD; x += 4)
-                    *reinterpret_cast<float4 *>(orow + x) =
-                        make_float4(o[x] * inv, o[x + 1] * inv, o[x + 2] * inv, o[x + 3] * inv);
-            } else {
-#pragma unroll
-                for (int x = 0; x < C::HD; x++) orow[x * p.os[3]] = o[x] * inv;
-            }
-            if (half == 0) p.lse[b * p.ls[0] + h * p.ls[1] + qrow * p.ls[2]] = mnat + logf(lfin);
         }
     }
 
@@ -579,9 +687,23 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
                        : (masked ? attn_fwd_tc_kernel<C, false, true, false> : attn_fwd_tc_kernel<C, false, false, false>);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
-    dim3 grid((unsigned)a.num_q_tiles, (unsigned)p.H, (unsigned)p.B);
+    a.num_tiles = (int64_t)a.num_q_tiles * p.H * p.B;
+    // Groups of heads whose K and V (S * (E + Ev) floats each) fit in about 64 MB of the L2.
+    const int64_t kv_bytes = p.S * (p.E + p.Ev) * 4, hb = p.H * p.B;
+    a.group_heads = kv_bytes > 0 ? (64ll << 20) / kv_bytes : hb;
+    a.group_heads = a.group_heads < 1 ? 1 : (a.group_heads > hb ? hb : a.group_heads);
+    // Short tiles (up to 64 key blocks) run persistently, one CTA per SM (tensor and shared
+    // memory admit one) walking the schedule, so that a tile's start-up overlaps the previous
+    // tile's tail; long tiles take one CTA each, which the hardware hands out in schedule order.
+    static int sms[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms[dev] = 148;
+    const bool persistent = (p.S + C::BN - 1) / C::BN <= 64;
+    const int64_t ctas = persistent && a.num_tiles > sms[dev] ? sms[dev] : a.num_tiles;
+    if (ctas > 0x7fffffffll) return fail(DC_ERR_UNSUPPORTED, "too many query tiles for one launch");
     KernelTrace tr(C::D == 64 ? "fwd_tc_d64" : "fwd_tc_d128", stream);
-    kernel<<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);
+    kernel<<<(unsigned)ctas, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);
     return check_launch("attn_fwd_tc");
 }
 
