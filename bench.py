@@ -517,7 +517,7 @@ def single_gpu_extras(device, steps):
         dc.set_sdpa_precision(prec)
         try:
             w = WORKLOADS[name]
-            r = measure(name, w, device, None, steps, 3, cpu=prec == "3xtf32", cpu_budget=3.0)
+            r = measure(name, w, device, None, steps, 3, cpu=prec == "3xtf32", cpu_budget=3.0, clocks=True)
         finally:
             dc.set_sdpa_precision(None)
         r.update(workload=name, precision=prec)
@@ -557,7 +557,7 @@ def _cfg3_strong(extras, device, dist, rank, world, steps, e2e_args):
         per = units // world
         wr = dict(w3, q=(1, per, 1024, 64), kv=(1, per, 1024, 64))
         r = measure("gpt2_causal_fwd_bwd", wr, device, dist, steps, 3, agg_amount=work(w3)[0], e2e=True,
-                    e2e_args=e2e_args, seed=4321 + rank)
+                    e2e_args=e2e_args, seed=4321 + rank, clocks=True)
         r.update(units_per_rank=per, scaling="strong",
                  scatter_gather="each rank copies its units' q, k, v, dO from pinned host memory and its "
                                 "out, dq, dk, dv back (inside e2e's timed region)")
@@ -582,7 +582,7 @@ def _ring_cfg4(extras, device, dist, rank, world, steps):
         try:
             ringn = NativeRingAttention(q.shape, k.shape, device, comm, causal=True)
             r = measure("long_causal_fwd", w4, device, dist, steps, 3, agg_amount=work(w4)[0],
-                        inputs=(q, k, v, None, None), ring=ringn)
+                        inputs=(q, k, v, None, None), ring=ringn, clocks=True)
             out, lse = ringn(q, k, v)
             torch.cuda.synchronize()
         finally:
@@ -592,7 +592,7 @@ def _ring_cfg4(extras, device, dist, rank, world, steps):
         rt = measure("long_causal_fwd", w4, device, dist, steps, 3, agg_amount=work(w4)[0],
                      inputs=(q, k, v, None, None), ring=ringt)
         one = measure("long_causal_fwd", w4, device, dist, max(3, steps // 4), 3, agg_amount=work(w4)[0],
-                      inputs=full)
+                      inputs=full, clocks=True)
         heads = [0, 9]
         so, sl = _native._flash_attention(*(t[:, heads].contiguous() for t in full[:3]), True)
         ref_o, ref_l = zigzag_shard(so, rank, world), zigzag_shard(sl.unsqueeze(-1), rank, world).squeeze(-1)
@@ -601,6 +601,7 @@ def _ring_cfg4(extras, device, dist, rank, world, steps):
         err = _max_over_ranks(max(err_o, err_l), dist, device)
         r.update(impl="dc_ring_sdpa_fwd (C ABI; NCCL send/recv on a side stream, merges in the library)",
                  scaling="strong", one_gpu_ms=one["ms_per_step"], one_gpu_value=one["value"],
+                 one_gpu_clocks=one.get("clocks"),
                  frac_of_n_x_one_gpu=r["value"] / (world * one["value"]),
                  torch_ring={"ms_per_step": rt["ms_per_step"], "value": rt["value"],
                              "impl": "densecore_b200.ring.RingAttention (batch_isend_irecv over the NCCL process group)"},
@@ -619,7 +620,8 @@ def _decode_shard(extras, device, dist, rank, world, steps):
     if w5["q"][0] % world == 0:
         bpr = w5["q"][0] // world
         wr = dict(w5, q=(bpr,) + w5["q"][1:], kv=(bpr,) + w5["kv"][1:])
-        r = measure("decode_splitkv", wr, device, dist, steps, 3, agg_amount=work(w5)[0], seed=999 + rank)
+        r = measure("decode_splitkv", wr, device, dist, steps, 3, agg_amount=work(w5)[0], seed=999 + rank,
+                    clocks=True)
         r.update(batch_per_rank=bpr, scaling="strong",
                  frac_of_n_x_hbm=r["value"] / (world * peaks()["hbm"]))
         extras["decode_shard"] = r

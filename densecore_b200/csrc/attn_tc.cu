@@ -236,8 +236,8 @@ __global__ void __maxnreg__(128)
         return (int)((kv_end + C::BN - 1) / C::BN);
     };
     auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
-    auto vslot = [&](int64_t x) { return (int)(x % C::VST); };
-    auto vpar = [&](int64_t x) { return (uint32_t)((x / C::VST) & 1); };
+    auto vslot = [&](int x) { return x % C::VST; };
+    auto vpar = [&](int x) { return (uint32_t)((x / C::VST) & 1); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
     volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
     int *err = a.err;
@@ -286,7 +286,7 @@ __global__ void __maxnreg__(128)
     if (warp == C::W_PROD) {
         // ------------------------------------------------------------ TMA producer ----
         if (lane == 0) {
-            int64_t x = 0, kk = 0, x_last = -1, k_last = -1;
+            int x = 0, kk = 0, x_last = -1, k_last = -1;
             bool ok = true;
             for (int64_t r = 0; ok; r++) {
                 const int64_t t = fwd_tile_of(r, cta, G, T);
@@ -306,7 +306,7 @@ __global__ void __maxnreg__(128)
                     x_last = x;
                 }
                 for (int j = 0; ok && j < nblk; j++) {
-                    const int ks = (int)(kk % C::KST);
+                    const int ks = kk % C::KST;
                     if (kk >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), (uint32_t)(((kk / C::KST) - 1) & 1), abort, err)) {
                         ok = false;
                         break;
@@ -331,9 +331,9 @@ __global__ void __maxnreg__(128)
             if (*abort) {
                 // Let the copies already in flight land before the CTA's memory goes away.
                 volatile int never = 0;
-                for (int64_t i = max((int64_t)0, k_last - C::KST + 1); i <= k_last; i++)
-                    mbar_wait(bar(C::K_FULL + (int)(i % C::KST)), (uint32_t)((i / C::KST) & 1), &never, nullptr);
-                for (int64_t i = max((int64_t)0, x_last - C::VST + 1); i <= x_last; i++)
+                for (int i = max(0, k_last - C::KST + 1); i <= k_last; i++)
+                    mbar_wait(bar(C::K_FULL + i % C::KST), (uint32_t)((i / C::KST) & 1), &never, nullptr);
+                for (int i = max(0, x_last - C::VST + 1); i <= x_last; i++)
                     mbar_wait(bar(C::V_FULL + vslot(i)), vpar(i), &never, nullptr);
             }
         }
@@ -344,7 +344,7 @@ __global__ void __maxnreg__(128)
             // Descriptor of K stage 0; stage and k-step offsets go into the address field.
             const uint64_t kdesc0 = sdesc_sw128(sb + C::OFF_K, 16, 1024);
             const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO;
-            int64_t x = 0, kk = 0, jg = 0;
+            int x = 0, kk = 0, jg = 0;
             bool ok = true;
             for (int64_t r = 0; ok; r++) {
                 const int64_t t = fwd_tile_of(r, cta, G, T);
@@ -361,7 +361,7 @@ __global__ void __maxnreg__(128)
                 x += QS + nblk;
                 tc_fence_after();
                 for (int j = 0; j < nblk; j++, jg++, kk++) {
-                    const int bb = (int)(jg & 1), ks = (int)(kk % C::KST);
+                    const int bb = jg & 1, ks = kk % C::KST;
                     // S buffer bb held P of block jg - 2, read by its PV.
                     if (jg >= 2 && !(ok = mbar_wait_warp(bar(C::PV_DONE_B + bb), (uint32_t)(((jg - 2) >> 1) & 1), abort, err)))
                         break;
@@ -395,7 +395,7 @@ __global__ void __maxnreg__(128)
         // ----------------------------------------------------- MMA issuer: O_blk = P V ----
         {
             const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
-            int64_t x = 0, jg = 0;
+            int x = 0, jg = 0;
             bool ok = true;
             for (int64_t r = 0; ok; r++) {
                 const int64_t t = fwd_tile_of(r, cta, G, T);
@@ -405,7 +405,7 @@ __global__ void __maxnreg__(128)
                 const int nblk = tile_blocks(q0);
                 x += QS;
                 for (int j = 0; j < nblk; j++, jg++, x++) {
-                    const int bi = (int)(jg & 1), vs = vslot(x);
+                    const int bi = jg & 1, vs = vslot(x);
                     if (!(ok = mbar_wait_warp(bar(C::P_FULL + bi), (uint32_t)((jg >> 1) & 1), abort, err))) break;
                     if (!(ok = mbar_wait_warp(bar(C::V_READY + vs), vpar(x), abort, err))) break;
                     // O_blk buffer jg % NOB held block jg - NOB until the softmax threads folded it.
@@ -440,7 +440,7 @@ __global__ void __maxnreg__(128)
         const int ct = threadIdx.x - 32 * C::W_CVT;
         const int quad = warp & 3;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        int64_t x = 0, kk = 0, jg = 0;
+        int x = 0, kk = 0, jg = 0;
         bool ok = true;
         for (int64_t r = 0; ok; r++) {
             const int64_t t = fwd_tile_of(r, cta, G, T);
@@ -464,7 +464,7 @@ __global__ void __maxnreg__(128)
             tc_fence_before();
             for (int s = 0; s < QS; s++) mbar_arrive(bar(C::V_READY + vslot(x - QS + s)));
             for (int j = 0; j < nblk; j++, kk++, x++) {
-                const int ks = (int)(kk % C::KST), vs = vslot(x);
+                const int ks = kk % C::KST, vs = vslot(x);
                 if (!(ok = mbar_wait(bar(C::K_FULL + ks), (uint32_t)((kk / C::KST) & 1), abort, err))) break;
                 split_tile<SPLIT>(sg + C::OFF_K + ks * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
                 fence_proxy_async_smem();
@@ -482,7 +482,7 @@ __global__ void __maxnreg__(128)
         const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         float *xmax = reinterpret_cast<float *>(sg + C::OFF_XMAX);  // [2][2][BM]
         float *xsum = reinterpret_cast<float *>(sg + C::OFF_XSUM);  // [2][BM]
-        int64_t jg = 0;
+        int jg = 0;
         bool ok = true;
         for (int64_t r = 0; ok; r++) {
             const int64_t t = fwd_tile_of(r, cta, G, T);
@@ -497,7 +497,7 @@ __global__ void __maxnreg__(128)
 #pragma unroll
             for (int x = 0; x < C::HD; x++) o[x] = 0.0f;
             for (int j = 0; j < nblk; j++, jg++) {
-                const int bb = (int)(jg & 1);
+                const int bb = jg & 1;
                 const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
                 // Rows past L (zero-filled by TMA) are computed but never stored. Column c is key
                 // k0 + c: valid below S and, under causal masking, up to qrow (one bit per column
@@ -607,7 +607,7 @@ __global__ void __maxnreg__(128)
             }
             // The tile's last block: its O_blk into the registers, its buffer freed for the next
             // tile's PV MMAs.
-            const int64_t jl = jg - 1;
+            const int jl = jg - 1;
             if (ok) {
                 ok = mbar_wait(bar(C::PV_DONE_B + (int)(jl & 1)), (uint32_t)((jl >> 1) & 1), abort, err);
                 tc_fence_after();
@@ -688,19 +688,18 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
     a.num_tiles = (int64_t)a.num_q_tiles * p.H * p.B;
-    // Groups of heads whose K and V (S * (E + Ev) floats each) fit in about 64 MB of the L2.
+    // Groups of heads whose K and V (S * (E + Ev) floats each) fit in about 48 MB, within one of
+    // the L2's two 63 MB partitions (at 67 MB, two of config 4's heads, the forward measured
+    // 28 ms against 22 ms with one head at a time).
     const int64_t kv_bytes = p.S * (p.E + p.Ev) * 4, hb = p.H * p.B;
-    a.group_heads = kv_bytes > 0 ? (64ll << 20) / kv_bytes : hb;
+    a.group_heads = kv_bytes > 0 ? (48ll << 20) / kv_bytes : hb;
     a.group_heads = a.group_heads < 1 ? 1 : (a.group_heads > hb ? hb : a.group_heads);
     // Short tiles (up to 64 key blocks) run persistently, one CTA per SM (tensor and shared
     // memory admit one) walking the schedule, so that a tile's start-up overlaps the previous
     // tile's tail; long tiles take one CTA each, which the hardware hands out in schedule order.
-    static int sms[64] = {0};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-    if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms[dev] = 148;
+    const int64_t sms = device_sm_count();
     const bool persistent = (p.S + C::BN - 1) / C::BN <= 64;
-    const int64_t ctas = persistent && a.num_tiles > sms[dev] ? sms[dev] : a.num_tiles;
+    const int64_t ctas = persistent && a.num_tiles > sms ? sms : a.num_tiles;
     if (ctas > 0x7fffffffll) return fail(DC_ERR_UNSUPPORTED, "too many query tiles for one launch");
     KernelTrace tr(C::D == 64 ? "fwd_tc_d64" : "fwd_tc_d128", stream);
     kernel<<<(unsigned)ctas, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);

@@ -46,6 +46,9 @@ int keep_bits(const uint32_t *st_in, uint32_t *st_out, int64_t n, double keep_pr
               cudaStream_t stream);
 int rng_skip(const uint32_t *st_in, uint64_t outputs, uint32_t *st_out);
 
+// SM count of the current device (cached per device; 148 if it cannot be read).
+int device_sm_count();
+
 // Side streams (streams.cu): the library's stream for `role` (0 = the backward's dQ kernel,
 // 1 = ring attention's transfers) beside caller stream `caller` on the current device, and an
 // event edge that makes `to` wait for the work enqueued on `from` so far.

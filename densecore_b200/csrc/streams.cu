@@ -1,4 +1,5 @@
-// streams.cu -- the library's own side streams and the event edges that fork and join them.
+// streams.cu -- the library's own side streams and the event edges that fork and join them,
+// and the device's SM count (the size of the persistent kernels' grids).
 //
 // Work that may run beside the caller's stream (the backward's dQ kernel, ring attention's
 // NCCL transfers) goes to a side stream that belongs to the caller's stream: one per (device,
@@ -38,6 +39,17 @@ int side_stream(cudaStream_t caller, int role, cudaStream_t *out) {
     }
     *out = it->second;
     return DC_OK;
+}
+
+int device_sm_count() {
+    static int counts[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!counts[dev]) {
+        int n = 0;
+        counts[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+    }
+    return counts[dev];
 }
 
 int stream_edge(cudaStream_t from, cudaStream_t to) {
