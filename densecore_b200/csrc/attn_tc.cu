@@ -72,7 +72,7 @@ struct FwdCfg {
     static constexpr uint32_t OFF_XMAX = OFF_V + VST * KV_STAGE;     // float [2][2][BM]
     static constexpr uint32_t OFF_XSUM = OFF_XMAX + 2 * 2 * BM * 4;  // float [2][BM]
     static constexpr uint32_t OFF_BAR = OFF_XSUM + 2 * BM * 4;
-    static constexpr int K_FULL = 0, K_READY = K_FULL + KST,
+    static constexpr int Q_FULL = 0, Q_READY = 1, K_FULL = 2, K_READY = K_FULL + KST,
                          K_EMPTY = K_READY + KST, V_FULL = K_EMPTY + KST, V_READY = V_FULL + VST,
                          V_EMPTY = V_READY + VST, S_FULL = V_EMPTY + VST, P_FULL = S_FULL + 2,
                          PV_DONE_B = P_FULL + 2, OB_FREE = PV_DONE_B + 2,
@@ -190,6 +190,380 @@ __device__ __forceinline__ void row_to_tmem(const uint8_t *raw, uint32_t chunk_b
     }
 }
 
+// One CTA per tile (long tiles: config 4). Grid (q-tiles, H, B), longest causal tiles first
+// within a head, so that the tiles the hardware runs together share their head's K / V in L2.
+// The same roles and pipelines as the persistent kernel below for a single tile: the raw Q tile
+// waits in the V ring while the K ring fills, and the first V load waits until Q has left.
+template <class C, bool SPLIT, bool MASKED, bool DROP>
+__global__ void __maxnreg__(128)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                       const __grid_constant__ CUtensorMap tmv, const TcFwdArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    const uint32_t sb = (raw + 1023u) & ~1023u;
+    uint8_t *sg = smem_raw + (sb - raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const AttnProblem &p = a.p;
+    const int qt = a.num_q_tiles - 1 - (int)blockIdx.x;  // longest (causal) tiles first
+    const int64_t h = blockIdx.y, b = blockIdx.z, hk = h / p.group;
+    const int64_t q0 = (int64_t)qt * C::BM;
+    const int64_t kv_end = p.causal ? min(p.S, q0 + C::BM) : p.S;
+    const int nblk = (int)((kv_end + C::BN - 1) / C::BN);
+    auto bar = [&](int i) { return sb + C::OFF_BAR + 8u * (uint32_t)i; };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sg + C::OFF_MISC);
+    volatile int *abort = reinterpret_cast<volatile int *>(sg + C::OFF_MISC + 4);
+    int *err = a.err;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(C::Q_FULL), 1);
+        mbar_init(bar(C::Q_READY), 128);
+        for (int s = 0; s < C::KST; s++) {
+            mbar_init(bar(C::K_FULL + s), 1);
+            mbar_init(bar(C::K_READY + s), 128);
+            mbar_init(bar(C::K_EMPTY + s), 1);
+        }
+        for (int s = 0; s < C::VST; s++) {
+            mbar_init(bar(C::V_FULL + s), 1);
+            mbar_init(bar(C::V_READY + s), 128);
+            mbar_init(bar(C::V_EMPTY + s), 1);
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(bar(C::S_FULL + s), 1);
+            mbar_init(bar(C::P_FULL + s), C::SOFTMAX_THREADS);
+        }
+        mbar_init(bar(C::PV_DONE_B), 1);
+        mbar_init(bar(C::PV_DONE_B + 1), 1);
+        mbar_init(bar(C::OB_FREE), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::OB_FREE + 1), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::XCH), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::XCH + 1), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::XSUM), C::SOFTMAX_THREADS);
+        mbar_init(bar(C::DRAIN), 1);
+        mbar_init(bar(C::DRAIN_PV), 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == C::W_MMA) {
+        tmem_alloc(smem_addr(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (warp == C::W_PROD && lane == 0) {
+        prefetch_tmap(&tmq);
+        prefetch_tmap(&tmk);
+        prefetch_tmap(&tmv);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == C::W_PROD) {
+        // ------------------------------------------------------------ TMA producer ----
+        if (lane == 0) {
+            int k_issued = -1, v_issued = -1;
+            // The raw Q tile lands in the V ring and the converters move it into TMEM; the K
+            // ring fills meanwhile (S_0 needs Q and K_0), and the first V load waits until Q has
+            // left the V ring.
+            mbar_expect_tx(bar(C::Q_FULL), C::Q_BYTES);
+            for (int c = 0; c < C::CHUNKS; c++)
+                tma_load_4d(&tmq, sb + C::OFF_V + c * C::Q_CHUNK, bar(C::Q_FULL), 32 * c, (int)q0, (int)h, (int)b);
+            bool ok = true;
+            for (int j = 0; ok && j < nblk; j++) {
+                const int ks = j % C::KST, vs = j % C::VST;
+                if (j >= C::KST && !mbar_wait(bar(C::K_EMPTY + ks), ((j / C::KST) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(C::K_FULL + ks), C::KV_BYTES);
+                const uint32_t kd = sb + C::OFF_K + ks * C::KV_STAGE;
+                for (int c = 0; c < C::CHUNKS; c++)
+                    tma_load_4d(&tmk, kd + c * C::KV_CHUNK, bar(C::K_FULL + ks), 32 * c, j * C::BN, (int)hk, (int)b);
+                k_issued = j;
+                if (j == 0 && !(ok = mbar_wait(bar(C::Q_READY), 0, abort, err))) break;
+                if (j >= C::VST && !mbar_wait(bar(C::V_EMPTY + vs), ((j / C::VST) - 1) & 1, abort, err)) break;
+                mbar_expect_tx(bar(C::V_FULL + vs), C::KV_BYTES);
+                const uint32_t vd = sb + C::OFF_V + vs * C::KV_STAGE;
+                for (int c = 0; c < C::CHUNKS; c++)
+                    tma_load_4d(&tmv, vd + c * C::KV_CHUNK, bar(C::V_FULL + vs), 32 * c, j * C::BN, (int)hk, (int)b);
+                v_issued = j;
+            }
+            if (*abort) {
+                // Let the copies already in flight land before the CTA's memory goes away.
+                volatile int never = 0;
+                mbar_wait(bar(C::Q_FULL), 0, &never, nullptr);
+                for (int j = max(0, k_issued - C::KST + 1); j <= k_issued; j++)
+                    mbar_wait(bar(C::K_FULL + j % C::KST), (j / C::KST) & 1, &never, nullptr);
+                for (int j = max(0, v_issued - C::VST + 1); j <= v_issued; j++)
+                    mbar_wait(bar(C::V_FULL + j % C::VST), (j / C::VST) & 1, &never, nullptr);
+            }
+        }
+    } else if (warp == C::W_MMA) {
+        // -------------------------------------------------------- MMA issuer: S = Q K^T ----
+        // The whole warp runs the loop converged; one elected lane issues each MMA.
+        {
+            // Descriptor of K stage 0; stage and k-step offsets go into the address field.
+            const uint64_t kdesc0 = sdesc_sw128(sb + C::OFF_K, 16, 1024);
+            const uint32_t q_hi = tmem + C::COL_QHI, q_lo = tmem + C::COL_QLO;
+            bool ok = mbar_wait_warp(bar(C::Q_READY), 0, abort, err);
+            tc_fence_after();
+            for (int j = 0; ok && j < nblk; j++) {
+                const int bb = j & 1, ks = j % C::KST;
+                // S buffer bb held P_{j-2}, read by PV_{j-2}.
+                if (j >= 2 && !mbar_wait_warp(bar(C::PV_DONE_B + bb), ((j - 2) >> 1) & 1, abort, err)) break;
+                if (!mbar_wait_warp(bar(C::K_READY + ks), (j / C::KST) & 1, abort, err)) break;
+                tc_fence_after();
+                const uint64_t kd = kdesc0 + ((ks * C::KV_STAGE) >> 4);
+                const uint32_t d_s = tmem + C::col_s(bb);
+                if (SPLIT) {  // Qhi Klo + Qlo Khi first, then Qhi Khi
+#pragma unroll
+                    for (int kk = 0; kk < C::D / 8; kk++) {
+                        const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
+                        mma_tf32_ts_w(d_s, q_hi + kk * 8, kd + ((C::KV_BYTES >> 4) + off), C::IDESC_S, kk > 0 ? 1u : 0u);
+                        mma_tf32_ts_w(d_s, q_lo + kk * 8, kd + off, C::IDESC_S, 1u);
+                    }
+                }
+#pragma unroll
+                for (int kk = 0; kk < C::D / 8; kk++) {
+                    const uint32_t off = ((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4;
+                    mma_tf32_ts_w(d_s, q_hi + kk * 8, kd + off, C::IDESC_S, (SPLIT || kk > 0) ? 1u : 0u);
+                }
+                tc_commit_w(bar(C::S_FULL + bb));
+                tc_commit_w(bar(C::K_EMPTY + ks));
+            }
+            // Every MMA this warp issued completes before TMEM is released.
+            tc_commit_w(bar(C::DRAIN));
+            volatile int never = 0;
+            mbar_wait_warp(bar(C::DRAIN), 0, &never, nullptr);
+        }
+    } else if (warp == C::W_PV) {
+        // ----------------------------------------------------- MMA issuer: O_blk = P V ----
+        {
+            const uint64_t vdesc0 = sdesc_mn_sw128_32b(sb + C::OFF_V, C::KV_CHUNK, 512);
+            for (int i = 0; i < nblk; i++) {
+                const int bi = i & 1, vs = i % C::VST;
+                if (!mbar_wait_warp(bar(C::P_FULL + bi), (i >> 1) & 1, abort, err)) break;
+                if (!mbar_wait_warp(bar(C::V_READY + vs), (i / C::VST) & 1, abort, err)) break;
+                // O_blk buffer i % NOB held block i - NOB until the softmax threads folded it.
+                if (i >= C::NOB && !mbar_wait_warp(bar(C::OB_FREE + i % C::NOB), ((i / C::NOB) - 1) & 1, abort, err))
+                    break;
+                const uint32_t d_ob = tmem + C::col_ob(i);
+                tc_fence_after();
+                const uint64_t vd = vdesc0 + ((vs * C::KV_STAGE) >> 4);
+                const uint32_t a_hi = tmem + C::col_s(bi), a_lo = tmem + C::col_plo(bi);
+                if (SPLIT) {  // the small cross terms first, then the main products
+#pragma unroll
+                    for (int kk = 0; kk < C::BN / 8; kk++) {
+                        mma_tf32_ts_w(d_ob, a_hi + kk * 8, vd + ((C::KV_BYTES + kk * 1024) >> 4), C::IDESC_O,
+                                      kk > 0 ? 1u : 0u);
+                        mma_tf32_ts_w(d_ob, a_lo + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, 1u);
+                    }
+                }
+#pragma unroll
+                for (int kk = 0; kk < C::BN / 8; kk++)
+                    mma_tf32_ts_w(d_ob, a_hi + kk * 8, vd + ((kk * 1024) >> 4), C::IDESC_O, (SPLIT || kk > 0) ? 1u : 0u);
+                tc_commit_w(bar(C::PV_DONE_B + bi));
+                tc_commit_w(bar(C::V_EMPTY + vs));
+            }
+            tc_commit_w(bar(C::DRAIN_PV));
+            volatile int never = 0;
+            mbar_wait_warp(bar(C::DRAIN_PV), 0, &never, nullptr);
+        }
+    } else if (warp >= C::W_CVT && warp < C::W_PV) {
+        // --------------------------------------------------------------- converters ----
+        const int ct = threadIdx.x - 32 * C::W_CVT;
+        const int quad = warp & 3;
+        if (mbar_wait(bar(C::Q_FULL), 0, abort, err)) {
+            row_to_tmem<C::CHUNKS, SPLIT>(sg + C::OFF_V, C::Q_CHUNK, quad * 32 + lane,
+                                          tmem + ((uint32_t)(quad * 32) << 16), C::COL_QHI, C::COL_QLO);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(C::Q_READY));
+            for (int j = 0; j < nblk; j++) {
+                const int ks = j % C::KST, vs = j % C::VST;
+                if (!mbar_wait(bar(C::K_FULL + ks), (j / C::KST) & 1, abort, err)) break;
+                split_tile<SPLIT>(sg + C::OFF_K + ks * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
+                fence_proxy_async_smem();
+                mbar_arrive(bar(C::K_READY + ks));
+                if (!mbar_wait(bar(C::V_FULL + vs), (j / C::VST) & 1, abort, err)) break;
+                split_tile<SPLIT>(sg + C::OFF_V + vs * C::KV_STAGE, C::KV_BYTES, C::KV_BYTES, ct);
+                fence_proxy_async_smem();
+                mbar_arrive(bar(C::V_READY + vs));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax ----
+        const int row = threadIdx.x & 127, half = threadIdx.x >> 7;
+        const int64_t qrow = q0 + row;
+        const bool row_ok = qrow < p.L;
+        const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        float *xmax = reinterpret_cast<float *>(sg + C::OFF_XMAX);  // [2][2][BM]
+        float *xsum = reinterpret_cast<float *>(sg + C::OFF_XSUM);  // [2][BM]
+        float m = -INFINITY, l = 0.0f;
+        float o[C::HD];
+#pragma unroll
+        for (int x = 0; x < C::HD; x++) o[x] = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nblk; j++) {
+            const int bb = j & 1;
+            const int64_t k0 = (int64_t)j * C::BN + half * C::HB;
+            // Rows past L (zero-filled by TMA) are computed but never stored. Column c is key
+            // k0 + c: valid below S and, under causal masking, up to qrow (one bit per column
+            // keeps the edge path as short as the fast one).
+            const bool edge = MASKED || (k0 + C::HB > p.S) || (p.causal && k0 + C::HB - 1 > q0);
+            uint32_t vbits = 0xFFFFFFFFu;
+            if (edge) {
+                const int64_t lim = (p.causal ? min(p.S, qrow + 1) : p.S) - k0;
+                const int n = !row_ok || lim <= 0 ? 0 : (lim >= C::HB ? C::HB : (int)lim);
+                vbits = n == 0 ? 0u : (0xFFFFFFFFu >> (32 - n));
+            }
+            // The user mask's values for these columns, loaded before the wait for S so that
+            // the wait hides their latency.
+            float mk[MASKED ? C::HB : 1];
+            if constexpr (MASKED) mask_run<C::HB>(p, b, h, qrow, k0, p.ms[3], vbits, mk);
+            // Dropout: this row's keep bits for these columns (the weights that meet V are
+            // P * keep_scale where kept, 0 where dropped; the row sum and lse stay undropped).
+            uint32_t kbits = 0;
+            if constexpr (DROP) kbits = row_ok ? keep_run32(p, b, h, qrow, k0) : 0u;
+            if (!mbar_wait(bar(C::S_FULL + bb), (j >> 1) & 1, abort, err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[C::HB];
+            {
+                uint32_t r[C::HB];
+                tmem_ld<C::HB>(tl + C::col_s(bb) + half * C::HB, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int x = 0; x < C::HB; x++) s[x] = __uint_as_float(r[x]);
+            }
+            // Interior blocks keep the raw scores and fold the scale into the exponent's FFMA
+            // (the max commutes with a positive scale); edge blocks scale, mask and fill first.
+            const bool raw = !edge && a.scale_log2 > 0.0f;
+            const float smul = raw ? a.scale_log2 : 1.0f;
+            if (!raw) {
+#pragma unroll
+                for (int c = 0; c < C::HB; c++) {
+                    float x = s[c] * a.scale_log2;
+                    if (MASKED) x += mk[MASKED ? c : 0] * LOG2E;
+                    s[c] = ((vbits >> c) & 1u) ? x : -INFINITY;
+                }
+            }
+            float bmax = max_tree<C::HB>(s) * smul;
+            // The block's row max, shared with the partner thread (the other half) through
+            // shared memory and an mbarrier (a bounded wait, unlike bar.sync).
+            xmax[(bb * 2 + half) * C::BM + row] = bmax;
+            mbar_arrive(bar(C::XCH + bb));
+            if (!mbar_wait(bar(C::XCH + bb), (j >> 1) & 1, abort, err)) {
+                ok = false;
+                break;
+            }
+            bmax = fmaxf(bmax, xmax[(bb * 2 + (half ^ 1)) * C::BM + row]);
+            const float m_new = fmaxf(m, bmax);
+            const bool rescale = m_new > m + 8.0f;
+            float corr = 1.0f;
+            if (rescale) {
+                corr = ex2_approx(m - m_new);
+                m = m_new;
+            }
+            const bool dead = (m == -INFINITY);
+            float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four partial row sums: shorter chains
+#pragma unroll
+            for (int r0 = 0; r0 < C::HB; r0 += 16) {  // P in 16-column pieces
+                uint32_t phi[16], plo[16];
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    const float pc = dead ? 0.0f : ex2_approx(fmaf(s[r0 + c], smul, -m));
+                    part[c & 3] += pc;
+                    float pw = pc;
+                    if constexpr (DROP) pw = ((kbits >> (r0 + c)) & 1u) ? pc * p.keep_scale : 0.0f;
+                    if (SPLIT) {
+                        phi[c] = __float_as_uint(pw);
+                        plo[c] = tf32_lo_trunc(pw);
+                    } else {
+                        phi[c] = tf32_rna(pw);
+                    }
+                }
+                tmem_st16(tl + C::col_s(bb) + half * C::HB + r0, phi);
+                if (SPLIT) tmem_st16(tl + C::col_plo(bb) + half * C::HB + r0, plo);
+            }
+            const float rs = (part[0] + part[1]) + (part[2] + part[3]);
+            l = fmaf(l, corr, rs);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(C::P_FULL + bb));
+            // Fold the previous block: o = (o + O_blk(j-1)) * corr (both relative to the
+            // previous max; corr moves them to m).
+            if (j >= 1) {
+                // Per-buffer barrier: with two O_blk buffers PV_j may finish before this wait,
+                // so a single barrier could be two phases ahead of it.
+                if (!mbar_wait(bar(C::PV_DONE_B + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const bool scaled = __any_sync(0xffffffffu, corr != 1.0f);
+#pragma unroll
+                for (int c = 0; c < C::HD / 16; c++) {
+                    uint32_t r[16];
+                    tmem_ld16(tl + C::col_ob(j - 1) + half * C::HD + 16 * c, r);
+                    tmem_wait_ld();
+                    if (scaled) {
+#pragma unroll
+                        for (int x = 0; x < 16; x++) o[16 * c + x] = (o[16 * c + x] + __uint_as_float(r[x])) * corr;
+                    } else {
+#pragma unroll
+                        for (int x = 0; x < 16; x++) o[16 * c + x] += __uint_as_float(r[x]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(bar(C::OB_FREE + (j - 1) % C::NOB));
+            }
+        }
+        if (ok && nblk > 0) {
+            ok = mbar_wait(bar(C::PV_DONE_B + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort, err);
+            tc_fence_after();
+        }
+        const bool read_o = __all_sync(0xffffffffu, ok) && nblk > 0;
+        const bool aborted = __any_sync(0xffffffffu, *abort != 0);
+        if (read_o) {
+#pragma unroll
+            for (int c = 0; c < C::HD / 32; c++) {
+                uint32_t r[32];
+                tmem_ld32(tl + C::col_ob(nblk - 1) + half * C::HD + 32 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int x = 0; x < 32; x++) o[32 * c + x] += __uint_as_float(r[x]);
+            }
+        }
+        // The row sum: this half's part plus the partner's.
+        xsum[half * C::BM + row] = l;
+        mbar_arrive(bar(C::XSUM));
+        const bool have_sum = mbar_wait(bar(C::XSUM), 0, abort, err);
+        l += xsum[(half ^ 1) * C::BM + row];
+        if (!aborted && have_sum && row_ok) {
+            const float lfin = l == 0.0f ? 1.0f : l;
+            const float mnat = m == -INFINITY ? 0.0f : m * LN2;
+            const float inv = 1.0f / lfin;
+            float *orow = p.out + b * p.os[0] + h * p.os[1] + qrow * p.os[2] + (int64_t)half * C::HD * p.os[3];
+            if (p.os[3] == 1 && (reinterpret_cast<uintptr_t>(orow) & 15u) == 0) {
+#pragma unroll
+                for (int x = 0; x < C::HD; x += 4)
+                    *reinterpret_cast<float4 *>(orow + x) =
+                        make_float4(o[x] * inv, o[x + 1] * inv, o[x + 2] * inv, o[x + 3] * inv);
+            } else {
+#pragma unroll
+                for (int x = 0; x < C::HD; x++) orow[x * p.os[3]] = o[x] * inv;
+            }
+            if (half == 0) p.lse[b * p.ls[0] + h * p.ls[1] + qrow * p.ls[2]] = mnat + logf(lfin);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == C::W_MMA) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
 // Tile t of the schedule: groups of group_heads (batch, head) pairs, and within a group the
 // tiles with the most causal work first (q-tile major, pair minor). Tiles handed out together
 // then share their heads' K / V in L2.
@@ -209,7 +583,8 @@ __device__ __forceinline__ int64_t fwd_tile_of(int64_t r, int c, int G, int64_t 
     return t < T ? t : -1;
 }
 
-// Persistent: gridDim.x CTAs (at most one per SM) walk the tiles in fwd_tile_of order. Every
+// Persistent (short tiles: configs 1-3): gridDim.x CTAs (at most one per SM) walk the tiles in
+// fwd_tile_of order. Every
 // role keeps running counters across tiles: K items (one per key block) in the K ring; V-ring
 // items, which are each tile's Q (QS slots) followed by its V blocks, so that the barriers of a
 // V-ring slot count Q and V uses alike; and blocks (the S / P buffers, the O blocks). The next
@@ -219,7 +594,7 @@ __device__ __forceinline__ int64_t fwd_tile_of(int64_t r, int c, int G, int64_t 
 // overlaps the next tile's first S MMAs.
 template <class C, bool SPLIT, bool MASKED, bool DROP>
 __global__ void __maxnreg__(128)
-    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+    attn_fwd_tc_persist_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                        const __grid_constant__ CUtensorMap tmv, const TcFwdArgs a) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
@@ -662,6 +1037,18 @@ __global__ void __maxnreg__(128)
     }
 }
 
+// The forward instantiation for (split, masked, dropout): persistent, or one CTA per tile.
+template <class C, bool PERSIST>
+decltype(&attn_fwd_tc_kernel<C, true, true, true>) pick_fwd(bool split, bool masked, bool drop) {
+#define DC_FWD(S, M, D) (PERSIST ? attn_fwd_tc_persist_kernel<C, S, M, D> : attn_fwd_tc_kernel<C, S, M, D>)
+    if (drop)
+        return split ? (masked ? DC_FWD(true, true, true) : DC_FWD(true, false, true))
+                     : (masked ? DC_FWD(false, true, true) : DC_FWD(false, false, true));
+    return split ? (masked ? DC_FWD(true, true, false) : DC_FWD(true, false, false))
+                 : (masked ? DC_FWD(false, true, false) : DC_FWD(false, false, false));
+#undef DC_FWD
+}
+
 template <class C>
 int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     CUtensorMap tq, tk, tv;
@@ -678,15 +1065,6 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     if (!a.err) return fail(DC_ERR_CUDA, "device error word is unavailable");
     const bool masked = p.mask_kind != MASK_NONE;
     const bool drop = p.keep != nullptr;
-    decltype(&attn_fwd_tc_kernel<C, true, true, true>) kernel;
-    if (drop)
-        kernel = split ? (masked ? attn_fwd_tc_kernel<C, true, true, true> : attn_fwd_tc_kernel<C, true, false, true>)
-                       : (masked ? attn_fwd_tc_kernel<C, false, true, true> : attn_fwd_tc_kernel<C, false, false, true>);
-    else
-        kernel = split ? (masked ? attn_fwd_tc_kernel<C, true, true, false> : attn_fwd_tc_kernel<C, true, false, false>)
-                       : (masked ? attn_fwd_tc_kernel<C, false, true, false> : attn_fwd_tc_kernel<C, false, false, false>);
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
     a.num_tiles = (int64_t)a.num_q_tiles * p.H * p.B;
     // Groups of heads whose K and V (S * (E + Ev) floats each) fit in about 48 MB, within one of
     // the L2's two 63 MB partitions (at 67 MB, two of config 4's heads, the forward measured
@@ -700,9 +1078,12 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     const int64_t sms = device_sm_count();
     const bool persistent = (p.S + C::BN - 1) / C::BN <= 64;
     const int64_t ctas = persistent && a.num_tiles > sms ? sms : a.num_tiles;
-    if (ctas > 0x7fffffffll) return fail(DC_ERR_UNSUPPORTED, "too many query tiles for one launch");
+    auto kernel = persistent ? pick_fwd<C, true>(split, masked, drop) : pick_fwd<C, false>(split, masked, drop);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_tc smem attribute");
+    const dim3 grid = persistent ? dim3((unsigned)ctas) : dim3((unsigned)a.num_q_tiles, (unsigned)p.H, (unsigned)p.B);
     KernelTrace tr(C::D == 64 ? "fwd_tc_d64" : "fwd_tc_d128", stream);
-    kernel<<<(unsigned)ctas, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);
+    kernel<<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, a);
     return check_launch("attn_fwd_tc");
 }
 
