@@ -56,9 +56,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // is set by another thread or after timeout_ns (WAIT_TIMEOUT_NS in every kernel; only the
 // wait probe of selftest.cu passes a shorter bound), in which case it sets *abort and
 // records DEV_WAIT_TIMEOUT in *err_flag.
+//
+// Only the first try_wait is inlined at each call site; the bounded spin after it is one
+// out-of-line function, which keeps the kernels' many wait sites from crowding the hot loops
+// out of the instruction cache.
+static __device__ __noinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int *abort, int *err_flag,
+                                                   uint64_t timeout_ns);
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
                                           int *err_flag, uint64_t timeout_ns = WAIT_TIMEOUT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_spin(bar, parity, abort, err_flag, timeout_ns);
+}
+static __device__ __noinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int *abort, int *err_flag,
+                                                   uint64_t timeout_ns) {
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
