@@ -126,3 +126,18 @@ def test_ring_entry_validates_before_any_device_work():
     strided.strides[2] = 128                                    # k not contiguous
     assert call(k_=strided) == _lib.DC_ERR_VALUE
     assert b"contiguous" in L.dc_last_error()
+
+
+def test_batch_or_heads_beyond_grid_limits_are_refused_before_any_launch():
+    """Every kernel family's grid carries the batch and head counts in its y / z dimensions
+    (at most 65535): a larger count is refused with DC_ERR_UNSUPPORTED by the shared
+    validation, for the q_len == 1 (decode) shapes as for the rest, before anything launches."""
+    L = _lib.load()
+    for B, H in ((70000, 1), (1, 70000)):
+        for Lq in (1, 8):
+            q, k = _fake((B, H, Lq, 64)), _fake((B, H, 16, 64))
+            out, lse = _fake((B, H, Lq, 64)), _fake((B, H, Lq))
+            st = L.dc_sdpa_fwd(ctypes.byref(q), ctypes.byref(k), ctypes.byref(k), None, 0, 0, 0.0, 0,
+                               ctypes.byref(out), ctypes.byref(lse), None)
+            assert st == _lib.DC_ERR_UNSUPPORTED, (B, H, Lq, st)
+            assert b"65535" in L.dc_last_error()
