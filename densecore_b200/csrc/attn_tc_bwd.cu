@@ -1213,33 +1213,6 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
         if ((st = stream_edge(stream, side))) return st;
     }
     StreamJoin join(stream, side);  // joins side back into stream on every return below
-    // dQ first: its CTAs take the SMs as they come free beside the dK / dV kernel's.
-    if (p.L > 0) {
-        HiLoMaps tq, tdo, tkk, tkmn, tvk;
-        st = q_maps(tq, TILE, KM);
-        if (!st) st = do_maps(tdo, TILE, KM);
-        if (!st) st = k_maps(tkk, QC::NB, KM);
-        if (!st) st = k_maps(tkmn, QC::NB, MN);
-        if (!st) st = v_maps(tvk, QC::NB, KM);
-        if (st) return st;
-        auto kernel = pick_kernel(split, masked, drop, attn_bwd_dq_tc_kernel<DD, true, true, true>,
-                                  attn_bwd_dq_tc_kernel<DD, true, true, false>,
-                                  attn_bwd_dq_tc_kernel<DD, true, false, true>,
-                                  attn_bwd_dq_tc_kernel<DD, true, false, false>,
-                                  attn_bwd_dq_tc_kernel<DD, false, true, true>,
-                                  attn_bwd_dq_tc_kernel<DD, false, true, false>,
-                                  attn_bwd_dq_tc_kernel<DD, false, false, true>,
-                                  attn_bwd_dq_tc_kernel<DD, false, false, false>);
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QC::SMEM);
-        if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
-        const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B * QC::NH);
-        {
-            KernelTrace tr("bwd_dq_tc", side);
-            kernel<<<grid, THREADS, QC::SMEM, side>>>(tq.hi, tdo.hi, tkk.hi, tkmn.hi, tvk.hi, tq.lo, tdo.lo, tkk.lo,
-                                                      tkmn.lo, tvk.lo, a);
-        }
-        if ((st = check_launch("attn_bwd_dq_tc"))) return st;
-    }
     if (p.S > 0) {
         HiLoMaps tk, tv, tqk, tqmn, tdok, tdomn;
         st = k_maps(tk, TILE, KM);
@@ -1265,7 +1238,34 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
                                                      tqk.lo, tqmn.lo, tdok.lo, tdomn.lo, a);
         if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
     }
-    if (p.L > 0 && (st = join.join())) return st;
+    if (p.L > 0) {
+        HiLoMaps tq, tdo, tkk, tkmn, tvk;
+        st = q_maps(tq, TILE, KM);
+        if (!st) st = do_maps(tdo, TILE, KM);
+        if (!st) st = k_maps(tkk, QC::NB, KM);
+        if (!st) st = k_maps(tkmn, QC::NB, MN);
+        if (!st) st = v_maps(tvk, QC::NB, KM);
+        if (st) return st;
+        auto kernel = pick_kernel(split, masked, drop, attn_bwd_dq_tc_kernel<DD, true, true, true>,
+                                  attn_bwd_dq_tc_kernel<DD, true, true, false>,
+                                  attn_bwd_dq_tc_kernel<DD, true, false, true>,
+                                  attn_bwd_dq_tc_kernel<DD, true, false, false>,
+                                  attn_bwd_dq_tc_kernel<DD, false, true, true>,
+                                  attn_bwd_dq_tc_kernel<DD, false, true, false>,
+                                  attn_bwd_dq_tc_kernel<DD, false, false, true>,
+                                  attn_bwd_dq_tc_kernel<DD, false, false, false>);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QC::SMEM);
+        if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dq_tc smem attribute");
+        const unsigned grid = (unsigned)((p.L + TILE - 1) / TILE * p.H * p.B * QC::NH);
+        {
+            KernelTrace tr("bwd_dq_tc", side);
+            kernel<<<grid, THREADS, QC::SMEM, side>>>(tq.hi, tdo.hi, tkk.hi, tkmn.hi, tvk.hi, tq.lo, tdo.lo, tkk.lo,
+                                                      tkmn.lo, tvk.lo, a);
+        }
+        const int launched = check_launch("attn_bwd_dq_tc");
+        if ((st = join.join())) return st;
+        if (launched) return launched;
+    }
     return DC_OK;
 }
 
