@@ -16,8 +16,10 @@
 //
 // K and V travel packed in one (2, B, Hkv, 2C, E) buffer of the caller's workspace: at step t
 // the rank sends the block it holds to rank r+1 and receives the next one from rank r-1 into
-// the second buffer, with ncclSend / ncclRecv in one group on a side stream of the library's,
-// while the step's attention runs on the caller's stream; the next step waits for the receive.
+// the second buffer, with ncclSend / ncclRecv in one group on a side stream of the library's.
+// The transfer that feeds step t + 1 runs beside step t's attention on the caller's stream;
+// the side stream has the device's greatest priority, so NCCL's blocks are scheduled ahead
+// of the attention blocks still waiting for an SM.
 // No kernel reads another GPU's memory: the only traffic between GPUs is NCCL's.
 //
 // libnccl is not a link-time dependency of the library: its entry points are resolved at the
@@ -155,9 +157,10 @@ int dc_ring_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor
     if (nr != ncclSuccess) return nccl_fail(api, nr, "communicator size / rank");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-    // Step 0: causal (or full) attention of the local rows over the local keys.
-    int st = dc_sdpa_fwd(q, k, v, nullptr, causal, has_scale, scale, precision, out, lse, stream);
-    if (st || world == 1 || B * H * L2 == 0) return st;
+    // One rank: the whole sequence is local.
+    if (world == 1 || B * H * L2 == 0)
+        return dc_sdpa_fwd(q, k, v, nullptr, causal, has_scale, scale, precision, out, lse, stream);
+    int st = DC_OK;
 
     const int64_t C = L2 / 2;
     const size_t kv_elems = 2 * (size_t)B * Hkv * L2 * E;
@@ -169,37 +172,45 @@ int dc_ring_sdpa_fwd(const dc_tensor_t *q, const dc_tensor_t *k, const dc_tensor
     if ((st = side_stream(s, kSideRoleRing, &side))) return st;
     StreamJoin join(s, side);  // the side stream joins the caller's on every return
 
-    for (int t = 1; t < world; t++) {
-        // Bring in the block of rank (rank - t): send what this rank holds, receive into the
-        // free buffer. Before the first transfer the held block is k and v themselves.
-        float *recv_buf = bufs[t % 2];
-        if ((st = stream_edge(s, side))) return st;  // the buffer's last reader is done
+    // Transfer j (1 <= j < P) brings the block of rank (rank - j) into bufs[j % 2]: this rank
+    // sends the block it holds (k and v themselves for j = 1) and receives the next. It is
+    // enqueued before the attention of step j - 1, so the two overlap; it starts once step
+    // j - 2's attention, the last reader of bufs[j % 2], is done, and step j waits for it.
+    auto transfer = [&](int j) -> int {
+        int rc = stream_edge(s, side);  // the buffer's last reader is done
+        if (rc) return rc;
+        float *recv_buf = bufs[j % 2];
         const size_t half = kv_elems / 2;
-        nr = api.group_start();
-        if (nr == ncclSuccess) {
-            if (t == 1) {
-                nr = api.send(k->data, half, ncclFloat32, next, comm, side);
-                if (nr == ncclSuccess) nr = api.send(v->data, half, ncclFloat32, next, comm, side);
+        ncclResult_t r = api.group_start();
+        if (r == ncclSuccess) {
+            if (j == 1) {
+                r = api.send(k->data, half, ncclFloat32, next, comm, side);
+                if (r == ncclSuccess) r = api.send(v->data, half, ncclFloat32, next, comm, side);
+                if (r == ncclSuccess) r = api.recv(recv_buf, half, ncclFloat32, prev, comm, side);
+                if (r == ncclSuccess) r = api.recv(recv_buf + half, half, ncclFloat32, prev, comm, side);
             } else {
-                nr = api.send(bufs[(t - 1) % 2], kv_elems, ncclFloat32, next, comm, side);
-            }
-            if (nr == ncclSuccess) {
-                if (t == 1) {
-                    nr = api.recv(recv_buf, half, ncclFloat32, prev, comm, side);
-                    if (nr == ncclSuccess) nr = api.recv(recv_buf + half, half, ncclFloat32, prev, comm, side);
-                } else {
-                    nr = api.recv(recv_buf, kv_elems, ncclFloat32, prev, comm, side);
-                }
+                r = api.send(bufs[(j - 1) % 2], kv_elems, ncclFloat32, next, comm, side);
+                if (r == ncclSuccess) r = api.recv(recv_buf, kv_elems, ncclFloat32, prev, comm, side);
             }
             const ncclResult_t ge = api.group_end();
-            if (nr == ncclSuccess) nr = ge;
+            if (r == ncclSuccess) r = ge;
         }
-        if (nr != ncclSuccess) return nccl_fail(api, nr, "send / recv of the K/V block");
-        if ((st = stream_edge(side, s))) return st;  // this step's attention reads the new block
+        return r == ncclSuccess ? DC_OK : nccl_fail(api, r, "send / recv of the K/V block");
+    };
+
+    // Step 0: causal (or full) attention of the local rows over the local keys, beside transfer 1.
+    if ((st = transfer(1))) return st;
+    if ((st = dc_sdpa_fwd(q, k, v, nullptr, causal, has_scale, scale, precision, out, lse, stream))) return st;
+
+    for (int t = 1; t < world; t++) {
+        // The side stream's tail is transfer t here: this step's attention reads its block.
+        if ((st = stream_edge(side, s))) return st;
+        if (t + 1 < world && (st = transfer(t + 1))) return st;
 
         const int src = (rank - t + world) % world;
-        dc_tensor_t kk = contiguous_view(recv_buf, B, Hkv, L2, E, 4);
-        dc_tensor_t vv = contiguous_view(recv_buf + kv_elems / 2, B, Hkv, L2, E, 4);
+        float *blk = bufs[t % 2];
+        dc_tensor_t kk = contiguous_view(blk, B, Hkv, L2, E, 4);
+        dc_tensor_t vv = contiguous_view(blk + kv_elems / 2, B, Hkv, L2, E, 4);
         if (!causal || src < rank) {
             // All local rows against the first C keys of the block (all of them without causal).
             const int64_t nk = causal ? C : L2;

@@ -32,8 +32,12 @@ int side_stream(cudaStream_t caller, int role, cudaStream_t *out) {
     auto key = std::make_tuple(dev, caller, role);
     auto it = g_side.find(key);
     if (it == g_side.end()) {
+        // Ring transfers (role 1) run at the device's greatest priority: their few blocks then
+        // take the next free SM ahead of the attention blocks queued beside them.
+        int least = 0, greatest = 0;
+        if (role == 1 && cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) greatest = 0;
         cudaStream_t s = nullptr;
-        e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        e = cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, role == 1 ? greatest : 0);
         if (e != cudaSuccess) return cuda_fail(e, "side stream: create");
         it = g_side.emplace(key, s).first;
     }
