@@ -324,7 +324,7 @@ struct KvCfg {
     // resident lo copies (DD = 128 loads them once the hi tiles are in TMEM).
     enum { KV_FULL, KV_READY, KVLO_FULL, QK_FULL, QK_EMPTY, DOK_FULL, DOK_EMPTY, DOMN_FULL, DOMN_EMPTY, QMN_FULL,
            QMN_EMPTY, S_FULL, DP_FULL, P_READY, DS_READY, DV_DONE, DK_DONE, DV_FREE, DK_FREE, DRAIN, DRAIN_G,
-           NBAR };
+           DK_ISSUED, NBAR };
     static constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr uint32_t SMEM = OFF_MISC + 16 + 1024;
     // TMEM: K hi | V hi | S^T / P^T hi | P^T lo | dP^T / dS^T hi | dS^T lo | dV_blk | dK_blk
@@ -394,6 +394,7 @@ __global__ void __maxnreg__(168)
         mbar_init(bar(C::DK_FREE), 128);
         mbar_init(bar(C::DRAIN), 1);
         mbar_init(bar(C::DRAIN_G), 1);
+        mbar_init(bar(C::DK_ISSUED), 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -491,6 +492,9 @@ __global__ void __maxnreg__(168)
             for (int i = 0; ok && i < nblk; i++) {
                 if (!warp_wait(bar(C::QK_FULL), i & 1, abort, err)) break;
                 if (i >= 1 && !warp_wait(bar(C::DV_DONE), (i - 1) & 1, abort, err)) break;
+                // dK_{i-1} goes to the tensor core ahead of S^T_i: the warps folding dK finish
+                // with it while S^T_i runs, instead of after, on the way to P^T_i.
+                if (i >= 1 && !warp_wait(bar(C::DK_ISSUED), (i - 1) & 1, abort, err)) break;
                 tc_fence_after();
                 mma_s<SPLIT, QB, DD>(tmem + C::C_S, tmem + C::C_KHI, klo, sdesc_sw128(sb + C::OFF_QK, 16, 1024));
                 tc_commit_w(bar(C::S_FULL));
@@ -527,6 +531,7 @@ __global__ void __maxnreg__(168)
                 mma_g<SPLIT, QB>(tmem + C::C_DK, tmem + C::C_DP, tmem + C::C_DSLO,
                                  sdesc_mn_sw128_32b(sb + C::OFF_QMN, C::TM_CHUNK, 512), false);
                 tc_commit_w(bar(C::DK_DONE));
+                if (lane == 0) mbar_arrive(bar(C::DK_ISSUED));
                 tc_commit_w(bar(C::QMN_EMPTY));
             }
             tc_commit_w(bar(C::DRAIN_G));

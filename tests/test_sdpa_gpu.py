@@ -313,6 +313,42 @@ def test_full_size_decode_sampled_rows():
     torch.cuda.empty_cache()
 
 
+@pytest.mark.parametrize("layout", ["bthd", "unaligned"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_forward_into_callers_strided_out(precision, D, layout):
+    # dc_sdpa_fwd writes into the caller's out view: a (B, T, H, D) buffer seen as (B, H, T, D),
+    # or rows of D floats inside rows of D + 1 at an odd offset (unaligned rows). 288 query
+    # tiles: the persistent kernel runs several per CTA; the last tile of each head is partial
+    # (300 rows), and nothing outside the view may be written.
+    from densecore_b200 import _lib
+    from densecore_b200.backends import precision_code
+    rng = np.random.default_rng(31)
+    B, H, L = 8, 12, 300
+    q, k, v = (rng.normal(size=(B, H, L, D)).astype(np.float32) for _ in range(3))
+    tq, tk, tv = (_cuda(a) for a in (q, k, v))
+    if layout == "bthd":
+        buf = torch.full((B, L, H, D), 7.0, device=DEV)
+        o = buf.transpose(1, 2)
+        outside = None
+    else:
+        buf = torch.full((B, H, L, D + 1), 7.0, device=DEV)
+        o = buf[..., 1:]
+        outside = buf[..., 0]
+    lse = torch.empty((B, H, L), device=DEV)
+    lib = _lib.load()
+    vq, vk, vv, vo, vl = (_lib.view(t) for t in (tq, tk, tv, o, lse))
+    st = lib.dc_sdpa_fwd(_lib.ref(vq), _lib.ref(vk), _lib.ref(vv), None, 1, 0, 0.0, precision_code(),
+                         _lib.ref(vo), _lib.ref(vl), _lib.stream_of(tq))
+    _lib.check(st, "forward")
+    torch.cuda.synchronize()
+    ro, rl = oracle.flash_forward(q, k, v, causal=True)
+    _assert_close("out", o.cpu().numpy(), ro, TOL[precision])
+    _assert_close("lse", lse.cpu().numpy(), rl, TOL[precision])
+    if outside is not None:
+        assert bool((outside == 7.0).all()), "a store left the caller's view"
+    assert lib.dc_device_status(0) == 0
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_backward_with_inputs_tma_cannot_read(precision, D):
     # Rows of D floats inside rows of D + 1: strides that are not 16-byte multiples and bases off
