@@ -264,6 +264,9 @@ __device__ __forceinline__ void split_store(float *hl, int64_t at, int64_t lo_of
 template <int DD>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
     constexpr int LPR = DD / 4, RPB = 256 / LPR;  // lanes per row, rows per block
+    // The dK / dV kernel after this one may become resident now (when it is launched as a
+    // dependent: short rows).
+    griddep_launch_dependents();
     const AttnProblem &p = a.p;
     const int64_t rows_a = p.B * p.H * p.L, rows_b = p.B * p.Hkv * p.S;
     const int64_t r = (int64_t)blockIdx.x * RPB + threadIdx.x / LPR;
@@ -406,6 +409,9 @@ __global__ void __maxnreg__(168)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Launched as a dependent of the pre-pass: set-up above overlapped its last blocks; its
+    // lo copies, lse and delta are read only after this.
+    griddep_wait();
 
     // One streamed tile (hi and, with SPLIT, lo) of query block i into a stage: all DD columns
     // (K-major) or this CTA's 64-column half (MN-major).
@@ -1239,9 +1245,19 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
         if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc smem attribute");
         const unsigned grid = (unsigned)((p.S + TILE - 1) / TILE * p.Hkv * p.B * KC::NH);
         KernelTrace tr("bwd_dkdv_tc", stream);
-        kernel<<<grid, THREADS, KC::SMEM, stream>>>(tk.hi, tv.hi, tqk.hi, tqmn.hi, tdok.hi, tdomn.hi, tk.lo, tv.lo,
-                                                     tqk.lo, tqmn.lo, tdok.lo, tdomn.lo, a);
-        if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
+        // Short rows (at most 512 queries): the CTAs are short and start-up bound, so the dK / dV
+        // CTAs become resident while the pre-pass drains (a programmatic dependent launch).
+        // Longer rows launch normally: there dK / dV taking every SM first delays the dQ kernel,
+        // the pair's longer part.
+        if (p.L <= 512) {
+            e = launch_dependent(kernel, dim3(grid), dim3(THREADS), KC::SMEM, stream, tk.hi, tv.hi, tqk.hi, tqmn.hi,
+                                 tdok.hi, tdomn.hi, tk.lo, tv.lo, tqk.lo, tqmn.lo, tdok.lo, tdomn.lo, a);
+            if (e != cudaSuccess) return cuda_fail(e, "attn_bwd_dkdv_tc");
+        } else {
+            kernel<<<grid, THREADS, KC::SMEM, stream>>>(tk.hi, tv.hi, tqk.hi, tqmn.hi, tdok.hi, tdomn.hi, tk.lo, tv.lo,
+                                                         tqk.lo, tqmn.lo, tdok.lo, tdomn.lo, a);
+            if ((st = check_launch("attn_bwd_dkdv_tc"))) return st;
+        }
     }
     if (p.L > 0) {
         HiLoMaps tq, tdo, tkk, tkmn, tvk;

@@ -161,4 +161,29 @@ int cuda_fail(cudaError_t err, const char *what);
 // Checks the launch just issued on `stream`; returns DC_OK or DC_ERR_CUDA.
 int check_launch(const char *what);
 
+// Programmatic dependent launch: the kernel may become resident while the kernel before it on
+// `stream` drains (and run its set-up: barriers, tensor memory, tensor-map prefetch); it must
+// execute griddep_wait() before it reads anything that kernel wrote. The primary lets its
+// dependents launch early with griddep_launch_dependents(); without that they launch as it
+// completes. (The runtime tracks the dependency; nothing spins on a flag.)
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
+// Device side of the above (no-ops for a kernel launched without the attribute).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace dc
