@@ -567,13 +567,17 @@ __global__ void __maxnreg__(128)
 // Tile t of the schedule: groups of group_heads (batch, head) pairs, and within a group the
 // tiles with the most causal work first (q-tile major, pair minor). Tiles handed out together
 // then share their heads' K / V in L2.
+// The persistent kernel runs only when the tile count is below 2^31 (checked at launch), so
+// the decode divides in 32 bits: the 64-bit divisions had sat on the softmax warps' path from
+// one tile to the next.
 __device__ __forceinline__ void fwd_tile(const TcFwdArgs &a, int64_t t, int64_t &q0, int64_t &h, int64_t &b) {
-    const int64_t nq = a.num_q_tiles, g = a.group_heads, hb = a.p.H * a.p.B;
-    const int64_t grp = t / (g * nq), base = grp * g, gs = min(g, hb - base), r = t - grp * g * nq;
-    const int64_t qt = nq - 1 - r / gs, bh = base + r % gs;
-    h = bh % a.p.H;
-    b = bh / a.p.H;
-    q0 = qt * 128;
+    const uint32_t nq = (uint32_t)a.num_q_tiles, g = (uint32_t)a.group_heads, hb = (uint32_t)(a.p.H * a.p.B),
+                   H = (uint32_t)a.p.H, tt = (uint32_t)t;
+    const uint32_t grp = tt / (g * nq), base = grp * g, gs = min(g, hb - base), r = tt - grp * g * nq;
+    const uint32_t qt = nq - 1 - r / gs, bh = base + r % gs;
+    h = bh % H;
+    b = bh / H;
+    q0 = (int64_t)qt * 128;
 }
 
 // Tile of round r of CTA c among G persistent CTAs: rounds alternate direction (a snake), which
@@ -1076,7 +1080,7 @@ int launch_fwd(const AttnProblem &p, int split, cudaStream_t stream) {
     // memory admit one) walking the schedule, so that a tile's start-up overlaps the previous
     // tile's tail; long tiles take one CTA each, which the hardware hands out in schedule order.
     const int64_t sms = device_sm_count();
-    const bool persistent = (p.S + C::BN - 1) / C::BN <= 64;
+    const bool persistent = (p.S + C::BN - 1) / C::BN <= 64 && a.num_tiles < (1ll << 31);
     const int64_t ctas = persistent && a.num_tiles > sms ? sms : a.num_tiles;
     auto kernel = persistent ? pick_fwd<C, true>(split, masked, drop) : pick_fwd<C, false>(split, masked, drop);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
