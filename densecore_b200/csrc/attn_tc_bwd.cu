@@ -200,11 +200,13 @@ __device__ __forceinline__ void store_row(float *dst, int64_t inner, const float
 }
 
 // Tile `tile` and (batch, head) pair `bh` of CTA `idx` in the grouped order: idx runs over
-// groups of GROUP_HEADS pairs, inside a group over tiles (outer) and pairs (inner).
-__device__ __forceinline__ void grouped_tile(int64_t idx, int64_t ntiles, int64_t bh_n, int64_t &tile, int64_t &bh) {
-    const int64_t per_group = ntiles * GROUP_HEADS;
-    const int64_t g = idx / per_group, base = g * GROUP_HEADS;
-    const int64_t gsize = min((int64_t)GROUP_HEADS, bh_n - base), r = idx - g * per_group;
+// groups of GROUP_HEADS pairs, inside a group over tiles (outer) and pairs (inner). The grids
+// are below 2^31 CTAs (tc_backward_supported), so the decode divides in 32 bits (every CTA
+// runs it before its first load).
+__device__ __forceinline__ void grouped_tile(uint32_t idx, uint32_t ntiles, uint32_t bh_n, int64_t &tile, int64_t &bh) {
+    const uint32_t per_group = ntiles * GROUP_HEADS;
+    const uint32_t g = idx / per_group, base = g * GROUP_HEADS;
+    const uint32_t gsize = min((uint32_t)GROUP_HEADS, bh_n - base), r = idx - g * per_group;
     tile = r / gsize;
     bh = base + r % gsize;
 }
@@ -364,10 +366,10 @@ __global__ void __maxnreg__(168)
     const AttnProblem &p = a.p;
     // Key tiles in ascending order: under causal masking tile 0 sees the most query rows.
     int64_t kt, bhd;
-    grouped_tile(blockIdx.x, (p.S + TILE - 1) / TILE, p.B * p.Hkv * C::NH, kt, bhd);
+    grouped_tile(blockIdx.x, (uint32_t)((p.S + TILE - 1) / TILE), (uint32_t)(p.B * p.Hkv * C::NH), kt, bhd);
     const int dh = (int)(bhd % C::NH);  // gradient column half
-    const int64_t bh = bhd / C::NH;
-    const int64_t hk = bh % p.Hkv, b = bh / p.Hkv, k0 = kt * TILE;
+    const uint32_t bh = (uint32_t)(bhd / C::NH);
+    const int64_t hk = bh % (uint32_t)p.Hkv, b = bh / (uint32_t)p.Hkv, k0 = kt * TILE;
     // Query blocks this CTA visits: for each query head of the group, rows [r_begin, L).
     const int64_t r_begin = p.causal ? min(k0, p.L) : 0;
     const int qb_first = (int)(r_begin / QB);
@@ -779,11 +781,11 @@ __global__ void __maxnreg__(168)
     // Query tiles in descending order: under causal masking the last tile sees the most keys.
     const int64_t ntiles = (p.L + TILE - 1) / TILE;
     int64_t qt, bhd;
-    grouped_tile(blockIdx.x, ntiles, p.B * p.H * C::NH, qt, bhd);
+    grouped_tile(blockIdx.x, (uint32_t)ntiles, (uint32_t)(p.B * p.H * C::NH), qt, bhd);
     qt = ntiles - 1 - qt;
     const int dh = (int)(bhd % C::NH);  // dQ column half
-    const int64_t bh = bhd / C::NH;
-    const int64_t h = bh % p.H, b = bh / p.H, hk = h / p.group;
+    const uint32_t bh = (uint32_t)(bhd / C::NH);
+    const int64_t h = bh % (uint32_t)p.H, b = bh / (uint32_t)p.H, hk = (uint32_t)h / (uint32_t)p.group;
     const int64_t q0 = qt * TILE;
     const int64_t kv_end = p.causal ? min(p.S, q0 + TILE) : p.S;
     const int nblk = (int)((kv_end + NB - 1) / NB);
