@@ -231,7 +231,28 @@ struct PrepArgs {
     // The kernels read the hi operand from the inputs themselves (the tensor core reads their
     // top 19 bits: x truncated to TF32); write only lo = x - trunc(x), exact in fp32.
     int lo_only;
+    // Every row index (rows of q plus rows of k) is below 2^31: the (batch, head, row) decode
+    // divides in 32 bits (its 64-bit divisions were a large share of this memory-bound
+    // kernel's instructions).
+    int rows32;
 };
+
+// Row r of a (B, heads, rows) stack as (batch, head, row).
+__device__ __forceinline__ void row_bhl(int64_t r, int64_t rows, int64_t heads, int rows32, int64_t &b, int64_t &h,
+                                        int64_t &l) {
+    if (rows32) {
+        const uint32_t r32 = (uint32_t)r, n = (uint32_t)rows, hh = (uint32_t)heads;
+        const uint32_t bh = r32 / n, b32 = bh / hh;
+        l = r32 - bh * n;
+        b = b32;
+        h = bh - b32 * hh;
+    } else {
+        const int64_t bh = r / rows;
+        l = r - bh * rows;
+        b = bh / heads;
+        h = bh - b * heads;
+    }
+}
 
 __device__ __forceinline__ float4 load4(const float *row, int64_t inner, int j, int vec) {
     if (vec) return *reinterpret_cast<const float4 *>(row + 4 * j);
@@ -275,7 +296,8 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
     const int j = threadIdx.x % LPR;
     const unsigned group_mask = LPR == 32 ? FULL : (0xFFFFu << (threadIdx.x & 16));
     if (r < rows_a) {
-        const int64_t l = r % p.L, bh = r / p.L, h = bh % p.H, b = bh / p.H;
+        int64_t b, h, l;
+        row_bhl(r, p.L, p.H, a.rows32, b, h, l);
         const float4 q4 = load4(p.q + b * p.qs[0] + h * p.qs[1] + l * p.qs[2], p.qs[3], j, a.vec);
         const float4 d4 = load4(a.g.dout + b * a.g.dos[0] + h * a.g.dos[1] + l * a.g.dos[2], a.g.dos[3], j, a.vec);
         const float4 o4 = load4(p.out + b * p.os[0] + h * p.os[1] + l * p.os[2], p.os[3], j, a.vec);
@@ -290,7 +312,8 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(PrepArgs a) {
         }
     } else if (r < rows_a + rows_b) {
         const int64_t rr = r - rows_a;
-        const int64_t sidx = rr % p.S, bh = rr / p.S, hk = bh % p.Hkv, b = bh / p.Hkv;
+        int64_t b, hk, sidx;
+        row_bhl(rr, p.S, p.Hkv, a.rows32, b, hk, sidx);
         const float4 k4 = load4(p.k + b * p.ks[0] + hk * p.ks[1] + sidx * p.ks[2], p.ks[3], j, a.vec);
         const float4 v4 = load4(p.v + b * p.vs[0] + hk * p.vs[1] + sidx * p.vs[2], p.vs[3], j, a.vec);
         split_store(a.khl, rr * DD + 4 * j, rows_b * DD, k4, a.split, a.lo_only);
@@ -1185,6 +1208,7 @@ int tc_backward_dd(const AttnProblem &p, const AttnGrads &g, int precision, cuda
     pa.lse2 = pa.vhl + NC * rows_b * DD;
     pa.split = split ? 1 : 0;
     pa.lo_only = raw ? 1 : 0;
+    pa.rows32 = rows_a + rows_b < (1ll << 31) ? 1 : 0;
     pa.vec = rows_vec(p.q, p.qs) && rows_vec(p.k, p.ks) && rows_vec(p.v, p.vs) && rows_vec(g.dout, g.dos) &&
              rows_vec(p.out, p.os);
     if (rows_a + rows_b > 0) {
