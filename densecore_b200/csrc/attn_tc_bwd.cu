@@ -5,7 +5,9 @@
 //   dV += P^T dO, dP = dO V^T, dS = P (dP - delta), dQ += scale dS K, dK += scale dS^T Q
 // (:381-446), with delta = sum(dO * O) per row (:327-330).
 //
-// Three launches (the last two run concurrently, on the caller's stream and a second one):
+// Three launches (the last two run concurrently, on the caller's stream and a second one; for
+// rows of at most 512 queries the dK / dV kernel is a programmatic dependent of the pre-pass,
+// resident and set up before the pre-pass ends):
 //
 //   prep: one pass over q, grad_out, out, k and v (HBM-bound). Writes TF32 hi = tf32(x) and
 //         lo = tf32(x - hi) copies of q, grad_out, k and v into contiguous scratch (3xTF32:
